@@ -1,0 +1,429 @@
+"""Benchmark: fused tANS-decode + FP8 add vs raw FP8 add on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--n-fp8 8192] [--elems-log2 29] [--sweep] [--no-e2e] [--no-cpu]
+
+Workload (one "step"): one fused decode-and-add pass over a 1 GiB working set
+per GPU — two e4m3 inputs of 2^29 elements each drawn from N(0,1) scaled by
+448/max|x| (seed = rank), exponent nibbles tANS-coded in 4096-pair-symbol
+streams (n_fp8_per_stream = 8192) with one table from the combined exponent
+histogram, e4m3 output.  Inputs (≈1.4 GB) exceed the 126 MB L2, so no flush
+is needed between steps.  Multi-GPU: one process per GPU, each with its own
+shard (weak scaling), no collective on the data path.
+
+Printed JSON (rank 0, one line): `value` = whole-job uncompressed-equivalent
+GB/s (3 bytes per output element: two inputs read, one output written) of the
+device-resident fused kernel; `x_raw` = raw-kernel time / fused time on the
+same data; `roofline` of the fused kernel on algorithmic bytes (compressed
+streams + sign/mantissa + metadata + output); `e2e` = the same metric through
+the public API with pinned host buffers and the H2D/D2H copies inside the
+timed region; `cpu_baseline` = the CPU decode+add (oracle port of the
+reference decoder, all host threads) on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "tans-vectoradd_b200"))
+
+METRIC = "fused/raw FP8 vecadd x speedup; effective GB/s and % HBM peak"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n-fp8", type=int, default=8192, help="fp8 bytes per stream")
+    ap.add_argument("--elems-log2", type=int, default=29, help="log2 elements per input")
+    ap.add_argument("--sweep", action="store_true", help="extra lines over stream lengths")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--out", default=None, help="also append the JSON line(s) to this file")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------- setup
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(n_fp8: int):
+    """Per-launch DRAM bytes of the fused kernel from the committed ncu summary
+    (profiles/fused_kernel_traffic.json), scaled to this launch, or None."""
+    path = os.path.join(ROOT, "profiles", "fused_kernel_traffic.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return d.get(str(n_fp8))
+    except Exception:
+        return None
+
+
+def make_workload(n: int, N: int, seed: int):
+    """Encode two N(0,1) e4m3 inputs of n elements (host), one shared table."""
+    from rans_vectoradd import tans_codec
+    from rans_vectoradd.data import exponent_histogram, normal_fp8_bytes
+
+    gen = torch.Generator().manual_seed(seed)
+    x = normal_fp8_bytes(n, generator=gen)
+    y = normal_fp8_bytes(n, generator=gen)
+    hist = exponent_histogram(x, y).double()
+    K = n // N
+    ex = tans_codec.encode(x.view(K, N), hist, tile=8)
+    ey = tans_codec.encode(y.view(K, N), hist, tile=8)
+    tbl = tans_codec.build_decode_table(ex[6].numpy(), ex[5].numpy())
+    # kernel argument order: comp, offsets, states, partial, sm
+    a = [ex[0], ex[2], ex[1], ex[3], ex[4]]
+    b = [ey[0], ey[2], ey[1], ey[3], ey[4]]
+    return x, y, a, b, tbl, K
+
+
+def alg_bytes(a, b, n):
+    stream = sum(t.numel() * t.element_size() for t in a + b)
+    return stream + n, stream  # + output
+
+
+class Clocks:
+    """nvidia-smi sampler over the timed region (index = this GPU)."""
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.2)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or not self.path:
+            return None
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3])
+                          if v.lower() == "active"})
+        loaded = [r for r in rows if r[2] > 200.0] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in loaded),
+                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
+
+
+def timed(fn, steps, warmup, stream, barrier):
+    """W untimed + K timed calls between barrier/synchronize; device time (ms)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        fn()
+    t1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    return t0.elapsed_time(t1)
+
+
+def max_over_ranks(ms, ws, dev):
+    if ws == 1:
+        return ms
+    import torch.distributed as dist
+    t = torch.tensor([ms], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(v, ws, dev):
+    if ws == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# -------------------------------------------------------------- CPU legs
+
+def cpu_decode_add(a, b, tbl, N, n_total, budget_s=10.0):
+    """Oracle decode + add (port of the reference decoder and satfinite add,
+    OpenMP over streams) on a bounded sample of the workload's streams.
+    Returns (GB/s uncompressed-equivalent, threads, sample description)."""
+    sys.path.insert(0, ROOT)
+    import oracle
+
+    K = a[2].numel()
+    k_s = min(K, 1024)  # 1024 streams x N bytes
+    # slice whole encoder blocks: offsets rebased, comp sliced by byte range
+    nb = (k_s + 127) // 128
+
+    def shard(t):
+        comp, off, st, part, sm = t
+        end = int(off[nb])
+        sm_s = sm.view(N // 16, K, 8)[:, :k_s].contiguous()
+        return (comp[:end], off[:nb + 1], st[:k_s], part[:k_s], sm_s)
+
+    sa, sb = shard(a), shard(b)
+    elems = k_s * N
+    reps, t_used = 0, 0.0
+    t_start = time.perf_counter()
+    while t_used < budget_s and reps < 1000:
+        out, ok = oracle.vecadd_fused(sa, sb, tbl, N)
+        assert ok
+        reps += 1
+        t_used = time.perf_counter() - t_start
+    gbs = 3.0 * elems * reps / t_used / 1e9
+    return gbs, oracle.num_threads(), (f"{reps} pass(es) over {k_s} streams x {N} fp8 "
+                                       f"({elems} elements per input) of the workload, "
+                                       f"{t_used:.1f} s")
+
+
+def run_reference_arm(args, ws, rank):
+    """--impl reference: the reference's CPU implementation of the path on the
+    host cores.  The reference has no CPU decoder, so decode+add is the oracle
+    port of its decoder/adder; encode is timed with the reference's own
+    compiled encoder when oracle/_ref is present."""
+    if rank != 0:
+        return
+    n = 1 << args.elems_log2
+    N = args.n_fp8
+    x, y, a, b, tbl, K = make_workload(n, N, 0)
+    samples = []
+    for i in range(args.warmup + args.steps):
+        gbs, threads, desc = cpu_decode_add(a, b, tbl, N, n, budget_s=2.0)
+        if i >= args.warmup:
+            samples.append(gbs)
+    v = statistics.median(samples)
+    line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic", "config": workload_config(args, K),
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads,
+                             "kind": "port", "sample": desc},
+            "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    emit(line, args)
+
+
+def workload_config(args, K):
+    return {"workload": (f"fused tANS-decode + e4m3 add, 2 x 2^{args.elems_log2} e4m3 inputs per "
+                         f"GPU, N(0,1)*448/absmax, {args.n_fp8 // 2} pair-symbols per stream"),
+            "elements_per_input_per_gpu": 1 << args.elems_log2,
+            "n_fp8_per_stream": args.n_fp8, "pair_symbols_per_stream": args.n_fp8 // 2,
+            "streams_per_input": K, "table_log": 12, "l2": "inputs > L2 (no flush)",
+            "parallelism": f"dp{args.gpus} (independent stream shards)"}
+
+
+def emit(line, args):
+    s = json.dumps(line)
+    print(s, flush=True)
+    if args.out:
+        with open(args.out, "a") as f:
+            f.write(s + "\n")
+
+
+# ------------------------------------------------------------------- main
+
+def main():
+    args = parse()
+    ws, rank, local = dist_env()
+    if args.impl == "reference":
+        run_reference_arm(args, ws, rank)
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+        barrier = lambda: dist.barrier(device_ids=[local])  # noqa: E731
+    else:
+        barrier = lambda: None  # noqa: E731
+
+    import rans_vectoradd as rv
+    from rans_vectoradd import _C
+
+    n = 1 << args.elems_log2
+    N = args.n_fp8
+    t_setup = time.perf_counter()
+    x, y, a, b, tbl, K = make_workload(n, N, rank)
+    setup_s = time.perf_counter() - t_setup
+    total_alg, stream_bytes = alg_bytes(a, b, n)
+    bits_per_fp8 = stream_bytes * 8 / (2 * n)
+
+    da = [t.to(dev) for t in a]
+    db = [t.to(dev) for t in b]
+    dtbl = tbl.to(dev)
+    xd, yd = x.to(dev), y.to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    # correctness gate on the bench data itself: fused == raw
+    out = rv.fp8_vecadd_fused_tans(*da, *db, dtbl, N)
+    raw = rv.fp8_vecadd_raw(xd, yd)
+    same = torch.equal(out.view(N // 16, K, 16).permute(1, 0, 2).reshape(-1), raw)
+    assert _C.data_status(dev) == 0
+    del out, raw
+
+    fused = lambda: rv.fp8_vecadd_fused_tans(*da, *db, dtbl, N)  # noqa: E731
+    with Clocks(local) as clk:
+        ms_fused = timed(fused, args.steps, args.warmup, stream, barrier)
+    clocks = clk.summary()
+    ms_raw = timed(lambda: rv.fp8_vecadd_raw(xd, yd), args.steps, args.warmup, stream, barrier)
+    ms_cpy = timed(lambda: rv.fp8_memcpy(xd), args.steps, args.warmup, stream, barrier)
+
+    ms_fused_max = max_over_ranks(ms_fused, ws, dev)
+    ms_raw_max = max_over_ranks(ms_raw, ws, dev)
+    per_step = ms_fused_max / args.steps
+    value = 3.0 * n * ws / (per_step / 1e3) / 1e9
+    raw_step = ms_raw_max / args.steps
+    t_launch = ms_fused / args.steps / 1e3
+    achieved = total_alg / t_launch / 1e9
+    peak, peak_kind = measured_peak()
+
+    # ---- end to end through the public API: pinned host -> device -> host
+    e2e = None
+    if not args.no_e2e:
+        ha = [t.pin_memory() for t in a]
+        hb = [t.pin_memory() for t in b]
+        htbl = tbl.pin_memory()
+        hout = torch.empty(n, dtype=torch.uint8).pin_memory()
+        h2d = sum(t.numel() * t.element_size() for t in ha + hb) + htbl.numel() * 4
+        ea = [torch.empty_like(t, device=dev) for t in a]
+        eb = [torch.empty_like(t, device=dev) for t in b]
+        etbl = torch.empty_like(tbl, device=dev)
+
+        def e2e_step():
+            for d_, h_ in zip(ea + eb + [etbl], ha + hb + [htbl]):
+                d_.copy_(h_, non_blocking=True)
+            o = rv.fp8_vecadd_fused_tans(*ea, *eb, etbl, N)
+            hout.copy_(o, non_blocking=True)
+
+        e_steps = max(3, min(args.steps, 10))
+        ms_e2e = max_over_ranks(timed(e2e_step, e_steps, 3, stream, barrier), ws, dev)
+        e2e = {"value": round(3.0 * n * ws / (ms_e2e / e_steps / 1e3) / 1e9, 3), "unit": "GB/s",
+               "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(n),
+               "ms_per_step": round(ms_e2e / e_steps, 4)}
+
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu:
+        gbs, threads, desc = cpu_decode_add(a, b, tbl, N, n)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": desc}
+
+    same_all = sum_over_ranks(1.0 if same else 0.0, ws, dev) == ws
+    if rank == 0:
+        traffic = profile_traffic(N)
+        line = {
+            "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic (N(0,1)*448/absmax e4m3, seed = rank)",
+            "config": workload_config(args, K),
+            "x_raw": round(raw_step / per_step, 4),
+            "raw_ms_per_step": round(raw_step, 4),
+            "raw_gbs": round(3.0 * n * ws / (raw_step / 1e3) / 1e9, 3),
+            "memcpy_gbs_rank0": round(2.0 * n / (ms_cpy / args.steps / 1e3) / 1e9, 3),
+            "bits_per_fp8": round(bits_per_fp8, 4),
+            "algorithmic_bytes_per_step": int(total_alg),
+            "hbm_frac_compressed": round(achieved / peak, 4),
+            "bit_exact_vs_raw": bool(same_all),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
+                         "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic, "peak_source": peak_kind,
+                         "kernel": "fused_kernel"},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "e2e": e2e,
+            "cpu_baseline": cpu,
+            "setup_s": round(setup_s, 2),
+        }
+        emit(line, args)
+
+    if args.sweep and ws == 1:
+        for n_fp8 in (2048, 8192, 32768, 131072, 1024, 4096, 16384, 65536):
+            if n_fp8 == N:
+                continue
+            del da, db
+            torch.cuda.empty_cache()
+            _, _, a2, b2, tbl2, K2 = make_workload(n, n_fp8, rank)
+            da = [t.to(dev) for t in a2]
+            db = [t.to(dev) for t in b2]
+            dt2 = tbl2.to(dev)
+            ms = timed(lambda: rv.fp8_vecadd_fused_tans(*da, *db, dt2, n_fp8), args.steps,
+                       args.warmup, stream, barrier)
+            tot2, sb2 = alg_bytes(a2, b2, n)
+            ps = ms / args.steps
+            emit({"sweep": True, "n_fp8_per_stream": n_fp8, "pair_symbols": n_fp8 // 2,
+                  "streams": K2, "ms": round(ps, 4),
+                  "gbs_uncompressed_equiv": round(3.0 * n / (ps / 1e3) / 1e9, 2),
+                  "x_raw": round(raw_step / ps, 4), "bits_per_fp8": round(sb2 * 8 / (2 * n), 4),
+                  "hbm_frac_compressed": round(tot2 / (ps / 1e3) / 1e9 / peak, 4)}, args)
+
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,156 @@
+/*
+ * tans_b200.h — C ABI of the B200 (sm_100a) tANS FP8 decode library.
+ *
+ * Every entry point takes plain pointers and sizes, returns an int status
+ * (TANS_B200_OK == 0) and never allocates device memory: callers own every
+ * buffer.  Device entry points enqueue work on the given CUDA stream
+ * (cudaStream_t passed as void*; NULL = legacy default stream) on the device
+ * that is current on the calling thread, and return without synchronising.
+ * On failure, tans_b200_last_error() returns a message for the calling thread.
+ *
+ * Data formats are those of the reference (doublewordai/tans-vectoradd):
+ *   - pair symbols: sym = exp(elem 2i) << 4 | exp(elem 2i+1), alphabet 256,
+ *     rans_vectoradd/tans_codec.py:109-124
+ *   - sign/mantissa pairs: sm = sm(elem 2i) | sm(elem 2i+1) << 4,
+ *     rans_vectoradd/tans_codec.py:110-113
+ *   - slab layout: 128-stream encoder blocks, G_b uint32 slabs per stream,
+ *     slab g of stream t at byte offsets[b] + g*512 + 4*t, streams top-aligned,
+ *     csrc/tans_codec.cpp:139-181
+ *   - decode table: int32[4096], sym | nb << 8 | base << 16,
+ *     rans_vectoradd/tans_codec.py:63-87, csrc/tans_decode.cu:23-59
+ */
+#ifndef TANS_B200_H
+#define TANS_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define TANS_B200_OK 0
+#define TANS_B200_ERR_INVALID 1 /* bad argument (size, alignment, null)   */
+#define TANS_B200_ERR_CUDA 2    /* a CUDA runtime call failed            */
+#define TANS_B200_ERR_HOST 3    /* host-side failure (allocation, ...)   */
+
+/* Device-side data-error bits, OR-ed into the optional `status` word that
+ * the decode entry points take (a device int32, may be NULL).  Malformed
+ * metadata never makes a kernel read out of bounds; it is reported here. */
+#define TANS_B200_DATA_BAD_OFFSETS 1 /* block offsets not monotone/in range */
+#define TANS_B200_DATA_BAD_STATE 2   /* initial state outside [4096, 8192)  */
+#define TANS_B200_DATA_BAD_TABLE 4   /* spread/freqs/table entry malformed  */
+
+#define TANS_B200_TABLE_SIZE 4096   /* L = M, tans_codec.py:24-25 */
+#define TANS_B200_BLOCK_STREAMS 128 /* tans_codec.py:27          */
+
+/* Message for the last failed call on this thread ("" if none). */
+const char *tans_b200_last_error(void);
+/* Library version string. */
+const char *tans_b200_version(void);
+
+/* ---------------------------------------------------------------- host */
+
+/* Build the reference decode table (tans_codec.py:63-87; its C++ twin is
+ * csrc/tans_decode.cu:23-59).  spread[4096] slot->symbol, freqs[n_syms]
+ * summing to 4096.  Writes table[4096]. */
+int tans_b200_build_decode_table_host(const int32_t *spread,
+                                      const int32_t *freqs, int64_t n_syms,
+                                      int32_t *table);
+
+/* CPU slab encoder: replaces `tans_encode_interleaved`
+ * (csrc/tans_codec.cpp:69-196).  Two-phase so that the caller allocates the
+ * outputs:
+ *   1. tans_b200_encode(...) encodes symbols[K][N] (host, row-major) with
+ *      OpenMP over streams and returns an opaque handle;
+ *   2. tans_b200_encoded_sizes() reports the compressed byte count and the
+ *      number of encoder blocks B = ceil(K/128);
+ *   3. tans_b200_encoded_export() copies compressed[bytes] (uint8),
+ *      states[K] (uint16), offsets[B+1] (int32), partial[K] (uint8) into
+ *      caller buffers; output bytes are identical to the reference's;
+ *   4. tans_b200_encoded_free() releases the handle.
+ * `symbols` is borrowed: it must stay valid and unchanged until export.
+ * n_threads <= 0 uses the OpenMP default.  A symbol with zero frequency, a
+ * spread inconsistent with freqs, or freqs not summing to 4096 is an error
+ * (TANS_B200_ERR_INVALID). */
+typedef struct tans_b200_encoded tans_b200_encoded;
+int tans_b200_encode(const uint8_t *symbols, int64_t K, int64_t N,
+                     const int32_t *freqs, int64_t n_syms,
+                     const int32_t *spread, int n_threads,
+                     tans_b200_encoded **out);
+int tans_b200_encoded_sizes(const tans_b200_encoded *enc,
+                            int64_t *compressed_bytes, int64_t *n_blocks);
+int tans_b200_encoded_export(const tans_b200_encoded *enc, uint8_t *compressed,
+                             uint16_t *states, int32_t *offsets,
+                             uint8_t *partial);
+void tans_b200_encoded_free(tans_b200_encoded *enc);
+
+/* Split e4m3 bytes fp8[K][N] (N even) into the encoder's inputs, as
+ * rans_vectoradd/tans_codec.py:105-124 does with torch ops:
+ *   pair_syms[K][N/2] = exp(2i) << 4 | exp(2i+1),  exp = (b >> 3) & 15
+ *   sm = sm(2i) | sm(2i+1) << 4,  sm = ((b >> 4) & 8) | (b & 7), laid out
+ *   [N/2/tile][K][tile] when tile > 0, else [N/2][K]
+ * exp_hist[16] (optional) is incremented by the exponent histogram.
+ * Either output may be NULL. */
+int tans_b200_split_fp8(const uint8_t *fp8, int64_t K, int64_t N,
+                        int64_t tile, uint8_t *pair_syms, uint8_t *sm,
+                        int64_t *exp_hist, int n_threads);
+
+/* -------------------------------------------------------------- device */
+
+/* Number of SMs of the current device (cached per device). */
+int tans_b200_sm_count(int *sm_count);
+
+/* C = A: replaces `fp8_memcpy` (csrc/fp8_memcpy.cu:45-64).
+ * n bytes, n % 16 == 0, 16-byte aligned pointers. */
+int tans_b200_fp8_memcpy(const uint8_t *a, uint8_t *c, int64_t n,
+                         void *stream);
+
+/* C[i] = e4m3_satfinite(A[i] + B[i]): replaces `fp8_vecadd_raw`
+ * (csrc/vecadd.cu:268-288).  n % 16 == 0, 16-byte aligned pointers. */
+int tans_b200_fp8_vecadd_raw(const uint8_t *a, const uint8_t *b, uint8_t *c,
+                             int64_t n, void *stream);
+
+/* Build the reference-format decode table on the device from device copies
+ * of spread[4096] and freqs[n_syms] (n_syms <= 256).  This is the step that
+ * `gpu_tans_decode` performs on the host for every call
+ * (csrc/tans_decode.cu:23-59, :389).  table: device int32[4096].
+ * status: optional device int32; TANS_B200_DATA_BAD_TABLE is OR-ed in when
+ * spread/freqs are inconsistent (the entries concerned are written as 0). */
+int tans_b200_build_decode_table(const int32_t *spread, const int32_t *freqs,
+                                 int64_t n_syms, int32_t *table,
+                                 int32_t *status, void *stream);
+
+/* Standalone decode: replaces `gpu_tans_decode` (csrc/tans_decode.cu:159-210)
+ * given a device decode table.
+ *   compressed[compressed_bytes], offsets[B+1], states[K], partial[K],
+ *   sign_mantissa[N/2][K] -> out[N][K] (element j of stream k at j*K + k).
+ * N = n_fp8_per_stream (even).  status: optional device int32 (OR-ed data
+ * error bits), may be NULL. */
+int tans_b200_decode(const uint8_t *compressed, int64_t compressed_bytes,
+                     const int32_t *offsets, const uint16_t *states,
+                     const uint8_t *partial, const uint8_t *sign_mantissa,
+                     const int32_t *decode_table, uint8_t *out,
+                     int64_t n_streams, int64_t n_fp8_per_stream,
+                     int32_t *status, void *stream);
+
+/* Fused decode + FP8 add: replaces `fp8_vecadd_fused_tans`
+ * (csrc/vecadd.cu:290-393).  Both inputs share decode_table and the stream
+ * count K; sm tensors are tiled [N/16][K][8]; out is tiled [N/16][K][16]
+ * (element 16j+t of stream k at (j*K + k)*16 + t).  N % 16 == 0.
+ * status: optional device int32, may be NULL. */
+int tans_b200_fp8_vecadd_fused(
+    const uint8_t *a_compressed, int64_t a_compressed_bytes,
+    const int32_t *a_offsets, const uint16_t *a_states,
+    const uint8_t *a_partial, const uint8_t *a_sm,
+    const uint8_t *b_compressed, int64_t b_compressed_bytes,
+    const int32_t *b_offsets, const uint16_t *b_states,
+    const uint8_t *b_partial, const uint8_t *b_sm,
+    const int32_t *decode_table, uint8_t *out, int64_t n_streams,
+    int64_t n_fp8_per_stream, int32_t *status, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TANS_B200_H */

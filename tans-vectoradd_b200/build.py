@@ -1,0 +1,86 @@
+"""Build libtans_b200.so (the C-ABI library) in-tree, for sm_100a only.
+
+    python tans-vectoradd_b200/build.py [--force] [--verbose]
+
+Sources: csrc/kernels.cu (device kernels + device entry points) and
+csrc/host.cpp (CPU encoder, host table builder, FP8 splitter, errors).
+Output: rans_vectoradd/libtans_b200.so next to the Python package that loads
+it, so the built file travels with the source tree.  No torch headers are
+involved; the library depends only on the CUDA runtime and OpenMP.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+import tempfile
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join(HERE, "csrc")
+INCLUDE = os.path.join(os.path.dirname(HERE), "include")
+OUT = os.path.join(HERE, "rans_vectoradd", "libtans_b200.so")
+SOURCES = [os.path.join(CSRC, "kernels.cu"), os.path.join(CSRC, "host.cpp"),
+           os.path.join(INCLUDE, "tans_b200.h")]
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def cuda_home() -> str:
+    for cand in (os.environ.get("CUDA_HOME"), "/usr/local/cuda"):
+        if cand and os.path.exists(os.path.join(cand, "bin", "nvcc")):
+            return cand
+    nvcc = shutil.which("nvcc")
+    if nvcc:
+        return os.path.dirname(os.path.dirname(nvcc))
+    raise RuntimeError("nvcc not found: set CUDA_HOME")
+
+
+def up_to_date() -> bool:
+    if not os.path.exists(OUT):
+        return False
+    t = os.path.getmtime(OUT)
+    return all(os.path.getmtime(s) <= t for s in SOURCES + [__file__])
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    if not force and up_to_date():
+        return OUT
+    cuda = cuda_home()
+    nvcc = os.path.join(cuda, "bin", "nvcc")
+    # the system g++ carries OpenMP; some images point CXX at a compiler without it
+    cxx = shutil.which("g++") or "g++"
+    with tempfile.TemporaryDirectory() as tmp:
+        k_obj = os.path.join(tmp, "kernels.o")
+        h_obj = os.path.join(tmp, "host.o")
+        cmds = [
+            [nvcc, "-c", SOURCES[0], "-o", k_obj, *ARCH, "-O3", "-lineinfo", "-std=c++17",
+             "-Xcompiler", "-fPIC", "-ccbin", cxx, "-Xptxas", "-v" if verbose else "-O3"],
+            [cxx, "-c", SOURCES[1], "-o", h_obj, "-O3", "-fPIC", "-fopenmp", "-std=c++17",
+             "-Wall", "-Wextra"],
+        ]
+        procs = [subprocess.Popen(c, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+                 for c in cmds]
+        for cmd, p in zip(cmds, procs):
+            out, _ = p.communicate()
+            if verbose or p.returncode:
+                sys.stderr.write(out)
+            if p.returncode:
+                raise RuntimeError(f"build failed: {' '.join(cmd)}")
+        tmp_out = os.path.join(tmp, "libtans_b200.so")
+        link = [nvcc, "-shared", *ARCH, "-ccbin", cxx, k_obj, h_obj, "-o", tmp_out,
+                "-Xcompiler", "-fopenmp", "-lgomp", "-cudart", "shared"]
+        r = subprocess.run(link, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+        if r.returncode:
+            sys.stderr.write(r.stdout)
+            raise RuntimeError("link failed")
+        shutil.move(tmp_out, OUT)
+    return OUT
+
+
+if __name__ == "__main__":
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--verbose", action="store_true")
+    a = ap.parse_args()
+    print(build(force=a.force, verbose=a.verbose))

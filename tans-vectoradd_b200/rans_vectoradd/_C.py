@@ -1,0 +1,280 @@
+"""Operator surface of the reference's compiled module ``rans_vectoradd._C``
+(pybind, csrc/fp8_memcpy.cu:66-78), implemented over libtans_b200's C ABI.
+
+Same five ops, same argument meaning, same outputs and the same check
+messages (raised as RuntimeError, as TORCH_CHECK does).  Differences, all
+deliberate:
+
+* launches go to torch's *current* stream of the inputs' device, under a
+  device guard taken from the first tensor argument (the reference launches
+  on the legacy default stream of whatever device is current);
+* ``gpu_tans_decode`` builds its decode table on the device when spread and
+  freqs are CUDA tensors (no host round trip); with CPU tensors it builds it
+  on the host with the reference's checks, as csrc/tans_decode.cu:23-59 does;
+* malformed stream metadata never makes a kernel read out of bounds; data
+  errors are OR-ed into a per-device status word (``data_status``) and, with
+  ``TANS_B200_CHECK=1`` in the environment, raised after every call;
+* ``TANS_STREAMS_PER_BLOCK`` (csrc/vecadd.cu:245-258) is still validated, but
+  the kernel geometry is chosen from the stream count and the SM count.
+
+There is no CPU fallback: every op that the reference runs on the GPU
+requires CUDA tensors and the library's sm_100a kernels.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from ._lib import LIB, check
+
+_L = 4096
+_BLOCK = 128
+_TILE_PAIRS = 8
+
+_status_bufs: dict[int, torch.Tensor] = {}
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _status(device: torch.device) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _status_bufs.get(idx)
+    if buf is None:
+        buf = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", idx))
+        _status_bufs[idx] = buf
+    return buf
+
+
+def data_status(device: torch.device | int | None = None, reset: bool = True) -> int:
+    """Synchronise and return the OR of data-error bits (1 offsets, 2 states,
+    4 table) raised by decode/fused calls on `device` since the last reset."""
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index or 0))
+    buf = _status(dev)
+    v = int(buf.item())
+    if reset:
+        buf.zero_()
+    return v
+
+
+def _post_check(device: torch.device) -> None:
+    if os.environ.get("TANS_B200_CHECK", "") not in ("", "0"):
+        v = data_status(device)
+        if v:
+            raise RuntimeError(f"tANS data error status {v} (1 offsets, 2 states, 4 table)")
+
+
+def _req(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _check_u8_cuda_contiguous(name: str, t: torch.Tensor) -> None:
+    _req(t.is_cuda, f"{name} must be CUDA")
+    _req(t.dtype == torch.uint8, f"{name} must be uint8")
+    _req(t.is_contiguous(), f"{name} must be contiguous")
+
+
+def _same_device(dev: torch.device, *ts: torch.Tensor) -> None:
+    for t in ts:
+        _req(t.device == dev, f"all tensors must be on {dev}; got one on {t.device}")
+
+
+def _streams_per_block_from_env() -> int:
+    value = os.environ.get("TANS_STREAMS_PER_BLOCK")
+    if not value:
+        return 8
+    try:
+        parsed = int(value, 10)
+    except ValueError:
+        raise RuntimeError("TANS_STREAMS_PER_BLOCK must be an integer") from None
+    _req(parsed in (1, 2, 4, 8), "TANS_STREAMS_PER_BLOCK must be one of 1, 2, 4, or 8")
+    return parsed
+
+
+# ------------------------------------------------------------------ encoder
+
+def tans_encode_interleaved(symbols: torch.Tensor, freqs: torch.Tensor, spread: torch.Tensor):
+    """CPU tANS encoder -> GPU-ready interleaved slab layout
+    (csrc/tans_codec.cpp:69-196).  Returns (compressed u8, states u16[K],
+    offsets i32[B+1], partial u8[K]), all CPU tensors."""
+    _req(symbols.dim() == 2, "symbols must be [K, N]")
+    _req(symbols.dtype == torch.uint8, "symbols must be uint8")
+    _req(freqs.dtype == torch.int32, "freqs must be int32")
+    _req(spread.dtype == torch.int32, "spread must be int32")
+    _req(symbols.is_contiguous() and not symbols.is_cuda, "symbols must be contiguous CPU")
+    _req(freqs.is_contiguous() and not freqs.is_cuda, "freqs must be contiguous CPU")
+    _req(spread.is_contiguous() and not spread.is_cuda, "spread must be contiguous CPU")
+    _req(spread.numel() == _L, f"spread must have {_L} entries")
+    K, N = symbols.shape
+    h = ctypes.c_void_p()
+    check(LIB.tans_b200_encode(symbols.data_ptr(), K, N, freqs.data_ptr(), freqs.numel(),
+                               spread.data_ptr(), 0, ctypes.byref(h)))
+    try:
+        nbytes, nblocks = ctypes.c_int64(), ctypes.c_int64()
+        check(LIB.tans_b200_encoded_sizes(h, ctypes.byref(nbytes), ctypes.byref(nblocks)))
+        comp = torch.empty(nbytes.value, dtype=torch.uint8)
+        states = torch.empty(K, dtype=torch.uint16)
+        offsets = torch.empty(nblocks.value + 1, dtype=torch.int32)
+        partial = torch.empty(K, dtype=torch.uint8)
+        check(LIB.tans_b200_encoded_export(h, comp.data_ptr(), states.data_ptr(),
+                                           offsets.data_ptr(), partial.data_ptr()))
+    finally:
+        LIB.tans_b200_encoded_free(h)
+    return comp, states, offsets, partial
+
+
+# ------------------------------------------------------------ decode table
+
+def build_decode_table_device(spread: torch.Tensor, freqs: torch.Tensor,
+                              device: torch.device | None = None) -> torch.Tensor:
+    """Reference-format decode table int32[4096] on `device` (default: the
+    device of spread).  Built by a kernel from CUDA inputs, on the host from
+    CPU inputs (then copied)."""
+    _req(spread.dtype == torch.int32, "spread must be int32")
+    _req(spread.numel() == _L, f"spread must have {_L} entries")
+    _req(freqs.dtype == torch.int32, "freqs must be int32")
+    dev = device if device is not None else spread.device
+    if spread.is_cuda and freqs.is_cuda and spread.device == dev and freqs.device == dev:
+        _req(0 < freqs.numel() <= 256, "decode table alphabet must be 1..256 symbols")
+        spread_c, freqs_c = spread.contiguous(), freqs.contiguous()
+        with torch.cuda.device(dev):
+            table = torch.empty(_L, dtype=torch.int32, device=dev)
+            check(LIB.tans_b200_build_decode_table(spread_c.data_ptr(), freqs_c.data_ptr(),
+                                                   freqs_c.numel(), table.data_ptr(),
+                                                   _status(dev).data_ptr(), _stream(dev)))
+        return table
+    sp = spread.detach().cpu().contiguous()
+    fr = freqs.detach().cpu().contiguous()
+    table = torch.empty(_L, dtype=torch.int32)
+    check(LIB.tans_b200_build_decode_table_host(sp.data_ptr(), fr.data_ptr(), fr.numel(),
+                                                table.data_ptr()))
+    return table.to(dev)
+
+
+# ------------------------------------------------------------------ decode
+
+def gpu_tans_decode(compressed: torch.Tensor, offsets: torch.Tensor, states: torch.Tensor,
+                    partial_cnts: torch.Tensor, sign_mantissa: torch.Tensor,
+                    spread: torch.Tensor, freqs: torch.Tensor,
+                    n_fp8_per_stream: int) -> torch.Tensor:
+    """GPU tANS pair decoder.  Returns [n_fp8_per_stream, n_streams] uint8
+    (csrc/tans_decode.cu:159-210)."""
+    _req(compressed.is_cuda and compressed.dtype == torch.uint8 and compressed.is_contiguous(),
+         "compressed must be contiguous CUDA uint8")
+    _req(offsets.is_cuda and offsets.dtype == torch.int32 and offsets.is_contiguous(),
+         "offsets must be contiguous CUDA int32")
+    _req(states.is_cuda and states.dtype == torch.uint16 and states.is_contiguous(),
+         "states must be contiguous CUDA uint16")
+    _req(partial_cnts.is_cuda and partial_cnts.dtype == torch.uint8
+         and partial_cnts.is_contiguous(), "partial_cnts must be contiguous CUDA uint8")
+    _req(sign_mantissa.is_cuda and sign_mantissa.dtype == torch.uint8
+         and sign_mantissa.is_contiguous(), "sign_mantissa must be contiguous CUDA uint8")
+    N = int(n_fp8_per_stream)
+    _req(N % 2 == 0, "n_fp8_per_stream must be even")
+    _req(compressed.numel() % 4 == 0, "compressed length must be divisible by 4 bytes")
+    K = states.numel()
+    n_blocks = (K + _BLOCK - 1) // _BLOCK
+    _req(offsets.numel() == n_blocks + 1, "offsets must have n_blocks + 1 entries")
+    _req(partial_cnts.numel() == K, "partial_cnts must match states")
+    _req(sign_mantissa.numel() == (N // 2) * K, "sign_mantissa has the wrong shape")
+    dev = compressed.device
+    _same_device(dev, offsets, states, partial_cnts, sign_mantissa)
+    with torch.cuda.device(dev):
+        table = build_decode_table_device(spread, freqs, dev)
+        out = torch.empty((N, K), dtype=torch.uint8, device=dev)
+        check(LIB.tans_b200_decode(compressed.data_ptr(), compressed.numel(), offsets.data_ptr(),
+                                   states.data_ptr(), partial_cnts.data_ptr(),
+                                   sign_mantissa.data_ptr(), table.data_ptr(), out.data_ptr(),
+                                   K, N, _status(dev).data_ptr(), _stream(dev)))
+    _post_check(dev)
+    return out
+
+
+# ------------------------------------------------------------ memcpy / raw
+
+def fp8_memcpy(A: torch.Tensor) -> torch.Tensor:
+    """Pure HBM copy C[i] = A[i] (csrc/fp8_memcpy.cu:45-64): the practical
+    bandwidth ceiling of a 1-read + 1-write SM kernel."""
+    _req(A.is_cuda, "A must be CUDA")
+    _req(A.dtype == torch.uint8, "A must be uint8")
+    _req(A.is_contiguous(), "A must be contiguous")
+    _req(A.numel() % 16 == 0, "A length must be a multiple of 16")
+    with torch.cuda.device(A.device):
+        C = torch.empty_like(A)
+        check(LIB.tans_b200_fp8_memcpy(A.data_ptr(), C.data_ptr(), A.numel(), _stream(A.device)))
+    return C
+
+
+def fp8_vecadd_raw(A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
+    """Uncompressed FP8 vector add C[i] = e4m3(A[i] + B[i]) with satfinite
+    rounding (csrc/vecadd.cu:268-288)."""
+    _check_u8_cuda_contiguous("A", A)
+    _check_u8_cuda_contiguous("B", B)
+    _req(A.numel() == B.numel(), "A and B must have the same length")
+    _req(A.numel() % 16 == 0, "A/B length must be a multiple of 16")
+    _same_device(A.device, B)
+    with torch.cuda.device(A.device):
+        C = torch.empty_like(A)
+        check(LIB.tans_b200_fp8_vecadd_raw(A.data_ptr(), B.data_ptr(), C.data_ptr(), A.numel(),
+                                           _stream(A.device)))
+    return C
+
+
+# ------------------------------------------------------------------ fused
+
+def fp8_vecadd_fused_tans(a_comp: torch.Tensor, a_offsets: torch.Tensor,
+                          a_states: torch.Tensor, a_partial: torch.Tensor, a_sm: torch.Tensor,
+                          b_comp: torch.Tensor, b_offsets: torch.Tensor,
+                          b_states: torch.Tensor, b_partial: torch.Tensor, b_sm: torch.Tensor,
+                          decode_tbl: torch.Tensor, n_fp8_per_stream: int) -> torch.Tensor:
+    """Fused tANS decompress + FP8 vector add (csrc/vecadd.cu:290-393).
+    Returns the tiled output [N/16 * K * 16] uint8."""
+    for name, t in (("a_comp", a_comp), ("a_partial", a_partial), ("a_sm", a_sm),
+                    ("b_comp", b_comp), ("b_partial", b_partial), ("b_sm", b_sm)):
+        _check_u8_cuda_contiguous(name, t)
+    for name, t, dt, dn in (("a_offsets", a_offsets, torch.int32, "int32"),
+                            ("b_offsets", b_offsets, torch.int32, "int32"),
+                            ("a_states", a_states, torch.uint16, "uint16"),
+                            ("b_states", b_states, torch.uint16, "uint16"),
+                            ("decode_tbl", decode_tbl, torch.int32, "int32")):
+        _req(t.is_cuda and t.dtype == dt and t.is_contiguous(),
+             f"{name} must be contiguous CUDA {dn}")
+    _req(a_states.numel() == b_states.numel(), "A/B stream counts must match")
+    _req(a_partial.numel() == a_states.numel() and b_partial.numel() == b_states.numel(),
+         "partial-count tensors must match state tensors")
+    _req(a_comp.numel() % 4 == 0 and b_comp.numel() % 4 == 0,
+         "compressed tensors must have byte lengths divisible by 4")
+    _req(decode_tbl.numel() == _L, f"decode_tbl must have {_L} entries")
+    N = int(n_fp8_per_stream)
+    _req(N % (2 * _TILE_PAIRS) == 0, f"n_fp8_per_stream must be divisible by {2 * _TILE_PAIRS}")
+    K = a_states.numel()
+    n_enc_blocks = (K + _BLOCK - 1) // _BLOCK
+    _req(a_offsets.numel() == n_enc_blocks + 1 and b_offsets.numel() == n_enc_blocks + 1,
+         "offset tensors must have n_encoder_blocks + 1 entries")
+    n_tiles = (N // 2) // _TILE_PAIRS
+    expected_sm = n_tiles * K * _TILE_PAIRS
+    _req(a_sm.numel() == expected_sm and b_sm.numel() == expected_sm,
+         "sign/mantissa tensors have the wrong tiled size")
+    dev = a_comp.device
+    _same_device(dev, a_offsets, a_states, a_partial, a_sm, b_comp, b_offsets, b_states,
+                 b_partial, b_sm, decode_tbl)
+    _streams_per_block_from_env()
+    with torch.cuda.device(dev):
+        out = torch.empty(n_tiles * K * _TILE_PAIRS * 2, dtype=torch.uint8, device=dev)
+        check(LIB.tans_b200_fp8_vecadd_fused(
+            a_comp.data_ptr(), a_comp.numel(), a_offsets.data_ptr(), a_states.data_ptr(),
+            a_partial.data_ptr(), a_sm.data_ptr(),
+            b_comp.data_ptr(), b_comp.numel(), b_offsets.data_ptr(), b_states.data_ptr(),
+            b_partial.data_ptr(), b_sm.data_ptr(),
+            decode_tbl.data_ptr(), out.data_ptr(), K, N, _status(dev).data_ptr(), _stream(dev)))
+    _post_check(dev)
+    return out
+
+
+__all__ = ["tans_encode_interleaved", "gpu_tans_decode", "fp8_memcpy", "fp8_vecadd_raw",
+           "fp8_vecadd_fused_tans", "build_decode_table_device", "data_status"]

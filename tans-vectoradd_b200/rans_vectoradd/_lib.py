@@ -1,0 +1,62 @@
+"""ctypes binding of libtans_b200.so (C ABI: include/tans_b200.h).
+
+The library is loaded from this package directory.  There is no fallback:
+if it is missing or does not load, importing rans_vectoradd raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libtans_b200.so")
+
+OK = 0
+DATA_BAD_OFFSETS = 1
+DATA_BAD_STATE = 2
+DATA_BAD_TABLE = 4
+
+
+def _load() -> ctypes.CDLL:
+    if not os.path.exists(LIB_PATH):
+        raise ImportError(
+            f"{LIB_PATH} is missing: build it with `python tans-vectoradd_b200/build.py` "
+            "(rans_vectoradd has no CPU fallback)")
+    lib = ctypes.CDLL(LIB_PATH)
+    p, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int
+    sig = {
+        "tans_b200_last_error": (ctypes.c_char_p, []),
+        "tans_b200_version": (ctypes.c_char_p, []),
+        "tans_b200_build_decode_table_host": (i32, [p, p, i64, p]),
+        "tans_b200_encode": (i32, [p, i64, i64, p, i64, p, i32, ctypes.POINTER(p)]),
+        "tans_b200_encoded_sizes": (i32, [p, ctypes.POINTER(i64), ctypes.POINTER(i64)]),
+        "tans_b200_encoded_export": (i32, [p, p, p, p, p]),
+        "tans_b200_encoded_free": (None, [p]),
+        "tans_b200_split_fp8": (i32, [p, i64, i64, i64, p, p, p, i32]),
+        "tans_b200_sm_count": (i32, [ctypes.POINTER(i32)]),
+        "tans_b200_fp8_memcpy": (i32, [p, p, i64, p]),
+        "tans_b200_fp8_vecadd_raw": (i32, [p, p, p, i64, p]),
+        "tans_b200_build_decode_table": (i32, [p, p, i64, p, p, p]),
+        "tans_b200_decode": (i32, [p, i64, p, p, p, p, p, p, i64, i64, p, p]),
+        "tans_b200_fp8_vecadd_fused": (i32, [p, i64, p, p, p, p, p, i64, p, p, p, p, p, p,
+                                             i64, i64, p, p]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+LIB = _load()
+
+
+def check(rc: int) -> None:
+    """Raise RuntimeError (what TORCH_CHECK raises) for a nonzero status."""
+    if rc != OK:
+        msg = LIB.tans_b200_last_error().decode(errors="replace")
+        raise RuntimeError(msg or f"libtans_b200 error {rc}")
+
+
+def version() -> str:
+    return LIB.tans_b200_version().decode()

@@ -1,0 +1,196 @@
+"""Product codec (rans_vectoradd.tans_codec + the C++ encoder) against the
+reference's golden outputs, byte for byte.  CPU only."""
+from __future__ import annotations
+
+import hashlib
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from rans_vectoradd import QWEN3_14B_FP8_EXP, _C, random_fp8_bytes, tans_codec
+from rans_vectoradd.data import exponent_histogram, normal_fp8_bytes
+
+GOLDEN = os.path.join(os.path.dirname(__file__), "golden")
+NAMES = ["compressed", "states", "offsets", "partial", "sm", "pair_freqs", "spread"]
+QWEN = torch.tensor(QWEN3_14B_FP8_EXP, dtype=torch.float64)
+
+
+def sha(a) -> str:
+    a = a.numpy() if hasattr(a, "numpy") else np.asarray(a)
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def test_constants():
+    assert tans_codec.L == 4096 and tans_codec.M == 4096
+    assert tans_codec.SIGMA == 2563 and tans_codec.BLOCK_STREAMS == 128
+
+
+@pytest.mark.parametrize("K,N", [(128, 128), (1024, 128), (10_000, 128), (100_000, 128)])
+def test_decode_cases_byte_identical(golden_digests, K, N):
+    """test_gpu_decode_tans.py:17-25,69-74 inputs: seed 42, Qwen profile."""
+    g = golden_digests[f"decode_K{K}_N{N}"]
+    torch.manual_seed(42)
+    fp8 = random_fp8_bytes(K * N, device="cpu").reshape(K, N)
+    assert sha(fp8) == g["input"], "generator no longer reproduces the reference's bytes"
+    out = tans_codec.encode(fp8, QWEN)
+    for name, t in zip(NAMES, out):
+        assert sha(t) == g[name], name
+    tab = tans_codec.build_decode_table(out[6].numpy(), out[5].numpy())
+    assert sha(tab) == g["table"]
+
+
+@pytest.mark.parametrize("K,N", [(1024, 128), (10_000, 256), (1024, 1024)])
+def test_fused_cases_byte_identical(golden_digests, K, N):
+    """test_vecadd_tans.py:30-38,76-80 inputs: seed 0, two inputs, tile 8."""
+    g = golden_digests[f"fused_K{K}_N{N}"]
+    torch.manual_seed(0)
+    a = random_fp8_bytes(K * N, device="cpu").reshape(K, N)
+    b = random_fp8_bytes(K * N, device="cpu").reshape(K, N)
+    assert sha(a) == g["input_a"] and sha(b) == g["input_b"]
+    for x, gg in ((a, g["a"]), (b, g["b"])):
+        for name, t in zip(NAMES, tans_codec.encode(x, QWEN, tile=8)):
+            assert sha(t) == gg[name], name
+
+
+def test_cfg0_generator_and_encode(golden_digests):
+    """cfg0: x, y ~ N(0,1) (seed 0) * 448/max -> e4m3, 2^24 each, N = 8192."""
+    g = golden_digests["cfg0"]
+    gen = torch.Generator().manual_seed(0)
+    x = normal_fp8_bytes(g["n"], generator=gen)
+    y = normal_fp8_bytes(g["n"], generator=gen)
+    assert sha(x) == g["input_x"] and sha(y) == g["input_y"]
+    hist = exponent_histogram(x, y)
+    assert hist.tolist() == g["exp_hist"]
+    for v, gg in ((x, g["x"]), (y, g["y"])):
+        out = tans_codec.encode(v.reshape(g["K"], g["N"]), hist.double(), tile=8)
+        for name, t in zip(NAMES, out):
+            assert sha(t) == gg[name], name
+
+
+def test_tables_against_golden():
+    t = np.load(os.path.join(GOLDEN, "tables.npz"))
+    pf = tans_codec.pair_freqs_from_exponents(torch.from_numpy(t["qwen_exp"]))
+    assert np.array_equal(pf, t["qwen_pair_freqs"])
+    sp = tans_codec.build_spread(pf)
+    assert np.array_equal(sp, t["qwen_spread"])
+    assert np.array_equal(tans_codec.build_decode_table(sp, pf).numpy(), t["qwen_table"])
+    pf0 = tans_codec.pair_freqs_from_exponents(torch.from_numpy(t["cfg0_exp_hist"]).double())
+    assert np.array_equal(pf0, t["cfg0_pair_freqs"])
+    assert np.array_equal(tans_codec.build_decode_table(t["cfg0_spread"], pf0).numpy(),
+                          t["cfg0_table"])
+
+
+def test_host_table_builder_matches_numpy():
+    t = np.load(os.path.join(GOLDEN, "tables.npz"))
+    from rans_vectoradd._lib import LIB, check
+    sp = np.ascontiguousarray(t["qwen_spread"], np.int32)
+    pf = np.ascontiguousarray(t["qwen_pair_freqs"], np.int32)
+    out = np.empty(4096, np.int32)
+    check(LIB.tans_b200_build_decode_table_host(sp.ctypes.data, pf.ctypes.data, pf.size,
+                                                out.ctypes.data))
+    assert np.array_equal(out, t["qwen_table"])
+
+
+def test_quantize_freqs_properties():
+    rng = np.random.default_rng(3)
+    for _ in range(50):
+        p = rng.random(256) ** 4
+        p[rng.random(256) < 0.2] = 0
+        p /= p.sum()
+        f = tans_codec.quantize_freqs(p)
+        assert f.sum() == 4096
+        assert (f[p > 0] >= 1).all() and (f[p == 0] == 0).all()
+
+
+def test_quantize_freqs_single_symbol():
+    p = np.zeros(256)
+    p[7] = 1.0
+    f = tans_codec.quantize_freqs(p)
+    assert f[7] == 4096 and f.sum() == 4096
+    sp = tans_codec.build_spread(f)
+    assert (sp == 7).all()
+    tab = tans_codec.build_decode_table(sp, f).numpy().view(np.uint32)
+    assert ((tab >> 8) & 15 == 0).all()  # nb = 0 everywhere: zero bits per symbol
+
+
+def test_single_symbol_stream_round_trip():
+    """A one-symbol alphabet codes to zero bits: G_b = 1 padded slab, partial 0."""
+    f = np.zeros(256, np.int32)
+    f[0x77] = 4096
+    sp = tans_codec.build_spread(f)
+    syms = torch.full((130, 64), 0x77, dtype=torch.uint8)
+    comp, st, off, part = _C.tans_encode_interleaved(syms, torch.from_numpy(f),
+                                                     torch.from_numpy(sp))
+    oc, ost, ooff, opart = oracle.encode(syms, f, sp)
+    assert np.array_equal(comp.numpy(), oc) and np.array_equal(off.numpy(), ooff)
+    assert np.array_equal(st.numpy(), ost) and np.array_equal(part.numpy(), opart)
+    assert comp.numel() == 2 * 512
+
+
+@pytest.mark.parametrize("K,N", [(1, 2), (127, 30), (129, 2), (300, 1000)])
+def test_encoder_matches_oracle_ragged(K, N):
+    gen = torch.Generator().manual_seed(K * 1000 + N)
+    fp8 = random_fp8_bytes(K * N, device="cpu", generator=gen).reshape(K, N)
+    e = (fp8 >> 3) & 15
+    syms = (e[:, 0::2] * 16 + e[:, 1::2]).contiguous()
+    pf = tans_codec.pair_freqs_from_exponents(torch.tensor(QWEN3_14B_FP8_EXP))
+    sp = tans_codec.build_spread(pf)
+    got = _C.tans_encode_interleaved(syms, torch.from_numpy(pf), torch.from_numpy(sp))
+    want = oracle.encode(syms, pf, sp)
+    for g_, w_ in zip(got, want):
+        assert np.array_equal(g_.numpy(), w_)
+
+
+def test_empty_stream_set():
+    pf = tans_codec.pair_freqs_from_exponents(torch.tensor(QWEN3_14B_FP8_EXP))
+    sp = tans_codec.build_spread(pf)
+    comp, st, off, part = _C.tans_encode_interleaved(
+        torch.empty((0, 16), dtype=torch.uint8), torch.from_numpy(pf), torch.from_numpy(sp))
+    assert comp.numel() == 0 and st.numel() == 0 and off.tolist() == [0]
+
+
+def test_encoder_rejects_bad_inputs():
+    pf = tans_codec.pair_freqs_from_exponents(torch.tensor(QWEN3_14B_FP8_EXP))
+    sp = torch.from_numpy(tans_codec.build_spread(pf))
+    pft = torch.from_numpy(pf)
+    syms = torch.zeros((4, 8), dtype=torch.uint8)
+    bad = pft.clone()
+    bad[0] += 1
+    with pytest.raises(RuntimeError, match="freqs must sum to L=4096"):
+        _C.tans_encode_interleaved(syms, bad, sp)
+    with pytest.raises(RuntimeError, match="symbols must be"):
+        _C.tans_encode_interleaved(syms.flatten(), pft, sp)
+    # a symbol that occurs but has no slot: the reference loops forever here
+    f = np.zeros(256, np.int32)
+    f[1] = 4096
+    with pytest.raises(RuntimeError, match="zero frequency"):
+        _C.tans_encode_interleaved(syms, torch.from_numpy(f),
+                                   torch.from_numpy(tans_codec.build_spread(f)))
+    with pytest.raises(RuntimeError, match="spread"):
+        _C.tans_encode_interleaved(syms, pft, torch.zeros(4096, dtype=torch.int32))
+
+
+@pytest.mark.parametrize("tile", [0, 8, 4])
+def test_split_matches_torch_ops(tile):
+    """split_fp8 (C++) against the torch-op formulation of tans_codec.py:109-124."""
+    gen = torch.Generator().manual_seed(tile)
+    K, N = 37, 64
+    fp8 = torch.randint(0, 256, (K, N), dtype=torch.uint8, generator=gen)
+    syms, sm, hist = tans_codec.split_fp8(fp8, tile, want_hist=True)
+    e = (fp8 >> 3) & 15
+    smn = ((fp8 >> 4) & 8) | (fp8 & 7)
+    assert torch.equal(syms, (e[:, 0::2] * 16 + e[:, 1::2]))
+    packed = smn[:, 0::2] | (smn[:, 1::2] << 4)
+    want = (packed.reshape(K, N // 2 // tile, tile).permute(1, 0, 2).contiguous()
+            if tile else packed.t().contiguous())
+    assert torch.equal(sm, want)
+    assert torch.equal(hist, torch.bincount(e.flatten().long(), minlength=16))
+
+
+def test_encode_tile_assertion():
+    fp8 = torch.zeros((4, 20), dtype=torch.uint8)
+    with pytest.raises(AssertionError, match="not divisible by tile"):
+        tans_codec.encode(fp8, QWEN, tile=8)
