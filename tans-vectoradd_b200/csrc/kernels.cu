@@ -42,6 +42,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <climits>
 #include <mutex>
 
 namespace tans_b200 {
@@ -241,12 +242,17 @@ __device__ __forceinline__ void load_table(uint32_t *tbl, const int32_t *__restr
     if (bad && status) atomicOr(status, TANS_B200_DATA_BAD_TABLE);
 }
 
+// One stream's decoder state.  The bit window is hi:lo (next bits at the top
+// of hi after skipping cnt bits) plus one slab of look-ahead in nx.  `v` is
+// the word offset (row * 128) of the slab that the next advance loads into
+// nx; rows count down from the top of the encoder block, and row r of this
+// lane lives at src[r * 128].
 struct Chain {
     uint32_t addr;  // byte offset of the current entry in this lane's table copy
     uint32_t cnt;   // bits 0-4: bits used in hi; bit 5 flips per exhausted slab
     uint32_t hi, lo, nx;
-    int32_t pos;    // word index (from the block base) of the next slab to fetch
-    const uint32_t *blk;
+    int32_t v;
+    const uint32_t *src;
 };
 
 // A chain for a lane with no stream: steps harmlessly, never loads.
@@ -254,16 +260,18 @@ __device__ __forceinline__ void chain_idle(Chain &ch, const uint32_t *comp) {
     ch.addr = 0;
     ch.cnt = 0;
     ch.hi = ch.lo = ch.nx = 0;
-    ch.pos = -1;
-    ch.blk = comp;
+    ch.v = -kBlk;
+    ch.src = comp;
 }
 
 // init_tans_ctx (csrc/tans_decode.cu:65-92) with in-kernel validation.
-__device__ __forceinline__ bool chain_init(Chain &ch, const uint32_t *__restrict__ comp,
-                                           int64_t comp_bytes, const int32_t *__restrict__ offsets,
-                                           const uint16_t *__restrict__ states,
-                                           const uint8_t *__restrict__ partial, int64_t sid,
-                                           uint32_t lane_off, int32_t *status) {
+// Returns the block's slab count G (0 if the metadata is malformed).
+__device__ __forceinline__ int32_t chain_init(Chain &ch, const uint32_t *__restrict__ comp,
+                                              int64_t comp_bytes,
+                                              const int32_t *__restrict__ offsets,
+                                              const uint16_t *__restrict__ states,
+                                              const uint8_t *__restrict__ partial, int64_t sid,
+                                              uint32_t lane_off, int32_t *status) {
     const int64_t b = sid / kBlk;
     const int tid = (int)(sid % kBlk);
     const int64_t base = __ldg(offsets + b), next = __ldg(offsets + b + 1);
@@ -273,46 +281,137 @@ __device__ __forceinline__ bool chain_init(Chain &ch, const uint32_t *__restrict
     if (x < (uint32_t)kL || x >= 2u * kL) {
         if (status) atomicOr(status, TANS_B200_DATA_BAD_STATE);
     }
-    ch.addr = ((x - kL) & (kL - 1)) * (4u * kCopies) + lane_off;
     const uint32_t p = __ldg(partial + sid);
-    ch.cnt = p == 0 ? 0u : ((32u - p) & 31u);
     if (!ok) {
         if (status) atomicOr(status, TANS_B200_DATA_BAD_OFFSETS);
-        ch.blk = comp;
-        ch.hi = ch.lo = ch.nx = 0;
-        ch.pos = -1;
-        return false;
+        chain_idle(ch, comp);
+        return 0;
     }
     const int32_t G = (int32_t)((next - base) / 512);
-    ch.blk = comp + base / 4;
-    ch.hi = __ldg(ch.blk + (G - 1) * kBlk + tid);
-    ch.lo = G >= 2 ? __ldg(ch.blk + (G - 2) * kBlk + tid) : 0u;
-    ch.nx = G >= 3 ? __ldg(ch.blk + (G - 3) * kBlk + tid) : 0u;
-    ch.pos = (G - 4) * kBlk + tid;
-    return true;
+    ch.addr = ((x - kL) & (kL - 1)) * (4u * kCopies) + lane_off;
+    ch.cnt = p == 0 ? 0u : ((32u - p) & 31u);
+    ch.src = comp + base / 4 + tid;
+    ch.hi = __ldg(ch.src + (G - 1) * kBlk);
+    ch.lo = G >= 2 ? __ldg(ch.src + (G - 2) * kBlk) : 0u;
+    ch.nx = G >= 3 ? __ldg(ch.src + (G - 3) * kBlk) : 0u;
+    ch.v = (G - 4) * kBlk;
+    return G;
 }
 
-// One tANS step (tans_step, csrc/tans_decode.cu:94-123): returns the entry of
-// the current state (pair symbol in bits 8-15) and advances the chain.
-__device__ __forceinline__ uint32_t chain_step(Chain &ch, const uint8_t *tbl_bytes) {
+// Table lookup plus everything up to the refill decision; both step flavours
+// share it.  Refill itself is branch-free: on a slab advance hi <- lo <- nx
+// and nx is reloaded by a predicated load, so nx is first read one advance
+// later.  Once a chain has run past its block's first row nothing is loaded
+// and nx keeps a stale word; those bits lie beyond the end of the stream and
+// are never consumed.
+#define TANS_STEP_HEAD                                                            \
+    "shf.l.wrap.b32 w, %3, %2, %1;\n\t"  /* w = top 32 bits of (hi:lo) << cnt */ \
+    "shf.l.wrap.b32 bits, w, 0, %6;\n\t" /* bits = w >> (32 - nb), 0 if nb=0 */  \
+    "shr.u32 f, %6, 16;\n\t"                                                    \
+    "mad.lo.u32 %0, bits, %8, f;\n\t" /* next entry address */                  \
+    "add.u32 c2, %1, %6;\n\t"         /* bit 5 flips when a slab is used up */  \
+    "xor.b32 t, c2, %1;\n\t"                                                    \
+    "and.b32 t, t, 32;\n\t"                                                     \
+    "setp.ne.u32 pa, t, 0;\n\t"                                                 \
+    "mov.u32 %1, c2;\n\t"                                                       \
+    "@pa mov.u32 %2, %3;\n\t" /* hi <- lo */                                    \
+    "@pa mov.u32 %3, %4;\n\t" /* lo <- nx */
+
+// Refill from global memory (any row, any time).
+__device__ __forceinline__ uint32_t chain_step_global(Chain &ch, const uint8_t *tbl_bytes) {
     const uint32_t e = *reinterpret_cast<const uint32_t *>(tbl_bytes + ch.addr);
-    const uint32_t w = __funnelshift_l(ch.lo, ch.hi, ch.cnt);
-    const uint32_t bits = __funnelshift_l(w, 0u, e);
-    ch.addr = (e >> 16) + (bits << kLog4C);
-    const uint32_t c2 = ch.cnt + e;
-    if ((c2 ^ ch.cnt) & 32u) {
-        ch.hi = ch.lo;
-        ch.lo = ch.nx;
-        ch.nx = ch.pos >= 0 ? __ldg(ch.blk + ch.pos) : 0u;
-        ch.pos -= kBlk;
-    }
-    ch.cnt = c2;
+    asm volatile(
+        "{\n\t"
+        ".reg .u32 w, bits, f, c2, t;\n\t"
+        ".reg .pred pa, pl;\n\t"
+        ".reg .u64 ga;\n\t" TANS_STEP_HEAD
+        "setp.ge.and.s32 pl, %5, 0, pa;\n\t"
+        "mul.wide.s32 ga, %5, 4;\n\t"
+        "add.u64 ga, ga, %7;\n\t"
+        "@pl ld.global.nc.u32 %4, [ga];\n\t" /* nx <- next slab of this stream */
+        "@pa sub.s32 %5, %5, %9;\n\t"
+        "}"
+        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.nx), "+r"(ch.v)
+        : "r"(e), "l"(ch.src), "n"(4 * kCopies), "n"(kBlk));
     return e;
 }
 
-__device__ __forceinline__ void chain_prefetch(const Chain &ch) {
-    const int32_t ahead = ch.pos - 4 * kBlk;
-    if (ahead >= 0) prefetch_l2(ch.blk + ahead);
+// Refill from this warp's shared-memory row ring: the slot of row r for this
+// lane is at ring_lane + (r mod R) * 128, i.e. (v & mask) | ring_lane.
+__device__ __forceinline__ uint32_t chain_step_ring(Chain &ch, const uint8_t *tbl_bytes,
+                                                    uint32_t ring_lane, uint32_t mask) {
+    const uint32_t e = *reinterpret_cast<const uint32_t *>(tbl_bytes + ch.addr);
+    asm volatile(
+        "{\n\t"
+        ".reg .u32 w, bits, f, c2, t, sa;\n\t"
+        ".reg .pred pa;\n\t" TANS_STEP_HEAD
+        "and.b32 sa, %5, %10;\n\t"
+        "or.b32 sa, sa, %11;\n\t"
+        "@pa ld.shared.u32 %4, [sa];\n\t" /* nx <- next slab of this stream */
+        "@pa sub.s32 %5, %5, %9;\n\t"
+        "}"
+        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.nx), "+r"(ch.v)
+        : "r"(e), "l"(ch.src), "n"(4 * kCopies), "n"(kBlk), "r"(mask), "r"(ring_lane));
+    return e;
+}
+
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, bool pred) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t"
+        "@p cp.async.ca.shared.global [%0], [%1], 4;\n\t}" ::"r"(dst),
+        "l"(src), "r"((uint32_t)pred)
+        : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Row ring of one chain of one warp.  The warp fills whole rows (each lane
+// copies its own column with cp.async, so every row is one coalesced 128-byte
+// read and a lane only ever reads data it copied itself).  Rows are filled
+// from the top down, at most kLookahead rows below the warp's fastest lane
+// and never over a slot whose row the slowest lane still needs.  A tile may
+// refill from the ring only when every row its lanes can reach in that tile
+// belongs to a fill group that has completed (cp.async.wait_group 2, i.e.
+// two tiles old); otherwise that tile refills from global memory.
+constexpr int kLookahead = 9;  // >= 3 tiles x 3 rows per tile
+constexpr int kRingLag = 2;    // completed groups are kRingLag tiles old
+
+struct Ring {
+    uint32_t lane_base;  // shared address of this lane's column, row slot 0
+    int32_t fill;        // next row to fill (warp-uniform)
+    int32_t done[kRingLag + 1];  // lowest filled row after the last kRingLag+1 fills
+};
+
+template <int R>
+__device__ __forceinline__ void ring_reset(Ring &rg, int32_t G) {
+    rg.fill = G - 4;
+#pragma unroll
+    for (int i = 0; i <= kRingLag; i++) rg.done[i] = INT_MAX;
+}
+
+// Issue this tile's fills; returns the lowest row a lane may refill from
+// during the tile (rows at or below it need the ring to be complete).
+template <int R>
+__device__ __forceinline__ int32_t ring_fill(Ring &rg, const Chain &ch, bool live) {
+    const int32_t row = ch.v >> 7;
+    const int32_t r_fast = __reduce_min_sync(0xffffffffu, live ? row : INT_MAX);
+    const int32_t r_slow = __reduce_max_sync(0xffffffffu, live ? row : INT_MIN);
+    if (r_fast != INT_MAX) {
+        const int32_t target = max(r_fast - kLookahead, 0);
+        const int32_t lim = r_slow - R;
+        while (rg.fill >= target && rg.fill > lim) {
+            cp_async4(rg.lane_base + ((uint32_t)(rg.fill & (R - 1)) << 7),
+                      ch.src + (int64_t)rg.fill * kBlk, live);
+            rg.fill--;
+        }
+    }
+#pragma unroll
+    for (int i = kRingLag; i > 0; i--) rg.done[i] = rg.done[i - 1];
+    rg.done[0] = rg.fill + 1;
+    return r_fast == INT_MAX ? INT_MAX : max(r_fast - 2, 0);
 }
 
 // Pack the pair symbols of four entries into one word (byte k = entry k).
@@ -347,6 +446,22 @@ Geometry balance(int64_t n_groups, int sms, int max_warps_per_cta) {
     return {(int)grid, (int)wpc};
 }
 
+constexpr int kTableBytes = kL * kCopies * 4;
+constexpr int kMaxWarps = 16;  // 512 threads per CTA, one CTA per SM
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// Shared address of warp w's ring area (aligned to its size so that a slot
+// address is (v & mask) | lane_base).
+template <int R>
+__device__ __forceinline__ uint32_t ring_area(const uint8_t *smem, int warp, int chains) {
+    const uint32_t bytes = R * 128u;
+    const uint32_t first = (smem_addr(smem) + kTableBytes + bytes - 1) & ~(bytes - 1);
+    return first + (uint32_t)(warp * chains) * bytes;
+}
+
 // ---------------------------------------------------------------- decode
 
 struct DecodeArgs {
@@ -362,54 +477,75 @@ struct DecodeArgs {
     int32_t *status;
 };
 
-__global__ void __launch_bounds__(1024, 1) decode_kernel(const DecodeArgs p) {
-    extern __shared__ __align__(16) uint32_t tbl[];
-    load_table(tbl, p.table, p.status);
+template <int R>
+__global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeArgs p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
     __syncthreads();
-    const uint8_t *tb = reinterpret_cast<const uint8_t *>(tbl);
-    const int lane = threadIdx.x & 31;
+    const uint8_t *tb = smem;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t lane_off = 4u * (lane % kCopies);
+    const uint32_t mask = (uint32_t)(R - 1) << 7;
+    Ring rg;
+    rg.lane_base = ring_area<R>(smem, warp, 1) + 4u * lane;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int64_t n_groups = (p.K + 31) / 32;
     const int64_t P = p.N / 2, K = p.K;
-    for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < n_groups;
-         g += warps) {
+    for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; g < n_groups; g += warps) {
         const int64_t sid = g * 32 + lane;
         const bool active = sid < K;
         Chain ch;
         chain_idle(ch, p.comp);
-        bool ok = false;
+        int32_t G = 0;
         if (active)
-            ok = chain_init(ch, p.comp, p.comp_bytes, p.offsets, p.states, p.partial, sid, lane_off,
-                            p.status);
-        const bool live = active && ok;
-        int64_t i = 0;
-        for (; i + kTablePairs <= P; i += kTablePairs) {
-            uint8_t m[kTablePairs];
+            G = chain_init(ch, p.comp, p.comp_bytes, p.offsets, p.states, p.partial, sid, lane_off,
+                           p.status);
+        const bool live = active && G > 0;
+        ring_reset<R>(rg, __reduce_max_sync(0xffffffffu, G));
+        // sign/mantissa bytes of the next tile are loaded one tile ahead, the
+        // rows three tiles ahead are prefetched into L2
+        uint32_t mn[kTablePairs];
 #pragma unroll
-            for (int j = 0; j < kTablePairs; j++) m[j] = live ? __ldg(p.sm + (i + j) * K + sid) : 0;
-            chain_prefetch(ch);
+        for (int j = 0; j < kTablePairs; j++)
+            mn[j] = (live && j < P) ? __ldg(p.sm + j * K + sid) : 0u;
+        if (live)
+            for (int64_t r = kTablePairs; r < 4 * kTablePairs && r < P; r++)
+                prefetch_l2(p.sm + r * K + sid);
+        for (int64_t i = 0; i < P; i += kTablePairs) {
+            uint32_t m[kTablePairs];
 #pragma unroll
             for (int j = 0; j < kTablePairs; j++) {
-                const uint32_t s = (chain_step(ch, tb) >> 8) & 0xFFu;
-                if (active) {
-                    const uint32_t v0 = ((m[j] & 8u) << 4) | ((s >> 4) << 3) | (m[j] & 7u);
-                    const uint32_t v1 = (((m[j] >> 4) & 8u) << 4) | ((s & 15u) << 3) | ((m[j] >> 4) & 7u);
+                m[j] = mn[j];
+                const int64_t r = i + kTablePairs + j;
+                mn[j] = (live && r < P) ? __ldg(p.sm + r * K + sid) : 0u;
+                if (live && r + 3 * kTablePairs < P) prefetch_l2(p.sm + (r + 3 * kTablePairs) * K + sid);
+            }
+            const int32_t need = ring_fill<R>(rg, ch, live);
+            cp_async_commit();
+            cp_async_wait<kRingLag>();
+            uint32_t s[kTablePairs];
+            if (need >= rg.done[kRingLag]) {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++)
+                    s[j] = chain_step_ring(ch, tb, rg.lane_base, mask);
+            } else {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++) s[j] = chain_step_global(ch, tb);
+            }
+            if (active) {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++) {
+                    if (i + j >= P) break;
+                    const uint32_t sy = (s[j] >> 8) & 0xFFu;
+                    const uint32_t v0 = ((m[j] & 8u) << 4) | ((sy >> 4) << 3) | (m[j] & 7u);
+                    const uint32_t v1 =
+                        (((m[j] >> 4) & 8u) << 4) | ((sy & 15u) << 3) | ((m[j] >> 4) & 7u);
                     p.out[(2 * (i + j)) * K + sid] = live ? (uint8_t)v0 : 0;
                     p.out[(2 * (i + j) + 1) * K + sid] = live ? (uint8_t)v1 : 0;
                 }
             }
         }
-        for (; i < P; i++) {
-            const uint8_t m = live ? __ldg(p.sm + i * K + sid) : 0;
-            const uint32_t s = (chain_step(ch, tb) >> 8) & 0xFFu;
-            if (active) {
-                const uint32_t v0 = ((m & 8u) << 4) | ((s >> 4) << 3) | (m & 7u);
-                const uint32_t v1 = (((m >> 4) & 8u) << 4) | ((s & 15u) << 3) | ((m >> 4) & 7u);
-                p.out[(2 * i) * K + sid] = live ? (uint8_t)v0 : 0;
-                p.out[(2 * i + 1) * K + sid] = live ? (uint8_t)v1 : 0;
-            }
-        }
+        cp_async_wait<0>();
     }
 }
 
@@ -428,36 +564,49 @@ struct FusedArgs {
     int32_t *status;
 };
 
-__global__ void __launch_bounds__(1024, 1) fused_kernel(const FusedArgs p) {
-    extern __shared__ __align__(16) uint32_t tbl[];
-    load_table(tbl, p.table, p.status);
+template <int R>
+__global__ void __launch_bounds__(kMaxWarps * 32, 1) fused_kernel(const FusedArgs p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
     __syncthreads();
-    const uint8_t *tb = reinterpret_cast<const uint8_t *>(tbl);
-    const int lane = threadIdx.x & 31;
+    const uint8_t *tb = smem;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const uint32_t lane_off = 4u * (lane % kCopies);
+    const uint32_t mask = (uint32_t)(R - 1) << 7;
+    Ring ra, rb;
+    ra.lane_base = ring_area<R>(smem, warp, 2) + 4u * lane;
+    rb.lane_base = ra.lane_base + R * 128u;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int64_t n_groups = (p.K + 31) / 32;
     const int64_t n_tiles = p.N / 16, K = p.K;
-    for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); g < n_groups;
-         g += warps) {
+    for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; g < n_groups; g += warps) {
         const int64_t sid = g * 32 + lane;
         const bool active = sid < K;
         Chain ca, cb;
         chain_idle(ca, p.a_comp);
         chain_idle(cb, p.b_comp);
-        bool ok = false;
+        int32_t ga = 0, gb = 0;
         if (active) {
-            const bool oka = chain_init(ca, p.a_comp, p.a_bytes, p.a_off, p.a_st, p.a_part, sid,
-                                        lane_off, p.status);
-            const bool okb = chain_init(cb, p.b_comp, p.b_bytes, p.b_off, p.b_st, p.b_part, sid,
-                                        lane_off, p.status);
-            ok = oka && okb;
+            ga = chain_init(ca, p.a_comp, p.a_bytes, p.a_off, p.a_st, p.a_part, sid, lane_off,
+                            p.status);
+            gb = chain_init(cb, p.b_comp, p.b_bytes, p.b_off, p.b_st, p.b_part, sid, lane_off,
+                            p.status);
         }
-        const bool live = active && ok;
+        const bool live = active && ga > 0 && gb > 0;
+        if (!live) {
+            chain_idle(ca, p.a_comp);
+            chain_idle(cb, p.b_comp);
+        }
+        ring_reset<R>(ra, __reduce_max_sync(0xffffffffu, live ? ga : 0));
+        ring_reset<R>(rb, __reduce_max_sync(0xffffffffu, live ? gb : 0));
         uint2 sa_n = make_uint2(0, 0), sb_n = make_uint2(0, 0);
         if (live && n_tiles > 0) {
             sa_n = ld_stream_v2(p.a_sm + sid * 8);
             sb_n = ld_stream_v2(p.b_sm + sid * 8);
+            for (int64_t t = 1; t < 4 && t < n_tiles; t++) {
+                prefetch_l2(p.a_sm + (t * K + sid) * 8);
+                prefetch_l2(p.b_sm + (t * K + sid) * 8);
+            }
         }
         for (int64_t t = 0; t < n_tiles; t++) {
             const uint2 sa = sa_n, sb = sb_n;
@@ -465,13 +614,27 @@ __global__ void __launch_bounds__(1024, 1) fused_kernel(const FusedArgs p) {
                 sa_n = ld_stream_v2(p.a_sm + ((t + 1) * K + sid) * 8);
                 sb_n = ld_stream_v2(p.b_sm + ((t + 1) * K + sid) * 8);
             }
-            chain_prefetch(ca);
-            chain_prefetch(cb);
+            if (live && t + 4 < n_tiles) {
+                prefetch_l2(p.a_sm + ((t + 4) * K + sid) * 8);
+                prefetch_l2(p.b_sm + ((t + 4) * K + sid) * 8);
+            }
+            const int32_t need_a = ring_fill<R>(ra, ca, live);
+            const int32_t need_b = ring_fill<R>(rb, cb, live);
+            cp_async_commit();
+            cp_async_wait<kRingLag>();
             uint32_t ea[kTablePairs], eb[kTablePairs];
+            if (need_a >= ra.done[kRingLag] && need_b >= rb.done[kRingLag]) {
 #pragma unroll
-            for (int j = 0; j < kTablePairs; j++) {
-                ea[j] = chain_step(ca, tb);
-                eb[j] = chain_step(cb, tb);
+                for (int j = 0; j < kTablePairs; j++) {
+                    ea[j] = chain_step_ring(ca, tb, ra.lane_base, mask);
+                    eb[j] = chain_step_ring(cb, tb, rb.lane_base, mask);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++) {
+                    ea[j] = chain_step_global(ca, tb);
+                    eb[j] = chain_step_global(cb, tb);
+                }
             }
             const uint32_t SA0 = gather_syms(ea[0], ea[1], ea[2], ea[3]);
             const uint32_t SA1 = gather_syms(ea[4], ea[5], ea[6], ea[7]);
@@ -486,6 +649,7 @@ __global__ void __launch_bounds__(1024, 1) fused_kernel(const FusedArgs p) {
             if (!live) o = make_uint4(0, 0, 0, 0);
             if (active) st_stream_v4(p.out + (t * K + sid) * 16, o);
         }
+        cp_async_wait<0>();
     }
 }
 
@@ -512,12 +676,6 @@ int device_setup(int *sms) {
         cudaError_t e = cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev);
         if (e != cudaSuccess)
             return fail(TANS_B200_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
-        const int smem = kL * kCopies * 4;
-        e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e == cudaSuccess)
-            e = cudaFuncSetAttribute(fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-        if (e != cudaSuccess)
-            return fail(TANS_B200_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
         g_attr_set[dev] = true;
     }
     *sms = g_sms[dev];
@@ -531,6 +689,35 @@ int launch_status(const char *what) {
 }
 
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+constexpr int kSmemMax = 227 * 1024;
+
+// Ring depth by stream length: lanes of a warp drift apart by roughly
+// 0.3 * sqrt(pairs) rows over a stream; the ring must cover that spread plus
+// the look-ahead (rows outside it fall back to global refills, still exact).
+int ring_rows(int64_t pairs) { return pairs <= 4096 ? 32 : (pairs <= 16384 ? 64 : 128); }
+
+template <typename Kernel>
+int set_smem(Kernel k, int bytes) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e != cudaSuccess)
+        return fail(TANS_B200_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    return TANS_B200_OK;
+}
+
+template <int R, typename Args, typename Kernel>
+int launch_ring_kernel(Kernel kernel, const Args &args, int chains, int64_t n_streams, int sms,
+                       cudaStream_t stream, const char *name) {
+    const int per_warp = chains * R * 128;
+    int max_w = (kSmemMax - kTableBytes - R * 128) / per_warp;
+    if (max_w > kMaxWarps) max_w = kMaxWarps;
+    const Geometry geo = balance((n_streams + 31) / 32, sms, max_w);
+    const int smem = kTableBytes + R * 128 + geo.warps_per_cta * per_warp;
+    int rc = set_smem(kernel, smem);
+    if (rc) return rc;
+    kernel<<<geo.grid, geo.warps_per_cta * 32, smem, stream>>>(args);
+    return launch_status(name);
+}
 
 int stream_grid(int64_t n_vec, int sms) {
     const int64_t want = (n_vec + (int64_t)kStreamThreads * kStreamUnroll - 1) /
@@ -615,13 +802,15 @@ extern "C" int tans_b200_decode(const uint8_t *compressed, int64_t compressed_by
     int sms;
     int rc = device_setup(&sms);
     if (rc) return rc;
-    const int64_t n_groups = (n_streams + 31) / 32;
-    const Geometry geo = balance(n_groups, sms, 32);
     DecodeArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets,
                     states, partial, sign_mantissa, decode_table, out, n_streams,
                     n_fp8_per_stream, status};
-    decode_kernel<<<geo.grid, geo.warps_per_cta * 32, kL * kCopies * 4, (cudaStream_t)stream>>>(args);
-    return launch_status("decode_kernel");
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (ring_rows(n_fp8_per_stream / 2)) {
+        case 32: return launch_ring_kernel<32>(decode_kernel<32>, args, 1, n_streams, sms, st, "decode_kernel");
+        case 64: return launch_ring_kernel<64>(decode_kernel<64>, args, 1, n_streams, sms, st, "decode_kernel");
+        default: return launch_ring_kernel<128>(decode_kernel<128>, args, 1, n_streams, sms, st, "decode_kernel");
+    }
 }
 
 extern "C" int tans_b200_fp8_vecadd_fused(
@@ -651,13 +840,15 @@ extern "C" int tans_b200_fp8_vecadd_fused(
     int sms;
     int rc = device_setup(&sms);
     if (rc) return rc;
-    const int64_t n_groups = (n_streams + 31) / 32;
-    const Geometry geo = balance(n_groups, sms, 32);
     FusedArgs args{reinterpret_cast<const uint32_t *>(a_compressed),
                    reinterpret_cast<const uint32_t *>(b_compressed),
                    a_compressed_bytes, b_compressed_bytes, a_offsets, b_offsets, a_states,
                    b_states, a_partial, b_partial, a_sm, b_sm, decode_table, out, n_streams,
                    n_fp8_per_stream, status};
-    fused_kernel<<<geo.grid, geo.warps_per_cta * 32, kL * kCopies * 4, (cudaStream_t)stream>>>(args);
-    return launch_status("fused_kernel");
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (ring_rows(n_fp8_per_stream / 2)) {
+        case 32: return launch_ring_kernel<32>(fused_kernel<32>, args, 2, n_streams, sms, st, "fused_kernel");
+        case 64: return launch_ring_kernel<64>(fused_kernel<64>, args, 2, n_streams, sms, st, "fused_kernel");
+        default: return launch_ring_kernel<128>(fused_kernel<128>, args, 2, n_streams, sms, st, "fused_kernel");
+    }
 }

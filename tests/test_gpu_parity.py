@@ -241,3 +241,39 @@ def test_fused_flags_bad_metadata_without_fault(cuda):
     good = untile(out, 256, 64)[:128]
     raw = fp8_vecadd_raw(a.flatten().to(cuda), b.flatten().to(cuda)).reshape(256, 64)
     assert torch.equal(good, raw[:128])
+
+
+def skewed_fp8(K, N, seed):
+    """Even streams: one repeated byte (few bits per pair); odd streams:
+    exponents uniform over all 16 values (rare pairs cost up to 12 bits).
+    Lanes of a warp then drift far apart in their slab rows, which forces the
+    kernels' global-refill fallback."""
+    g = torch.Generator().manual_seed(seed)
+    x = random_fp8_bytes(K * N, device="cpu", generator=g,
+                         exp_probs=tuple([1.0] * 16)).reshape(K, N)
+    x[0::2] = 0x68  # exponent 13, mantissa 0
+    return x
+
+
+@pytest.mark.parametrize("N", [4096, 32768, 65536])
+def test_fused_skewed_streams_fallback(cuda, N):
+    K = 96
+    a = skewed_fp8(K, N, 1)
+    b = skewed_fp8(K, N, 2)
+    ea = tans_codec.encode(a, QWEN, tile=8)
+    eb = tans_codec.encode(b, QWEN, tile=8)
+    tbl = tans_codec.build_decode_table(ea[6].numpy(), ea[5].numpy())
+    args = (ea[0], ea[2], ea[1], ea[3], ea[4], eb[0], eb[2], eb[1], eb[3], eb[4], tbl)
+    out = fp8_vecadd_fused_tans(*[t.to(cuda) for t in args], N)
+    raw = fp8_vecadd_raw(a.flatten().to(cuda), b.flatten().to(cuda)).reshape(K, N)
+    assert torch.equal(untile(out, K, N), raw)
+
+
+@pytest.mark.parametrize("N", [4096, 65536])
+def test_decode_skewed_streams_fallback(cuda, N):
+    K = 96
+    x = skewed_fp8(K, N, 3)
+    comp, st, off, part, sm, pf, sp = tans_codec.encode(x, QWEN)
+    out = gpu_tans_decode(comp.to(cuda), off.to(cuda), st.to(cuda), part.to(cuda),
+                          sm.to(cuda), sp.to(cuda), pf.to(cuda), N)
+    assert torch.equal(out.cpu().t(), x)
