@@ -242,15 +242,41 @@ __device__ __forceinline__ void load_table(uint32_t *tbl, const int32_t *__restr
     if (bad && status) atomicOr(status, TANS_B200_DATA_BAD_TABLE);
 }
 
-// One stream's decoder state.  The bit window is hi:lo (next bits at the top
-// of hi after skipping cnt bits) plus one slab of look-ahead in nx.  `v` is
-// the word offset (row * 128) of the slab that the next advance loads into
-// nx; rows count down from the top of the encoder block, and row r of this
-// lane lives at src[r * 128].
+// Integer constants the kernels receive as parameters.  Their values are
+// fixed (set by the host), but because ptxas cannot see them it must emit
+// IMAD / IMAD.HI for the shifts, adds and moves written with them below.
+// Those run on the FMA pipe, which otherwise idles in this kernel, instead of
+// the ALU pipe that bounds it.
+struct Opq {
+    uint32_t one;    // 1
+    uint32_t p16;    // 2^16: mul.hi(x, p16) = x >> 16
+    uint32_t p31;    // 2^31: mul.hi(x, p31) = x >> 1
+    uint32_t p28;    // 2^28: mul.hi(x, p28) = x >> 4
+    uint32_t x16;    // 16:   x * 16 = x << 4
+    uint32_t x8;     // 8:    x * 8 = x << 3
+    uint32_t step;   // 4 * kCopies (bytes between successive entries of a copy)
+    int32_t back;    // -128: one slab row down, in words
+};
+
+__device__ __forceinline__ uint32_t mul_lo(uint32_t x, uint32_t y) {
+    uint32_t r;
+    asm("mul.lo.u32 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(y));
+    return r;
+}
+__device__ __forceinline__ uint32_t mul_hi(uint32_t x, uint32_t y) {
+    uint32_t r;
+    asm("mul.hi.u32 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(y));
+    return r;
+}
+
+// One stream's decoder state: the bit window hi:lo (next bits at the top of
+// hi after skipping cnt bits) and `v`, the word offset (row * 128) of the
+// slab that the next advance loads into lo.  Rows count down from the top of
+// the encoder block; row r of this lane lives at src[r * 128].
 struct Chain {
     uint32_t addr;  // byte offset of the current entry in this lane's table copy
     uint32_t cnt;   // bits 0-4: bits used in hi; bit 5 flips per exhausted slab
-    uint32_t hi, lo, nx;
+    uint32_t hi, lo;
     int32_t v;
     const uint32_t *src;
 };
@@ -259,7 +285,7 @@ struct Chain {
 __device__ __forceinline__ void chain_idle(Chain &ch, const uint32_t *comp) {
     ch.addr = 0;
     ch.cnt = 0;
-    ch.hi = ch.lo = ch.nx = 0;
+    ch.hi = ch.lo = 0;
     ch.v = -kBlk;
     ch.src = comp;
 }
@@ -293,65 +319,65 @@ __device__ __forceinline__ int32_t chain_init(Chain &ch, const uint32_t *__restr
     ch.src = comp + base / 4 + tid;
     ch.hi = __ldg(ch.src + (G - 1) * kBlk);
     ch.lo = G >= 2 ? __ldg(ch.src + (G - 2) * kBlk) : 0u;
-    ch.nx = G >= 3 ? __ldg(ch.src + (G - 3) * kBlk) : 0u;
-    ch.v = (G - 4) * kBlk;
+    ch.v = (G - 3) * kBlk;
     return G;
 }
 
-// Table lookup plus everything up to the refill decision; both step flavours
-// share it.  Refill itself is branch-free: on a slab advance hi <- lo <- nx
-// and nx is reloaded by a predicated load, so nx is first read one advance
-// later.  Once a chain has run past its block's first row nothing is loaded
-// and nx keeps a stale word; those bits lie beyond the end of the stream and
-// are never consumed.
+// Table lookup and window update shared by both step flavours.  On a slab
+// advance hi <- lo and lo is reloaded by a predicated load; once a chain has
+// run past its block's first row nothing is loaded and lo keeps a stale word,
+// whose bits lie beyond the end of the stream and are never consumed.
 #define TANS_STEP_HEAD                                                            \
+    "mul.hi.u32 f, %5, %8;\n\t"          /* f = e >> 16 */                        \
     "shf.l.wrap.b32 w, %3, %2, %1;\n\t"  /* w = top 32 bits of (hi:lo) << cnt */ \
-    "shf.l.wrap.b32 bits, w, 0, %6;\n\t" /* bits = w >> (32 - nb), 0 if nb=0 */  \
-    "shr.u32 f, %6, 16;\n\t"                                                    \
-    "mad.lo.u32 %0, bits, %8, f;\n\t" /* next entry address */                  \
-    "add.u32 c2, %1, %6;\n\t"         /* bit 5 flips when a slab is used up */  \
+    "shf.l.wrap.b32 bits, w, 0, %5;\n\t" /* bits = w >> (32 - nb), 0 if nb=0 */  \
+    "mad.lo.u32 %0, bits, %9, f;\n\t"    /* next entry address */                \
+    "mad.lo.u32 c2, %5, %7, %1;\n\t"     /* cnt + e: bit 5 flips per slab */     \
     "xor.b32 t, c2, %1;\n\t"                                                    \
     "and.b32 t, t, 32;\n\t"                                                     \
     "setp.ne.u32 pa, t, 0;\n\t"                                                 \
-    "mov.u32 %1, c2;\n\t"                                                       \
-    "@pa mov.u32 %2, %3;\n\t" /* hi <- lo */                                    \
-    "@pa mov.u32 %3, %4;\n\t" /* lo <- nx */
+    "mov.u32 %1, c2;\n\t"
 
 // Refill from global memory (any row, any time).
-__device__ __forceinline__ uint32_t chain_step_global(Chain &ch, const uint8_t *tbl_bytes) {
+__device__ __forceinline__ uint32_t chain_step_global(Chain &ch, const uint8_t *tbl_bytes,
+                                                      const Opq &q) {
     const uint32_t e = *reinterpret_cast<const uint32_t *>(tbl_bytes + ch.addr);
     asm volatile(
         "{\n\t"
         ".reg .u32 w, bits, f, c2, t;\n\t"
         ".reg .pred pa, pl;\n\t"
         ".reg .u64 ga;\n\t" TANS_STEP_HEAD
-        "setp.ge.and.s32 pl, %5, 0, pa;\n\t"
-        "mul.wide.s32 ga, %5, 4;\n\t"
-        "add.u64 ga, ga, %7;\n\t"
-        "@pl ld.global.nc.u32 %4, [ga];\n\t" /* nx <- next slab of this stream */
-        "@pa sub.s32 %5, %5, %9;\n\t"
+        "setp.ge.and.s32 pl, %4, 0, pa;\n\t"
+        "mul.wide.s32 ga, %4, 4;\n\t"
+        "add.u64 ga, ga, %6;\n\t"
+        "@pa mad.lo.u32 %2, %3, %7, 0;\n\t"    /* hi <- lo */
+        "@pl ld.global.nc.u32 %3, [ga];\n\t"   /* lo <- next slab of this stream */
+        "@pa mad.lo.s32 %4, %7, %10, %4;\n\t"  /* one row down */
         "}"
-        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.nx), "+r"(ch.v)
-        : "r"(e), "l"(ch.src), "n"(4 * kCopies), "n"(kBlk));
+        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.v)
+        : "r"(e), "l"(ch.src), "r"(q.one), "r"(q.p16), "r"(q.step), "r"(q.back));
     return e;
 }
 
 // Refill from this warp's shared-memory row ring: the slot of row r for this
 // lane is at ring_lane + (r mod R) * 128, i.e. (v & mask) | ring_lane.
 __device__ __forceinline__ uint32_t chain_step_ring(Chain &ch, const uint8_t *tbl_bytes,
-                                                    uint32_t ring_lane, uint32_t mask) {
+                                                    uint32_t ring_lane, uint32_t mask,
+                                                    const Opq &q) {
     const uint32_t e = *reinterpret_cast<const uint32_t *>(tbl_bytes + ch.addr);
     asm volatile(
         "{\n\t"
         ".reg .u32 w, bits, f, c2, t, sa;\n\t"
         ".reg .pred pa;\n\t" TANS_STEP_HEAD
-        "and.b32 sa, %5, %10;\n\t"
-        "or.b32 sa, sa, %11;\n\t"
-        "@pa ld.shared.u32 %4, [sa];\n\t" /* nx <- next slab of this stream */
-        "@pa sub.s32 %5, %5, %9;\n\t"
+        "and.b32 sa, %4, %11;\n\t"
+        "or.b32 sa, sa, %12;\n\t"
+        "@pa mad.lo.u32 %2, %3, %7, 0;\n\t"    /* hi <- lo */
+        "@pa ld.shared.u32 %3, [sa];\n\t"      /* lo <- next slab of this stream */
+        "@pa mad.lo.s32 %4, %7, %10, %4;\n\t"  /* one row down */
         "}"
-        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.nx), "+r"(ch.v)
-        : "r"(e), "l"(ch.src), "n"(4 * kCopies), "n"(kBlk), "r"(mask), "r"(ring_lane));
+        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.v)
+        : "r"(e), "l"(ch.src), "r"(q.one), "r"(q.p16), "r"(q.step), "r"(q.back), "r"(mask),
+          "r"(ring_lane));
     return e;
 }
 
@@ -370,43 +396,50 @@ __device__ __forceinline__ void cp_async_wait() {
 
 // Row ring of one chain of one warp.  The warp fills whole rows (each lane
 // copies its own column with cp.async, so every row is one coalesced 128-byte
-// read and a lane only ever reads data it copied itself).  Rows are filled
-// from the top down, at most kLookahead rows below the warp's fastest lane
-// and never over a slot whose row the slowest lane still needs.  A tile may
+// read and a lane only ever reads data it copied itself), from the top down,
+// never over a slot whose row the slowest lane still needs.  A tile may
 // refill from the ring only when every row its lanes can reach in that tile
-// belongs to a fill group that has completed (cp.async.wait_group 2, i.e.
-// two tiles old); otherwise that tile refills from global memory.
-constexpr int kLookahead = 9;  // >= 3 tiles x 3 rows per tile
-constexpr int kRingLag = 2;    // completed groups are kRingLag tiles old
+// (at most 3 rows per tile) belongs to a fill group that has completed
+// (cp.async.wait_group kRingLag: groups kRingLag tiles old); otherwise the
+// tile refills from global memory, which is always exact.
+constexpr int kRingLag = 2;
+constexpr int kRingBurst = 12;  // rows filled when a group starts
+constexpr int kRingPerTile = 2; // rows filled per tile after that
 
 struct Ring {
-    uint32_t lane_base;  // shared address of this lane's column, row slot 0
-    int32_t fill;        // next row to fill (warp-uniform)
-    int32_t done[kRingLag + 1];  // lowest filled row after the last kRingLag+1 fills
+    uint32_t lane_base;          // shared address of this lane's column, row slot 0
+    int32_t fill;                // next row to fill (warp-uniform)
+    int32_t done[kRingLag + 1];  // lowest filled row after the last fills
 };
 
 template <int R>
-__device__ __forceinline__ void ring_reset(Ring &rg, int32_t G) {
-    rg.fill = G - 4;
+__device__ __forceinline__ void ring_start(Ring &rg, const Chain &ch, int32_t G, bool live) {
+    rg.fill = G - 3;
 #pragma unroll
-    for (int i = 0; i <= kRingLag; i++) rg.done[i] = INT_MAX;
+    for (int k = 0; k < kRingBurst; k++) {
+        cp_async4(rg.lane_base + ((uint32_t)(rg.fill & (R - 1)) << 7),
+                  ch.src + (int64_t)rg.fill * kBlk, live && rg.fill >= 0);
+        rg.fill -= rg.fill >= 0 ? 1 : 0;
+    }
+    rg.done[0] = rg.fill + 1;
+#pragma unroll
+    for (int i = 1; i <= kRingLag; i++) rg.done[i] = INT_MAX;
 }
 
-// Issue this tile's fills; returns the lowest row a lane may refill from
-// during the tile (rows at or below it need the ring to be complete).
+// This tile's fills; returns the lowest row a lane may refill from during
+// the tile (the fast path needs it at or above done[kRingLag]).
 template <int R>
 __device__ __forceinline__ int32_t ring_fill(Ring &rg, const Chain &ch, bool live) {
     const int32_t row = ch.v >> 7;
     const int32_t r_fast = __reduce_min_sync(0xffffffffu, live ? row : INT_MAX);
     const int32_t r_slow = __reduce_max_sync(0xffffffffu, live ? row : INT_MIN);
-    if (r_fast != INT_MAX) {
-        const int32_t target = max(r_fast - kLookahead, 0);
-        const int32_t lim = r_slow - R;
-        while (rg.fill >= target && rg.fill > lim) {
-            cp_async4(rg.lane_base + ((uint32_t)(rg.fill & (R - 1)) << 7),
-                      ch.src + (int64_t)rg.fill * kBlk, live);
-            rg.fill--;
-        }
+    const int32_t lim = r_slow - R;
+#pragma unroll
+    for (int k = 0; k < kRingPerTile; k++) {
+        const bool go = rg.fill >= 0 && rg.fill > lim;
+        cp_async4(rg.lane_base + ((uint32_t)(rg.fill & (R - 1)) << 7),
+                  ch.src + (int64_t)rg.fill * kBlk, live && go);
+        rg.fill -= go ? 1 : 0;
     }
 #pragma unroll
     for (int i = kRingLag; i > 0; i--) rg.done[i] = rg.done[i - 1];
@@ -424,11 +457,13 @@ __device__ __forceinline__ uint32_t gather_syms(uint32_t e0, uint32_t e1, uint32
 // and four sign/mantissa pairs M (byte k = sm(2k) | sm(2k+1) << 4):
 // even: byte k = element 2k; odd: byte k = element 2k+1.
 // Byte = (sm & 8) << 4 | exp << 3 | (sm & 7)  (csrc/vecadd.cu:37-39).
-__device__ __forceinline__ uint32_t compose_even(uint32_t S, uint32_t M) {
-    return ((M << 4) & 0x80808080u) | ((S >> 1) & 0x78787878u) | (M & 0x07070707u);
+// Shifts go through the FMA pipe (see Opq).
+__device__ __forceinline__ uint32_t compose_even(uint32_t S, uint32_t M, const Opq &q) {
+    return (mul_lo(M, q.x16) & 0x80808080u) | (mul_hi(S, q.p31) & 0x78787878u) |
+           (M & 0x07070707u);
 }
-__device__ __forceinline__ uint32_t compose_odd(uint32_t S, uint32_t M) {
-    return (M & 0x80808080u) | ((S << 3) & 0x78787878u) | ((M >> 4) & 0x07070707u);
+__device__ __forceinline__ uint32_t compose_odd(uint32_t S, uint32_t M, const Opq &q) {
+    return (M & 0x80808080u) | (mul_lo(S, q.x8) & 0x78787878u) | (mul_hi(M, q.p28) & 0x07070707u);
 }
 
 // Persistent-grid geometry: every warp runs `rounds` 32-stream groups.
@@ -475,6 +510,7 @@ struct DecodeArgs {
     uint8_t *out;       // [N][K]
     int64_t K, N;
     int32_t *status;
+    Opq q;
 };
 
 template <int R>
@@ -501,7 +537,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
             G = chain_init(ch, p.comp, p.comp_bytes, p.offsets, p.states, p.partial, sid, lane_off,
                            p.status);
         const bool live = active && G > 0;
-        ring_reset<R>(rg, __reduce_max_sync(0xffffffffu, G));
+        ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, G), live);
+        cp_async_commit();
         // sign/mantissa bytes of the next tile are loaded one tile ahead, the
         // rows three tiles ahead are prefetched into L2
         uint32_t mn[kTablePairs];
@@ -527,10 +564,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
             if (need >= rg.done[kRingLag]) {
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j++)
-                    s[j] = chain_step_ring(ch, tb, rg.lane_base, mask);
+                    s[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
             } else {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++) s[j] = chain_step_global(ch, tb);
+                for (int j = 0; j < kTablePairs; j++) s[j] = chain_step_global(ch, tb, p.q);
             }
             if (active) {
 #pragma unroll
@@ -562,6 +599,7 @@ struct FusedArgs {
     uint8_t *out;                // [N/16][K][16]
     int64_t K, N;
     int32_t *status;
+    Opq q;
 };
 
 template <int R>
@@ -597,8 +635,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) fused_kernel(const FusedArg
             chain_idle(ca, p.a_comp);
             chain_idle(cb, p.b_comp);
         }
-        ring_reset<R>(ra, __reduce_max_sync(0xffffffffu, live ? ga : 0));
-        ring_reset<R>(rb, __reduce_max_sync(0xffffffffu, live ? gb : 0));
+        ring_start<R>(ra, ca, __reduce_max_sync(0xffffffffu, live ? ga : 0), live);
+        ring_start<R>(rb, cb, __reduce_max_sync(0xffffffffu, live ? gb : 0), live);
+        cp_async_commit();
         uint2 sa_n = make_uint2(0, 0), sb_n = make_uint2(0, 0);
         if (live && n_tiles > 0) {
             sa_n = ld_stream_v2(p.a_sm + sid * 8);
@@ -626,24 +665,24 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) fused_kernel(const FusedArg
             if (need_a >= ra.done[kRingLag] && need_b >= rb.done[kRingLag]) {
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j++) {
-                    ea[j] = chain_step_ring(ca, tb, ra.lane_base, mask);
-                    eb[j] = chain_step_ring(cb, tb, rb.lane_base, mask);
+                    ea[j] = chain_step_ring(ca, tb, ra.lane_base, mask, p.q);
+                    eb[j] = chain_step_ring(cb, tb, rb.lane_base, mask, p.q);
                 }
             } else {
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j++) {
-                    ea[j] = chain_step_global(ca, tb);
-                    eb[j] = chain_step_global(cb, tb);
+                    ea[j] = chain_step_global(ca, tb, p.q);
+                    eb[j] = chain_step_global(cb, tb, p.q);
                 }
             }
             const uint32_t SA0 = gather_syms(ea[0], ea[1], ea[2], ea[3]);
             const uint32_t SA1 = gather_syms(ea[4], ea[5], ea[6], ea[7]);
             const uint32_t SB0 = gather_syms(eb[0], eb[1], eb[2], eb[3]);
             const uint32_t SB1 = gather_syms(eb[4], eb[5], eb[6], eb[7]);
-            const uint32_t re0 = add_e4m3x4(compose_even(SA0, sa.x), compose_even(SB0, sb.x));
-            const uint32_t ro0 = add_e4m3x4(compose_odd(SA0, sa.x), compose_odd(SB0, sb.x));
-            const uint32_t re1 = add_e4m3x4(compose_even(SA1, sa.y), compose_even(SB1, sb.y));
-            const uint32_t ro1 = add_e4m3x4(compose_odd(SA1, sa.y), compose_odd(SB1, sb.y));
+            const uint32_t re0 = add_e4m3x4(compose_even(SA0, sa.x, p.q), compose_even(SB0, sb.x, p.q));
+            const uint32_t ro0 = add_e4m3x4(compose_odd(SA0, sa.x, p.q), compose_odd(SB0, sb.x, p.q));
+            const uint32_t re1 = add_e4m3x4(compose_even(SA1, sa.y, p.q), compose_even(SB1, sb.y, p.q));
+            const uint32_t ro1 = add_e4m3x4(compose_odd(SA1, sa.y, p.q), compose_odd(SB1, sb.y, p.q));
             uint4 o = make_uint4(__byte_perm(re0, ro0, 0x5140), __byte_perm(re0, ro0, 0x7362),
                                  __byte_perm(re1, ro1, 0x5140), __byte_perm(re1, ro1, 0x7362));
             if (!live) o = make_uint4(0, 0, 0, 0);
@@ -717,6 +756,19 @@ int launch_ring_kernel(Kernel kernel, const Args &args, int chains, int64_t n_st
     if (rc) return rc;
     kernel<<<geo.grid, geo.warps_per_cta * 32, smem, stream>>>(args);
     return launch_status(name);
+}
+
+Opq make_opq() {
+    Opq q;
+    q.one = 1;
+    q.p16 = 1u << 16;
+    q.p31 = 1u << 31;
+    q.p28 = 1u << 28;
+    q.x16 = 16;
+    q.x8 = 8;
+    q.step = 4 * kCopies;
+    q.back = -kBlk;
+    return q;
 }
 
 int stream_grid(int64_t n_vec, int sms) {
@@ -804,7 +856,7 @@ extern "C" int tans_b200_decode(const uint8_t *compressed, int64_t compressed_by
     if (rc) return rc;
     DecodeArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets,
                     states, partial, sign_mantissa, decode_table, out, n_streams,
-                    n_fp8_per_stream, status};
+                    n_fp8_per_stream, status, make_opq()};
     cudaStream_t st = (cudaStream_t)stream;
     switch (ring_rows(n_fp8_per_stream / 2)) {
         case 32: return launch_ring_kernel<32>(decode_kernel<32>, args, 1, n_streams, sms, st, "decode_kernel");
@@ -844,7 +896,7 @@ extern "C" int tans_b200_fp8_vecadd_fused(
                    reinterpret_cast<const uint32_t *>(b_compressed),
                    a_compressed_bytes, b_compressed_bytes, a_offsets, b_offsets, a_states,
                    b_states, a_partial, b_partial, a_sm, b_sm, decode_table, out, n_streams,
-                   n_fp8_per_stream, status};
+                   n_fp8_per_stream, status, make_opq()};
     cudaStream_t st = (cudaStream_t)stream;
     switch (ring_rows(n_fp8_per_stream / 2)) {
         case 32: return launch_ring_kernel<32>(fused_kernel<32>, args, 2, n_streams, sms, st, "fused_kernel");
