@@ -149,6 +149,31 @@ int tans_b200_fp8_vecadd_fused(
     const int32_t *decode_table, uint8_t *out, int64_t n_streams,
     int64_t n_fp8_per_stream, int32_t *status, void *stream);
 
+/* Allocation-free standalone decode.  No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory (a runtime that
+ * hands the library only buffers carved from a pre-sized pool, or a
+ * host-language binding with no device allocator).  Same inputs, output and
+ * data-status bits as building the table with tans_b200_build_decode_table
+ * and calling tans_b200_decode, but the decode table lives in a fixed
+ * file-scope device array of the library: 16 KiB (4096 int32) per GPU that
+ * loads the library, held until the process exits.  The caller passes only
+ * inputs and outputs (spread[4096] and freqs[n_syms] are device arrays).
+ *   - n_syms must be 1..256 (the table's alphabet); anything larger is
+ *     rejected with TANS_B200_ERR_INVALID.
+ *   - Calls no cudaMalloc/cudaFree and no allocating library routine.
+ *   - The first call on a device resolves the array's device address; make
+ *     that first call outside any stream capture.
+ *   - Every call rewrites the whole table, so nothing is carried over, but
+ *     all calls share the one array: calls whose GPU work overlaps (e.g. on
+ *     two streams) race on it and must be ordered by the caller. */
+int tans_b200_decode_noalloc(const uint8_t *compressed, int64_t compressed_bytes,
+                             const int32_t *offsets, const uint16_t *states,
+                             const uint8_t *partial, const uint8_t *sign_mantissa,
+                             const int32_t *spread, const int32_t *freqs,
+                             int64_t n_syms, uint8_t *out, int64_t n_streams,
+                             int64_t n_fp8_per_stream, int32_t *status,
+                             void *stream);
+
 #ifdef __cplusplus
 }
 #endif

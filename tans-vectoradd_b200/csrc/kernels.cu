@@ -904,3 +904,87 @@ extern "C" int tans_b200_fp8_vecadd_fused(
         default: return launch_ring_kernel<128>(fused_kernel<128>, args, 2, n_streams, sms, st, "fused_kernel");
     }
 }
+
+// ------------------------------------------------------- allocation-free decode
+//
+// tans_b200_decode_noalloc: the standalone decode from spread/freqs for
+// callers that cannot allocate device memory (a runtime that hands the
+// library a fixed set of buffers carved from a pre-sized pool, or a binding
+// from a host language with no device allocator).  The only scratch the path
+// needs, the 4096-entry decode table, lives in the file-scope array below:
+// 16 KiB on every GPU that loads the library, held until the process exits.
+// Each call rewrites the whole table before the decode reads it, so nothing
+// has to start at zero; because every call shares the one array, calls whose
+// GPU work overlaps (on different streams) race on it and must be ordered by
+// the caller.
+namespace {
+
+constexpr int kNoAllocTableEntries = kL;  // the maximum (and only) scratch: one table
+static __device__ __align__(256) int32_t g_noalloc_table[kNoAllocTableEntries];
+int32_t *g_noalloc_table_ptr[kMaxDevices];
+
+// Device address of this device's table, resolved once per device with that
+// device current (the first call on a device does this; make that first call
+// outside any stream capture).
+int noalloc_table(int32_t **ptr) {
+    int dev;
+    int rc = current_device(&dev);
+    if (rc) return rc;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_noalloc_table_ptr[dev]) {
+        void *p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_table);
+        if (e != cudaSuccess || !p)
+            return fail(TANS_B200_ERR_CUDA, "decode_noalloc: cudaGetSymbolAddress: %s",
+                        cudaGetErrorString(e));
+        g_noalloc_table_ptr[dev] = static_cast<int32_t *>(p);
+    }
+    *ptr = g_noalloc_table_ptr[dev];
+    return TANS_B200_OK;
+}
+
+}  // namespace
+
+extern "C" int tans_b200_decode_noalloc(const uint8_t *compressed, int64_t compressed_bytes,
+                                        const int32_t *offsets, const uint16_t *states,
+                                        const uint8_t *partial, const uint8_t *sign_mantissa,
+                                        const int32_t *spread, const int32_t *freqs,
+                                        int64_t n_syms, uint8_t *out, int64_t n_streams,
+                                        int64_t n_fp8_per_stream, int32_t *status, void *stream) {
+    tans_b200::clear_error();
+    if (n_syms <= 0 || n_syms > 256)
+        return fail(TANS_B200_ERR_INVALID,
+                    "decode_noalloc: alphabet of %lld symbols exceeds the scratch table "
+                    "(1..256 symbols, %d entries)",
+                    (long long)n_syms, kNoAllocTableEntries);
+    if (n_fp8_per_stream < 0 || n_fp8_per_stream % 2 != 0)
+        return fail(TANS_B200_ERR_INVALID, "n_fp8_per_stream must be even");
+    if (compressed_bytes < 0 || compressed_bytes % 4 != 0)
+        return fail(TANS_B200_ERR_INVALID, "compressed length must be divisible by 4 bytes");
+    if (n_streams < 0) return fail(TANS_B200_ERR_INVALID, "n_streams must be >= 0");
+    if (n_streams == 0 || n_fp8_per_stream == 0) return TANS_B200_OK;
+    if (!compressed || !offsets || !states || !partial || !sign_mantissa || !spread || !freqs ||
+        !out)
+        return fail(TANS_B200_ERR_INVALID, "decode_noalloc: null pointer");
+    if (!aligned(compressed, 4) || !aligned(offsets, 4) || !aligned(states, 2) ||
+        !aligned(spread, 4) || !aligned(freqs, 4))
+        return fail(TANS_B200_ERR_INVALID, "decode_noalloc: misaligned input");
+    int sms;
+    int rc = device_setup(&sms);
+    if (rc) return rc;
+    int32_t *table = nullptr;
+    rc = noalloc_table(&table);
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    build_table_kernel<<<1, 1024, 0, st>>>(spread, freqs, (int)n_syms, table, status);
+    rc = launch_status("build_table_kernel");
+    if (rc) return rc;
+    DecodeArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets,
+                    states, partial, sign_mantissa, table, out, n_streams,
+                    n_fp8_per_stream, status, make_opq()};
+    switch (ring_rows(n_fp8_per_stream / 2)) {
+        case 32: return launch_ring_kernel<32>(decode_kernel<32>, args, 1, n_streams, sms, st, "decode_kernel");
+        case 64: return launch_ring_kernel<64>(decode_kernel<64>, args, 1, n_streams, sms, st, "decode_kernel");
+        default: return launch_ring_kernel<128>(decode_kernel<128>, args, 1, n_streams, sms, st, "decode_kernel");
+    }
+}
