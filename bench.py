@@ -52,6 +52,12 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--out", default=None, help="also append the JSON line(s) to this file")
+    ap.add_argument("--workload", choices=["vecadd", "decode", "gemv", "stack"],
+                    default="vecadd", help="vecadd (cfg1, headline), decode (cfg2), "
+                    "gemv (cfg3), stack (cfg4: 40-layer row-sharded GEMV + all-gather)")
+    ap.add_argument("--decode-log2", type=int, default=32, help="log2 fp8 elements (decode)")
+    ap.add_argument("--layers", type=int, default=40, help="layers of the GEMV stack")
+    ap.add_argument("--batch", type=int, default=8, help="GEMV batch (1..8)")
     return ap.parse_args()
 
 
@@ -281,6 +287,162 @@ def emit(line, args):
             f.write(s + "\n")
 
 
+# -------------------------------------------------------------- other configs
+
+def encode_chunked(n: int, N: int, seed: int, dev, chunk_log2: int = 28):
+    """cfg2 input: n e4m3 bytes of N(0,1)*448/absmax (generated on the GPU,
+    seeded), encoded in chunks of whole encoder blocks with one table (from
+    the first chunk's exponent histogram, empty bins weighted 1); offsets of
+    later chunks are rebased.  Returns host tensors for tans_b200_decode and
+    the raw bytes on the device (for the round-trip check)."""
+    from rans_vectoradd import tans_codec
+    from rans_vectoradd.data import exponent_histogram
+    g = torch.Generator(device=dev).manual_seed(seed)
+    chunk = min(n, 1 << chunk_log2)
+    parts, raw = [], torch.empty(n, dtype=torch.uint8, device=dev)
+    hist = None
+    for off in range(0, n, chunk):
+        v = torch.randn(chunk, device=dev, generator=g)
+        raw[off:off + chunk] = (v * (448.0 / v.abs().max())).to(torch.float8_e4m3fn).view(torch.uint8)
+        host = raw[off:off + chunk].cpu()
+        if hist is None:
+            hist = exponent_histogram(host).clamp_min(1).double()
+        parts.append(tans_codec.encode(host.view(chunk // N, N), hist, tile=0))
+    comp, offs, states, part, sm = [], [], [], [], []
+    base = 0
+    for e in parts:
+        comp.append(e[0]); states.append(e[1]); part.append(e[3]); sm.append(e[4])
+        o = e[2].to(torch.int64) + base
+        offs.append(o[:-1] if e is not parts[-1] else o)
+        base += e[0].numel()
+    K = n // N
+    sm_all = torch.cat([s_.view(N // 2, -1) for s_ in sm], dim=1).contiguous()
+    table = tans_codec.build_decode_table(parts[0][6].numpy(), parts[0][5].numpy())
+    assert base < 2 ** 31, "compressed size exceeds the format's int32 offsets"
+    return (torch.cat(comp), torch.cat(offs).to(torch.int32), torch.cat(states), torch.cat(part),
+            sm_all, table, K, raw)
+
+
+def run_decode(args, dev, barrier):
+    """cfg2: standalone decode of 2^decode_log2 e4m3 bytes to [N][K] in HBM."""
+    from rans_vectoradd import _C
+    from rans_vectoradd._lib import LIB, check
+    n = 1 << args.decode_log2
+    N = args.n_fp8
+    comp, off, st, part, sm, tbl, K, raw = encode_chunked(n, N, 0, dev)
+    d = [t.to(dev) for t in (comp, off, st, part, sm, tbl)]
+    out = torch.empty((N, K), dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        check(LIB.tans_b200_decode(d[0].data_ptr(), d[0].numel(), d[1].data_ptr(),
+                                   d[2].data_ptr(), d[3].data_ptr(), d[4].data_ptr(),
+                                   d[5].data_ptr(), out.data_ptr(), K, N,
+                                   _C._status(dev).data_ptr(), stream.cuda_stream))
+    step()
+    ok = bool(torch.equal(out.t(), raw.view(K, N))) and _C.data_status(dev) == 0
+    ms = timed(step, args.steps, args.warmup, stream, barrier) / args.steps
+    alg = sum(t.numel() * t.element_size() for t in (comp, off, st, part, sm)) + n
+    peak, kind = measured_peak()
+    emit({"workload": "decode (cfg2)", "elements": n, "n_fp8_per_stream": N, "streams": K,
+          "ms": round(ms, 4), "output_gbs": round(n / (ms / 1e3) / 1e9, 2),
+          "hbm_frac_algorithmic": round(alg / (ms / 1e3) / 1e9 / peak, 4),
+          "algorithmic_bytes": alg, "bits_per_fp8": round((alg - n) * 8 / n, 4),
+          "bit_exact_round_trip": ok, "peak_source": kind}, args)
+
+
+def make_gemv_weight(R, C, seed, dev, col_splits):
+    from rans_vectoradd import tans_gemv
+    g = torch.Generator(device=dev).manual_seed(seed)
+    w = torch.randn(R, C, device=dev, generator=g) * 0.02
+    w8, s = tans_gemv.quantize_rows(w)
+    return tans_gemv.encode_weight(w8.cpu(), s.cpu(), col_splits=col_splits).to(dev), w8, s
+
+
+def run_gemv(args, dev, barrier):
+    """cfg3: W [17408 x 5120] (and [5120 x 17408], 4 column slices), x bf16
+    batch 1 and 8; rel err vs decode-then-dense fp32; effective GB/s."""
+    from rans_vectoradd import tans_gemv
+    peak, kind = measured_peak()
+    stream = torch.cuda.current_stream(dev)
+    for (R, C, KS, seed) in ((17408, 5120, None, 0), (5120, 17408, None, 1)):
+        enc, w8, s = make_gemv_weight(R, C, seed, dev, KS)
+        for B in (1, 8):
+            g = torch.Generator(device=dev).manual_seed(2)
+            x = torch.randn(B, C, device=dev, generator=g).to(torch.bfloat16)
+            y = torch.empty((B, R), dtype=torch.bfloat16, device=dev)
+            KS = enc.col_splits
+            part = torch.empty((KS, B, R), dtype=torch.float32, device=dev) if KS > 1 else None
+            tans_gemv.gemv(enc, x, y, part)
+            err = tans_gemv.rel_err(y, tans_gemv.reference_gemv(w8, s, x))
+            ms = timed(lambda: tans_gemv.gemv(enc, x, y, part), args.steps * 10, args.warmup,
+                       stream, barrier) / (args.steps * 10)
+            alg = enc.stream_bytes() + 4 * R + 2 * B * C + 2 * B * R
+            emit({"workload": "gemv (cfg3)", "rows": R, "cols": C, "batch": B, "col_splits": KS,
+                  "us": round(ms * 1e3, 2),
+                  "effective_gbs": round(R * C / (ms / 1e3) / 1e9, 2),
+                  "hbm_frac_algorithmic": round(alg / (ms / 1e3) / 1e9 / peak, 4),
+                  "rel_err": err, "bits_per_fp8": round(enc.stream_bytes() * 8 / (R * C), 4),
+                  "peak_source": kind}, args)
+
+
+def run_stack(args, ws, rank, dev, barrier):
+    """cfg4: `layers` x (up [17408 x 5120] + down [5120 x 17408]) e4m3 GEMVs,
+    rows sharded over the ranks, NCCL all-gather of each y; one step = one
+    forward through the stack at batch `batch`."""
+    import torch.distributed as dist
+    from rans_vectoradd import tans_gemv
+    H, F, B = 5120, 17408, args.batch
+    assert F % (16 * ws) == 0 and H % (16 * ws) == 0
+    fr, hr = F // ws, H // ws
+    t0 = time.perf_counter()
+    ups, downs = [], []
+    for layer in range(args.layers):
+        # each rank builds only its row shard of each layer's matrices
+        ups.append(make_gemv_weight(fr, H, 1000 * layer + rank, dev, None)[0])
+        downs.append(make_gemv_weight(hr, F, 1000 * layer + 500 + rank, dev, None)[0])
+    setup = time.perf_counter() - t0
+    x0 = torch.randn(B, H, device=dev, generator=torch.Generator(device=dev).manual_seed(7))
+    x0 = x0.to(torch.bfloat16)
+    yf = torch.empty((B, fr), dtype=torch.bfloat16, device=dev)
+    yh = torch.empty((B, hr), dtype=torch.bfloat16, device=dev)
+    gf = torch.empty((ws, B, fr), dtype=torch.bfloat16, device=dev)
+    gh = torch.empty((ws, B, hr), dtype=torch.bfloat16, device=dev)
+    pu = torch.empty((ups[0].col_splits, B, fr), dtype=torch.float32, device=dev)
+    pd = torch.empty((downs[0].col_splits, B, hr), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def gather(y, g_, full):
+        if ws == 1:
+            return y
+        dist.all_gather_into_tensor(g_, y)
+        return g_.permute(1, 0, 2).reshape(B, full)
+
+    def forward():
+        x = x0
+        for up, down in zip(ups, downs):
+            tans_gemv.gemv(up, x, yf, pu if up.col_splits > 1 else None)
+            h = gather(yf, gf, F)
+            tans_gemv.gemv(down, h, yh, pd if down.col_splits > 1 else None)
+            x = gather(yh, gh, H)
+        return x
+
+    ms = max_over_ranks(timed(forward, args.steps, args.warmup, stream, barrier), ws, dev)
+    per = ms / args.steps
+    wbytes = args.layers * 2 * F * H  # uncompressed e4m3 weight bytes, whole job
+    local = sum(u.stream_bytes() + d.stream_bytes() for u, d in zip(ups, downs))
+    alg = sum_over_ranks(local, ws, dev)
+    peak, kind = measured_peak()
+    if rank == 0:
+        emit({"workload": "gemv stack (cfg4)", "n_gpus": ws, "layers": args.layers, "batch": B,
+              "ms_per_forward": round(per, 4),
+              "effective_gbs": round(wbytes / (per / 1e3) / 1e9, 2),
+              "compressed_gb": round(alg / 1e9, 3),
+              "hbm_frac_per_gpu": round(alg / ws / (per / 1e3) / 1e9 / peak, 4),
+              "setup_s": round(setup, 1), "peak_source": kind,
+              "collective": "NCCL all_gather_into_tensor of each bf16 y shard"}, args)
+
+
 # ------------------------------------------------------------------- main
 
 def main():
@@ -302,6 +464,17 @@ def main():
 
     import rans_vectoradd as rv
     from rans_vectoradd import _C
+
+    if args.workload != "vecadd":
+        if args.workload == "stack":
+            run_stack(args, ws, rank, dev, barrier)
+        elif rank == 0 and ws == 1:
+            run_decode(args, dev, barrier) if args.workload == "decode" else run_gemv(args, dev, barrier)
+        if ws > 1:
+            import torch.distributed as dist
+            dist.barrier(device_ids=[local])
+            dist.destroy_process_group()
+        return
 
     n = 1 << args.elems_log2
     N = args.n_fp8

@@ -149,6 +149,24 @@ int tans_b200_fp8_vecadd_fused(
     const int32_t *decode_table, uint8_t *out, int64_t n_streams,
     int64_t n_fp8_per_stream, int32_t *status, void *stream);
 
+/* Fused tANS-decode GEMV (no counterpart in the reference; the BASELINE
+ * configuration cfg3/cfg4):
+ *   y[b][r] = bf16(scale[r] * sum_c e4m3(W[r][c]) * x[b][c]), fp32 accumulate,
+ * W rows x cols e4m3 stored as tANS streams in the GEMV stream order
+ * (rans_vectoradd.tans_gemv.encode_weight): K = rows*4*col_splits streams of
+ * cols/col_splits/4 fp8, sign/mantissa tiled [N/16][K][8].  x: bf16
+ * [batch][cols], batch 1..8; y: bf16 [batch][rows].  rows % 16 == 0,
+ * cols % (64*col_splits) == 0.  With col_splits > 1 the column slices are
+ * reduced through `partials` (caller-owned f32 [col_splits][batch][rows]),
+ * deterministically. */
+int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_bytes,
+                   const int32_t *offsets, const uint16_t *states,
+                   const uint8_t *partial, const uint8_t *sign_mantissa,
+                   const int32_t *decode_table, const float *scale,
+                   const uint16_t *x, uint16_t *y, float *partials, int64_t rows,
+                   int64_t cols, int64_t batch, int64_t col_splits,
+                   int32_t *status, void *stream);
+
 /* Allocation-free standalone decode.  No counterpart in the reference: it
  * exists for callers that cannot allocate device memory (a runtime that
  * hands the library only buffers carved from a pre-sized pool, or a

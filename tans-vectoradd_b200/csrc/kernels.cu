@@ -39,6 +39,8 @@
 
 #include "../../include/tans_b200.h"
 
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -692,6 +694,215 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) fused_kernel(const FusedArg
     }
 }
 
+// ------------------------------------------------------------------ GEMV
+//
+// y[b][r] = bf16(scale[r] * sum_c e4m3(W[r][c]) * x[b][c]), fp32 accumulate,
+// with W stored as tANS streams (no counterpart in the reference).
+//
+// Stream format (built by rans_vectoradd.tans_gemv.encode_weight): rows are
+// taken 16 at a time (row group w) and columns in KS slices of CS = C/KS;
+// within a slice, 16-column chunk j.  Lane l of a warp (g = l/4, t = l%4)
+// owns two streams, chain 0 for row 16w+g and chain 1 for row 16w+g+8, each
+// holding columns 16j+2t, 16j+2t+1, 16j+8+2t, 16j+9+2t of every chunk, in
+// that order: exactly the A fragment of mma.m16n8k16 (rows g, g+8; k = 2t..,
+// 2t+8..).  Stream id = ((w*KS + k)*2 + chain)*32 + l, so each chain of a
+// warp is 32 consecutive streams of one encoder block.  A pair symbol of a
+// stream is therefore one f16x2 fragment register after a single
+// cvt.rn.f16x2.e4m3x2, and one mma.sync per chunk does 16 rows x 8 batch x
+// 16 columns.  x (batch <= 8) sits in shared memory as f16 with a row pitch
+// of CS + 8 halves, which puts the B-fragment words of the 32 lanes in 32
+// different banks.  The work is the tANS decode (as in the vecadd kernel);
+// the tensor pipe only replaces 8 x 16 scalar FMAs per chunk.
+
+constexpr int kGemvMaxBatch = 8;
+
+struct GemvArgs {
+    const uint32_t *comp;
+    int64_t comp_bytes;
+    const int32_t *offsets;
+    const uint16_t *states;
+    const uint8_t *partial;
+    const uint8_t *sm;        // [N/16][K][8]
+    const int32_t *table;
+    const float *scale;       // [R]
+    const uint16_t *x;        // bf16 [B][C]
+    uint16_t *y;              // bf16 [B][R]   (KS == 1)
+    float *part;              // f32 [KS][B][R] (KS > 1)
+    int64_t R, C, B, KS;
+    int32_t *status;
+    Opq q;
+};
+
+__device__ __forceinline__ uint32_t cvt_f16x2_e4m3x2(uint32_t v16) {
+    uint32_t r;
+    asm("{\n\t.reg .b16 h;\n\tcvt.u16.u32 h, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, h;\n\t}"
+        : "=r"(r)
+        : "r"(v16));
+    return r;
+}
+
+__device__ __forceinline__ void mma_16x8x16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                            uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+        "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Natural-order e4m3 words of four pairs: lo = pairs 0,1 (bytes e0 e1 e0 e1),
+// hi = pairs 2,3.
+__device__ __forceinline__ void compose_pairs(uint32_t S, uint32_t M, const Opq &q, uint32_t &lo,
+                                              uint32_t &hi) {
+    const uint32_t ev = compose_even(S, M, q), od = compose_odd(S, M, q);
+    lo = __byte_perm(ev, od, 0x5140);
+    hi = __byte_perm(ev, od, 0x7362);
+}
+
+constexpr int kGemvMaxWarps = 20;
+
+template <int R>
+__global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvArgs p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
+    const int64_t CS = p.C / p.KS;
+    const int k = blockIdx.y;
+    const int64_t pitch = CS + 8;  // halves
+    uint16_t *xs = reinterpret_cast<uint16_t *>(smem + kTableBytes);
+    // x slice -> f16 in shared memory (rows >= B are zero)
+    for (int64_t i = threadIdx.x; i < kGemvMaxBatch * CS; i += blockDim.x) {
+        const int64_t b = i / CS, c = i % CS;
+        float v = 0.f;
+        if (b < p.B) v = __uint_as_float((uint32_t)p.x[b * p.C + k * CS + c] << 16);
+        xs[b * pitch + c] = __half_as_ushort(__float2half_rn(v));
+    }
+    __syncthreads();
+    const uint8_t *tb = smem;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t lane_off = 4u * (lane % kCopies);
+    const uint32_t mask = (uint32_t)(R - 1) << 7;
+    const uint32_t xbytes = ((uint32_t)(kGemvMaxBatch * pitch * 2) + 127u) & ~127u;
+    Ring ra, rb;
+    {
+        const uint32_t bytes = R * 128u;
+        const uint32_t first =
+            (smem_addr(smem) + kTableBytes + xbytes + bytes - 1) & ~(bytes - 1);
+        ra.lane_base = first + (uint32_t)(warp * 2) * bytes + 4u * lane;
+        rb.lane_base = ra.lane_base + bytes;
+    }
+    const int64_t K = p.R * 4 * p.KS;  // streams
+    const int64_t N = CS / 4;          // fp8 per stream
+    const int64_t n_tiles = N / 16;
+    const int64_t groups = p.R / 16;
+    const uint32_t *xw = reinterpret_cast<const uint32_t *>(xs) + g * (pitch / 2) + t;
+    for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; w < groups;
+         w += (int64_t)gridDim.x * (blockDim.x >> 5)) {
+        const int64_t sa_id = ((w * p.KS + k) * 2 + 0) * 32 + lane;
+        const int64_t sb_id = sa_id + 32;
+        Chain ca, cb;
+        const int32_t ga = chain_init(ca, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
+                                      sa_id, lane_off, p.status);
+        const int32_t gb = chain_init(cb, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
+                                      sb_id, lane_off, p.status);
+        const bool live = ga > 0 && gb > 0;
+        if (!live) {
+            chain_idle(ca, p.comp);
+            chain_idle(cb, p.comp);
+        }
+        ring_start<R>(ra, ca, __reduce_max_sync(0xffffffffu, live ? ga : 0), live);
+        ring_start<R>(rb, cb, __reduce_max_sync(0xffffffffu, live ? gb : 0), live);
+        cp_async_commit();
+        float d[4] = {0.f, 0.f, 0.f, 0.f};
+        uint2 sa_n = make_uint2(0, 0), sb_n = make_uint2(0, 0);
+        if (live && n_tiles > 0) {
+            sa_n = ld_stream_v2(p.sm + sa_id * 8);
+            sb_n = ld_stream_v2(p.sm + sb_id * 8);
+        }
+        for (int64_t tt = 0; tt < n_tiles; tt++) {
+            const uint2 sa = sa_n, sb = sb_n;
+            if (live && tt + 1 < n_tiles) {
+                sa_n = ld_stream_v2(p.sm + ((tt + 1) * K + sa_id) * 8);
+                sb_n = ld_stream_v2(p.sm + ((tt + 1) * K + sb_id) * 8);
+            }
+            if (live && tt + 4 < n_tiles) {
+                prefetch_l2(p.sm + ((tt + 4) * K + sa_id) * 8);
+                prefetch_l2(p.sm + ((tt + 4) * K + sb_id) * 8);
+            }
+            const int32_t need_a = ring_fill<R>(ra, ca, live);
+            const int32_t need_b = ring_fill<R>(rb, cb, live);
+            cp_async_commit();
+            cp_async_wait<kRingLag>();
+            uint32_t ea[kTablePairs], eb[kTablePairs];
+            if (need_a >= ra.done[kRingLag] && need_b >= rb.done[kRingLag]) {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++) {
+                    ea[j] = chain_step_ring(ca, tb, ra.lane_base, mask, p.q);
+                    eb[j] = chain_step_ring(cb, tb, rb.lane_base, mask, p.q);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++) {
+                    ea[j] = chain_step_global(ca, tb, p.q);
+                    eb[j] = chain_step_global(cb, tb, p.q);
+                }
+            }
+            uint32_t wa[4], wb[4];
+            compose_pairs(gather_syms(ea[0], ea[1], ea[2], ea[3]), sa.x, p.q, wa[0], wa[1]);
+            compose_pairs(gather_syms(ea[4], ea[5], ea[6], ea[7]), sa.y, p.q, wa[2], wa[3]);
+            compose_pairs(gather_syms(eb[0], eb[1], eb[2], eb[3]), sb.x, p.q, wb[0], wb[1]);
+            compose_pairs(gather_syms(eb[4], eb[5], eb[6], eb[7]), sb.y, p.q, wb[2], wb[3]);
+#pragma unroll
+            for (int j = 0; j < 4; j++) {  // chunk = 16 columns
+                const int64_t col = (tt * 4 + j) * 16;
+                const uint32_t b0 = xw[col / 2], b1 = xw[col / 2 + 4];
+                const uint32_t a0 = cvt_f16x2_e4m3x2(wa[j] & 0xFFFFu);
+                const uint32_t a2 = cvt_f16x2_e4m3x2(wa[j] >> 16);
+                const uint32_t a1 = cvt_f16x2_e4m3x2(wb[j] & 0xFFFFu);
+                const uint32_t a3 = cvt_f16x2_e4m3x2(wb[j] >> 16);
+                mma_16x8x16(d, a0, a1, a2, a3, b0, b1);
+            }
+        }
+        cp_async_wait<0>();
+        const int64_t r0 = w * 16 + g, r1 = r0 + 8;
+        const int64_t b0 = 2 * t, b1 = 2 * t + 1;
+        if (!live) d[0] = d[1] = d[2] = d[3] = 0.f;
+        if (p.KS == 1) {
+            const float s0 = p.scale[r0], s1 = p.scale[r1];
+            if (b0 < p.B) {
+                p.y[b0 * p.R + r0] = __bfloat16_as_ushort(__float2bfloat16_rn(d[0] * s0));
+                p.y[b0 * p.R + r1] = __bfloat16_as_ushort(__float2bfloat16_rn(d[2] * s1));
+            }
+            if (b1 < p.B) {
+                p.y[b1 * p.R + r0] = __bfloat16_as_ushort(__float2bfloat16_rn(d[1] * s0));
+                p.y[b1 * p.R + r1] = __bfloat16_as_ushort(__float2bfloat16_rn(d[3] * s1));
+            }
+        } else {
+            float *pk = p.part + (int64_t)k * p.B * p.R;
+            if (b0 < p.B) {
+                pk[b0 * p.R + r0] = d[0];
+                pk[b0 * p.R + r1] = d[2];
+            }
+            if (b1 < p.B) {
+                pk[b1 * p.R + r0] = d[1];
+                pk[b1 * p.R + r1] = d[3];
+            }
+        }
+    }
+}
+
+// y[b][r] = bf16(scale[r] * sum_k part[k][b][r]) for column-sliced GEMVs.
+__global__ void gemv_reduce_kernel(const float *__restrict__ part, const float *__restrict__ scale,
+                                   uint16_t *__restrict__ y, int64_t R, int64_t B, int64_t KS) {
+    const int64_t n = R * B;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float acc = 0.f;
+        for (int64_t k = 0; k < KS; k++) acc += part[k * n + i];
+        y[i] = __bfloat16_as_ushort(__float2bfloat16_rn(acc * scale[i % R]));
+    }
+}
+
 // ------------------------------------------------------------- host glue
 
 constexpr int kMaxDevices = 64;
@@ -734,7 +945,9 @@ constexpr int kSmemMax = 227 * 1024;
 // Ring depth by stream length: lanes of a warp drift apart by roughly
 // 0.3 * sqrt(pairs) rows over a stream; the ring must cover that spread plus
 // the look-ahead (rows outside it fall back to global refills, still exact).
-int ring_rows(int64_t pairs) { return pairs <= 4096 ? 32 : (pairs <= 16384 ? 64 : 128); }
+int ring_rows(int64_t pairs) {
+    return pairs <= 1024 ? 16 : pairs <= 4096 ? 32 : (pairs <= 16384 ? 64 : 128);
+}
 
 template <typename Kernel>
 int set_smem(Kernel k, int bytes) {
@@ -859,6 +1072,7 @@ extern "C" int tans_b200_decode(const uint8_t *compressed, int64_t compressed_by
                     n_fp8_per_stream, status, make_opq()};
     cudaStream_t st = (cudaStream_t)stream;
     switch (ring_rows(n_fp8_per_stream / 2)) {
+        case 16: return launch_ring_kernel<16>(decode_kernel<16>, args, 1, n_streams, sms, st, "decode_kernel");
         case 32: return launch_ring_kernel<32>(decode_kernel<32>, args, 1, n_streams, sms, st, "decode_kernel");
         case 64: return launch_ring_kernel<64>(decode_kernel<64>, args, 1, n_streams, sms, st, "decode_kernel");
         default: return launch_ring_kernel<128>(decode_kernel<128>, args, 1, n_streams, sms, st, "decode_kernel");
@@ -899,10 +1113,75 @@ extern "C" int tans_b200_fp8_vecadd_fused(
                    n_fp8_per_stream, status, make_opq()};
     cudaStream_t st = (cudaStream_t)stream;
     switch (ring_rows(n_fp8_per_stream / 2)) {
+        case 16: return launch_ring_kernel<16>(fused_kernel<16>, args, 2, n_streams, sms, st, "fused_kernel");
         case 32: return launch_ring_kernel<32>(fused_kernel<32>, args, 2, n_streams, sms, st, "fused_kernel");
         case 64: return launch_ring_kernel<64>(fused_kernel<64>, args, 2, n_streams, sms, st, "fused_kernel");
         default: return launch_ring_kernel<128>(fused_kernel<128>, args, 2, n_streams, sms, st, "fused_kernel");
     }
+}
+
+extern "C" int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_bytes,
+                              const int32_t *offsets, const uint16_t *states,
+                              const uint8_t *partial, const uint8_t *sm,
+                              const int32_t *decode_table, const float *scale,
+                              const uint16_t *x, uint16_t *y, float *partials, int64_t rows,
+                              int64_t cols, int64_t batch, int64_t col_splits, int32_t *status,
+                              void *stream) {
+    tans_b200::clear_error();
+    if (rows <= 0 || rows % 16 != 0) return fail(TANS_B200_ERR_INVALID, "gemv: rows must be a positive multiple of 16");
+    if (col_splits < 1 || cols <= 0 || cols % (64 * col_splits) != 0)
+        return fail(TANS_B200_ERR_INVALID, "gemv: cols must be a positive multiple of 64 * col_splits");
+    if (batch < 1 || batch > kGemvMaxBatch) return fail(TANS_B200_ERR_INVALID, "gemv: batch must be 1..8");
+    if (!compressed || !offsets || !states || !partial || !sm || !decode_table || !scale || !x || !y ||
+        (col_splits > 1 && !partials))
+        return fail(TANS_B200_ERR_INVALID, "gemv: null pointer");
+    if (!aligned(compressed, 4) || !aligned(offsets, 4) || !aligned(states, 2) || !aligned(sm, 8) ||
+        !aligned(decode_table, 4) || !aligned(scale, 4) || !aligned(x, 2) || !aligned(y, 2) ||
+        (partials && !aligned(partials, 4)))
+        return fail(TANS_B200_ERR_INVALID, "gemv: misaligned buffer");
+    if (compressed_bytes < 0 || compressed_bytes % 4 != 0)
+        return fail(TANS_B200_ERR_INVALID, "compressed length must be divisible by 4 bytes");
+    int sms;
+    int rc = device_setup(&sms);
+    if (rc) return rc;
+    const int64_t cs = cols / col_splits;
+    const int rr = ring_rows(cs / 8);
+    const int64_t xbytes = ((kGemvMaxBatch * (cs + 8) * 2) + 127) / 128 * 128;
+    const int64_t fixed = kTableBytes + xbytes + rr * 128;
+    const int64_t per_warp = 2 * rr * 128;
+    int64_t max_w = (kSmemMax - fixed) / per_warp;
+    if (max_w > kGemvMaxWarps) max_w = kGemvMaxWarps;
+    if (max_w < 1)
+        return fail(TANS_B200_ERR_INVALID,
+                    "gemv: a column slice of %lld does not fit in shared memory; use more col_splits",
+                    (long long)cs);
+    const int64_t groups = rows / 16;
+    int64_t gx = sms / col_splits;
+    if (gx < 1) gx = 1;
+    const int64_t rounds = (groups + gx * max_w - 1) / (gx * max_w);
+    const int64_t wpc = (groups + gx * rounds - 1) / (gx * rounds);
+    gx = (groups + wpc * rounds - 1) / (wpc * rounds);
+    const int smem = (int)(fixed + wpc * per_warp);
+    GemvArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets, states,
+                  partial, sm, decode_table, scale, x, y, partials, rows, cols, batch, col_splits,
+                  status, make_opq()};
+    cudaStream_t st = (cudaStream_t)stream;
+    const dim3 grid((unsigned)gx, (unsigned)col_splits);
+    switch (rr) {
+        case 16: rc = set_smem(gemv_kernel<16>, smem); if (!rc) gemv_kernel<16><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
+        case 32: rc = set_smem(gemv_kernel<32>, smem); if (!rc) gemv_kernel<32><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
+        case 64: rc = set_smem(gemv_kernel<64>, smem); if (!rc) gemv_kernel<64><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
+        default: rc = set_smem(gemv_kernel<128>, smem); if (!rc) gemv_kernel<128><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
+    }
+    if (rc) return rc;
+    rc = launch_status("gemv_kernel");
+    if (rc || col_splits == 1) return rc;
+    const int64_t n = rows * batch;
+    const int threads = 256;
+    const int64_t blocks = (n + threads - 1) / threads;
+    gemv_reduce_kernel<<<(unsigned)(blocks < 4 * sms ? blocks : 4 * sms), threads, 0, st>>>(
+        partials, scale, y, rows, batch, col_splits);
+    return launch_status("gemv_reduce_kernel");
 }
 
 // ------------------------------------------------------- allocation-free decode
@@ -983,6 +1262,7 @@ extern "C" int tans_b200_decode_noalloc(const uint8_t *compressed, int64_t compr
                     states, partial, sign_mantissa, table, out, n_streams,
                     n_fp8_per_stream, status, make_opq()};
     switch (ring_rows(n_fp8_per_stream / 2)) {
+        case 16: return launch_ring_kernel<16>(decode_kernel<16>, args, 1, n_streams, sms, st, "decode_kernel");
         case 32: return launch_ring_kernel<32>(decode_kernel<32>, args, 1, n_streams, sms, st, "decode_kernel");
         case 64: return launch_ring_kernel<64>(decode_kernel<64>, args, 1, n_streams, sms, st, "decode_kernel");
         default: return launch_ring_kernel<128>(decode_kernel<128>, args, 1, n_streams, sms, st, "decode_kernel");

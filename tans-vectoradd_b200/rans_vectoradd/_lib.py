@@ -41,6 +41,7 @@ def _load() -> ctypes.CDLL:
         "tans_b200_fp8_vecadd_fused": (i32, [p, i64, p, p, p, p, p, i64, p, p, p, p, p, p,
                                              i64, i64, p, p]),
         "tans_b200_decode_noalloc": (i32, [p, i64, p, p, p, p, p, p, i64, p, i64, i64, p, p]),
+        "tans_b200_gemv": (i32, [p, i64, p, p, p, p, p, p, p, p, p, i64, i64, i64, i64, p, p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

@@ -59,6 +59,11 @@ def build_spread(freqs: np.ndarray) -> np.ndarray:
     f = np.asarray(freqs, dtype=np.int64)
     if int(f.sum()) != L:
         raise AssertionError(f"freqs must sum to {L}")
+    if (f < 0).any():
+        # quantize_freqs can drive a zero-probability symbol to -1 when it has
+        # to remove units (as the reference's does); the reference's spread
+        # then trips its slot assertion
+        raise AssertionError("freqs must be non-negative")
     spread = np.full(L, -1, dtype=np.int32)
     spread[(np.arange(L, dtype=np.int64) * SIGMA) % L] = np.repeat(
         np.arange(f.size, dtype=np.int32), f)

@@ -1,0 +1,147 @@
+"""Fused tANS-decode GEMV: y = bf16(scale * (e4m3 W) @ x^T), fp32 accumulate.
+
+No counterpart in the reference (it is the GEMV configuration of the
+benchmark); it reuses the reference's codec unchanged — same pair symbols,
+table, slab layout and encoder — and only chooses which weight elements form
+each stream:
+
+* W [rows, cols] e4m3 bytes with a per-row fp32 scale (row max -> 448);
+* rows are taken 16 at a time and columns in `col_splits` slices; each
+  16-row group x slice is 64 streams: stream ((w*KS + k)*2 + chain)*32 + lane
+  holds row 16w + lane//4 + 8*chain and, of every 16-column chunk of the
+  slice, columns 2t, 2t+1, 8+2t, 9+2t (t = lane % 4) — the operand layout of
+  a 16x8x16 tensor-core fragment, so the kernel turns each decoded pair
+  straight into a fragment register.
+
+`encode_weight` builds that stream matrix and encodes it with
+`tans_codec.encode(..., tile=8)`; `gemv` runs the sm_100a kernel.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import tans_codec
+from ._C import _req, _same_device, _status, _stream
+from ._lib import LIB, check
+
+
+@dataclass
+class EncodedWeight:
+    compressed: torch.Tensor
+    offsets: torch.Tensor
+    states: torch.Tensor
+    partial: torch.Tensor
+    sm: torch.Tensor
+    table: torch.Tensor
+    scale: torch.Tensor
+    rows: int
+    cols: int
+    col_splits: int
+    pair_freqs: torch.Tensor
+    spread: torch.Tensor
+
+    def to(self, device) -> "EncodedWeight":
+        mv = lambda t: t.to(device)  # noqa: E731
+        return EncodedWeight(mv(self.compressed), mv(self.offsets), mv(self.states),
+                             mv(self.partial), mv(self.sm), mv(self.table), mv(self.scale),
+                             self.rows, self.cols, self.col_splits, self.pair_freqs,
+                             self.spread)
+
+    def stream_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in
+                   (self.compressed, self.offsets, self.states, self.partial, self.sm))
+
+
+def quantize_rows(w: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp32 W -> (e4m3 bytes, per-row fp32 scale) with row max|w| -> 448."""
+    w = w.float()
+    scale = w.abs().amax(dim=1).clamp_min(torch.finfo(torch.float32).tiny) / 448.0
+    w8 = (w / scale[:, None]).to(torch.float8_e4m3fn).view(torch.uint8)
+    return w8, scale
+
+
+def stream_matrix(w8: torch.Tensor, col_splits: int = 1) -> torch.Tensor:
+    """Reorder e4m3 bytes [rows, cols] into the GEMV stream matrix
+    [rows*4*col_splits, cols/col_splits/4] (see module docstring)."""
+    R, C = w8.shape
+    KS = col_splits
+    assert R % 16 == 0 and C % (64 * KS) == 0, "rows % 16 and cols % (64*col_splits) must be 0"
+    CS = C // KS
+    v = w8.reshape(R // 16, 2, 8, KS, CS // 16, 2, 4, 2)   # w c g k j h t e
+    return v.permute(0, 3, 1, 2, 6, 4, 5, 7).reshape(R * 4 * KS, CS // 4).contiguous()
+
+
+def default_col_splits(rows: int, cols: int, sms: int = 148, warps_per_sm: int = 18) -> int:
+    """Column slices giving each SM about `warps_per_sm` warps (one warp per
+    16-row group and slice), keeping a slice a multiple of 64 columns and at
+    least 1024 columns (shorter streams spend more on per-stream setup)."""
+    want = max(1, round(sms * warps_per_sm / max(1, rows // 16)))
+    best = 1
+    for ks in range(1, want + 1):
+        if cols % (64 * ks) == 0 and cols // ks >= 1024:
+            best = ks
+    return best
+
+
+def encode_weight(w8: torch.Tensor, scale: torch.Tensor, exp_freqs=None,
+                  col_splits: int | None = None) -> EncodedWeight:
+    """tANS-encode e4m3 weight bytes for `gemv` (host).  `col_splits`
+    defaults to default_col_splits(rows, cols)."""
+    w8 = w8.detach().to("cpu").contiguous()
+    if col_splits is None:
+        col_splits = default_col_splits(*w8.shape)
+    if exp_freqs is None:
+        # empty exponent bins get weight 1 so every pair keeps a slot (no
+        # zero-probability symbols for the frequency quantiser to misplace)
+        exp_freqs = torch.bincount(((w8.reshape(-1) >> 3) & 15).long(),
+                                   minlength=16).clamp_min(1).double()
+    streams = stream_matrix(w8, col_splits)
+    comp, st, off, part, sm, pf, sp = tans_codec.encode(streams, exp_freqs, tile=8)
+    table = tans_codec.build_decode_table(sp.numpy(), pf.numpy())
+    return EncodedWeight(comp, off, st, part, sm, table,
+                         scale.detach().float().to("cpu").contiguous(), w8.shape[0],
+                         w8.shape[1], col_splits, pf, sp)
+
+
+def gemv(weight: EncodedWeight, x: torch.Tensor, out: torch.Tensor | None = None,
+         partials: torch.Tensor | None = None) -> torch.Tensor:
+    """y [batch, rows] bf16 = scale * W @ x^T for x bf16 [batch, cols], batch 1..8.
+    All of `weight` and x must be CUDA tensors on one device."""
+    _req(x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(),
+         "x must be a contiguous CUDA bfloat16 [batch, cols] tensor")
+    B, C = x.shape
+    _req(C == weight.cols, f"x has {C} columns, the weight {weight.cols}")
+    _req(1 <= B <= 8, "batch must be 1..8")
+    dev = x.device
+    _same_device(dev, weight.compressed, weight.offsets, weight.states, weight.partial,
+                 weight.sm, weight.table, weight.scale)
+    R, KS = weight.rows, weight.col_splits
+    with torch.cuda.device(dev):
+        if out is None:
+            out = torch.empty((B, R), dtype=torch.bfloat16, device=dev)
+        if KS > 1 and partials is None:
+            partials = torch.empty((KS, B, R), dtype=torch.float32, device=dev)
+        check(LIB.tans_b200_gemv(
+            weight.compressed.data_ptr(), weight.compressed.numel(), weight.offsets.data_ptr(),
+            weight.states.data_ptr(), weight.partial.data_ptr(), weight.sm.data_ptr(),
+            weight.table.data_ptr(), weight.scale.data_ptr(), x.data_ptr(), out.data_ptr(),
+            partials.data_ptr() if partials is not None else None, R, C, B, KS,
+            _status(dev).data_ptr(), _stream(dev)))
+    return out
+
+
+def reference_gemv(w8: torch.Tensor, scale: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
+    """Decode-then-dense fp32 reference: bf16((W8.float() * s) @ x.float()^T)."""
+    w = w8.view(torch.float8_e4m3fn).float() * scale.float()[:, None]
+    return (x.float() @ w.t()).to(torch.bfloat16)
+
+
+def rel_err(y: torch.Tensor, y_ref: torch.Tensor) -> float:
+    a, b = y.float(), y_ref.float()
+    return float(torch.linalg.vector_norm(a - b) / torch.linalg.vector_norm(b).clamp_min(1e-30))
+
+
+__all__ = ["EncodedWeight", "quantize_rows", "stream_matrix", "encode_weight", "gemv",
+           "reference_gemv", "rel_err"]

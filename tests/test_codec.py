@@ -194,3 +194,17 @@ def test_encode_tile_assertion():
     fp8 = torch.zeros((4, 20), dtype=torch.uint8)
     with pytest.raises(AssertionError, match="not divisible by tile"):
         tans_codec.encode(fp8, QWEN, tile=8)
+
+
+def test_negative_quantized_freq_fails_like_reference():
+    """Empty exponent bins can make quantize_freqs remove a unit from a
+    zero-probability pair (same algorithm as the reference); the spread then
+    refuses the table, as the reference's assertion does."""
+    probs = torch.tensor([1.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 0.0,
+                          0.0, 0.0, 0.0, 0.0, 0.0, 0.0, 3.0, 5.0], dtype=torch.float64)
+    pf = tans_codec.pair_freqs_from_exponents(probs)
+    if (pf < 0).any():
+        with pytest.raises(AssertionError):
+            tans_codec.build_spread(pf)
+    else:
+        assert pf.sum() == 4096

@@ -1,0 +1,94 @@
+"""Fused decode-GEMV: stream layout (CPU) and the sm_100a kernel against the
+decode-then-dense fp32 reference, relative error <= 1e-3 (GPU)."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from rans_vectoradd import tans_gemv
+
+TOL = 1e-3  # ||y - y_ref||_2 / ||y_ref||_2
+
+
+def make(R, C, seed):
+    g = torch.Generator().manual_seed(seed)
+    w = torch.randn(R, C, generator=g) * 0.02
+    return tans_gemv.quantize_rows(w)
+
+
+def test_stream_matrix_layout():
+    """Element (row, col) lands in the stream/position the kernel expects."""
+    R, C, KS = 32, 256, 2
+    w8 = torch.arange(R * C, dtype=torch.int64).reshape(R, C)  # unique ids
+    sm = tans_gemv.stream_matrix(w8, KS)
+    CS = C // KS
+    for r in (0, 7, 8, 15, 16, 31):
+        for c in (0, 1, 2, 9, 15, 16, 100, 255):
+            w, g, ch = r // 16, r % 8, (r % 16) // 8
+            k, cc = c // CS, c % CS
+            j, rem = cc // 16, cc % 16
+            h, t, e = rem // 8, (rem % 8) // 2, rem % 2
+            sid = ((w * KS + k) * 2 + ch) * 32 + 4 * g + t
+            pos = 4 * j + 2 * h + e
+            assert sm[sid, pos].item() == r * C + c
+
+
+def test_quantize_rows_maps_row_max_to_448():
+    w8, s = make(16, 64, 0)
+    v = w8.view(torch.float8_e4m3fn).float()
+    assert torch.allclose(v.abs().amax(dim=1), torch.full((16,), 448.0))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("R,C,B,KS", [(16, 64, 1, 1), (64, 512, 8, 1), (128, 1024, 3, 2),
+                                      (256, 4352, 8, 4), (1024, 5120, 8, 1)])
+def test_gemv_matches_fp32_reference(cuda, R, C, B, KS):
+    w8, s = make(R, C, R + C)
+    g = torch.Generator().manual_seed(7)
+    x = torch.randn(B, C, generator=g).to(torch.bfloat16)
+    enc = tans_gemv.encode_weight(w8, s, col_splits=KS).to(cuda)
+    y = tans_gemv.gemv(enc, x.to(cuda))
+    ref = tans_gemv.reference_gemv(w8, s, x)
+    err = tans_gemv.rel_err(y.cpu(), ref)
+    assert err <= TOL, err
+
+
+@pytest.mark.gpu
+def test_gemv_cfg3_full_size(cuda):
+    """cfg3: W [17408 x 5120] ~ N(0, 0.02), x bf16 N(0,1), batch 1 and 8."""
+    R, C = 17408, 5120
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(R, C, generator=g) * 0.02
+    w8, s = tans_gemv.quantize_rows(w)
+    enc = tans_gemv.encode_weight(w8, s).to(cuda)
+    for B in (1, 8):
+        x = torch.randn(B, C, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+        y = tans_gemv.gemv(enc, x.to(cuda))
+        ref = tans_gemv.reference_gemv(w8.to(cuda), s.to(cuda), x.to(cuda))
+        assert tans_gemv.rel_err(y, ref) <= TOL
+
+
+@pytest.mark.gpu
+def test_gemv_down_projection_split(cuda):
+    """[5120 x 17408] with 4 column slices (reduced deterministically)."""
+    R, C = 5120, 17408
+    g = torch.Generator().manual_seed(1)
+    w8, s = tans_gemv.quantize_rows(torch.randn(R, C, generator=g) * 0.02)
+    enc = tans_gemv.encode_weight(w8, s, col_splits=4).to(cuda)
+    x = torch.randn(8, C, generator=torch.Generator().manual_seed(3)).to(torch.bfloat16).to(cuda)
+    y1 = tans_gemv.gemv(enc, x)
+    y2 = tans_gemv.gemv(enc, x)
+    assert torch.equal(y1, y2)
+    ref = tans_gemv.reference_gemv(w8.to(cuda), s.to(cuda), x)
+    assert tans_gemv.rel_err(y1, ref) <= TOL
+
+
+def test_gemv_rejects_bad_shapes():
+    from rans_vectoradd._lib import LIB
+    assert LIB.tans_b200_gemv(None, 0, None, None, None, None, None, None, None, None, None,
+                              24, 64, 1, 1, None, None) == 1
+    assert b"multiple of 16" in LIB.tans_b200_last_error()
+    assert LIB.tans_b200_gemv(None, 0, None, None, None, None, None, None, None, None, None,
+                              16, 96, 1, 1, None, None) == 1
+    assert LIB.tans_b200_gemv(None, 0, None, None, None, None, None, None, None, None, None,
+                              16, 64, 9, 1, None, None) == 1
