@@ -427,7 +427,23 @@ def run_stack(args, ws, rank, dev, barrier):
             x = gather(yh, gh, H)
         return x
 
-    ms = max_over_ranks(timed(forward, args.steps, args.warmup, stream, barrier), ws, dev)
+    # the whole forward (80 GEMV launches, their split-K reductions and the
+    # all-gathers) is captured once in a CUDA graph and replayed per step
+    for _ in range(2):
+        forward()
+    torch.cuda.synchronize()
+    barrier()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            forward()
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    ms = max_over_ranks(timed(graph.replay, args.steps, args.warmup, stream, barrier), ws, dev)
+    ms_eager = max_over_ranks(timed(forward, args.steps, 1, stream, barrier), ws, dev)
+    del graph  # release the captured collectives before the process group goes
     per = ms / args.steps
     wbytes = args.layers * 2 * F * H  # uncompressed e4m3 weight bytes, whole job
     local = sum(u.stream_bytes() + d.stream_bytes() for u, d in zip(ups, downs))
@@ -435,7 +451,8 @@ def run_stack(args, ws, rank, dev, barrier):
     peak, kind = measured_peak()
     if rank == 0:
         emit({"workload": "gemv stack (cfg4)", "n_gpus": ws, "layers": args.layers, "batch": B,
-              "ms_per_forward": round(per, 4),
+              "ms_per_forward": round(per, 4), "graph": True,
+              "ms_per_forward_eager": round(ms_eager / args.steps, 4),
               "effective_gbs": round(wbytes / (per / 1e3) / 1e9, 2),
               "compressed_gb": round(alg / 1e9, 3),
               "hbm_frac_per_gpu": round(alg / ws / (per / 1e3) / 1e9 / peak, 4),

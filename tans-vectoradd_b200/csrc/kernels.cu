@@ -423,9 +423,10 @@ __device__ __forceinline__ void ring_start(Ring &rg, const Chain &ch, int32_t G,
                   ch.src + (int64_t)rg.fill * kBlk, live && rg.fill >= 0);
         rg.fill -= rg.fill >= 0 ? 1 : 0;
     }
-    rg.done[0] = rg.fill + 1;
+    // the caller commits and waits for this burst (cp.async.wait_group 0)
+    // before the first tile, so every tile can refill from the ring
 #pragma unroll
-    for (int i = 1; i <= kRingLag; i++) rg.done[i] = INT_MAX;
+    for (int i = 0; i <= kRingLag; i++) rg.done[i] = rg.fill + 1;
 }
 
 // This tile's fills; returns the lowest row a lane may refill from during
@@ -541,6 +542,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
         const bool live = active && G > 0;
         ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, G), live);
         cp_async_commit();
+        cp_async_wait<0>();
         // sign/mantissa bytes of the next tile are loaded one tile ahead, the
         // rows three tiles ahead are prefetched into L2
         uint32_t mn[kTablePairs];
@@ -640,6 +642,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) fused_kernel(const FusedArg
         ring_start<R>(ra, ca, __reduce_max_sync(0xffffffffu, live ? ga : 0), live);
         ring_start<R>(rb, cb, __reduce_max_sync(0xffffffffu, live ? gb : 0), live);
         cp_async_commit();
+        cp_async_wait<0>();
         uint2 sa_n = make_uint2(0, 0), sb_n = make_uint2(0, 0);
         if (live && n_tiles > 0) {
             sa_n = ld_stream_v2(p.a_sm + sid * 8);
@@ -813,6 +816,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
         ring_start<R>(ra, ca, __reduce_max_sync(0xffffffffu, live ? ga : 0), live);
         ring_start<R>(rb, cb, __reduce_max_sync(0xffffffffu, live ? gb : 0), live);
         cp_async_commit();
+        cp_async_wait<0>();
         float d[4] = {0.f, 0.f, 0.f, 0.f};
         uint2 sa_n = make_uint2(0, 0), sb_n = make_uint2(0, 0);
         if (live && n_tiles > 0) {
