@@ -5,7 +5,7 @@
 //   vecadd_raw_kernel    csrc/vecadd.cu:41-73         (uncompressed FP8 add)
 //   build_table_kernel   csrc/tans_decode.cu:23-59    (host table build, per call)
 //   decode_kernel        csrc/tans_decode.cu:125-155  (standalone decode, [N,K] out)
-//   fused_kernel         csrc/vecadd.cu:156-243       (decode A and B + add, tiled out)
+//   fused_split_kernel   csrc/vecadd.cu:156-243       (decode A and B + add, tiled out)
 //
 // Design (B200-first, not a translation of the reference):
 //  * FP8 add: e4m3x2 -> f16x2 (exact), add.rn.f16x2, cvt.rn.satfinite.e4m3x2.
@@ -27,12 +27,13 @@
 //  * The consumed-bit counter is bumped by the whole entry (bits 5-7 are 0),
 //    so its low 5 bits track the position inside the current slab and bit 5
 //    flips exactly when a slab is exhausted: one add and one xor-test per step.
-//  * Three slab registers (hi, lo, next) keep one slab load in flight ahead of
-//    use; each 8-pair tile also prefetches this lane's slab four rows ahead
-//    into L2.
-//  * One thread owns one stream (both inputs A and B in the fused kernel:
-//    two independent dependency chains).  Grids are persistent and balanced
-//    over the SMs: every warp runs the same number of 32-stream groups.
+//  * Slab refills come from a per-warp shared-memory ring of slab rows that
+//    the warp fills ahead of use with cp.async (see Ring); the bit window is
+//    the two registers hi:lo.
+//  * One thread owns one stream.  In the fused kernel a pair of warps owns a
+//    32-stream group, one warp per input, exchanging decoded pair symbols per
+//    tile through shared memory.  Grids are persistent and balanced over the
+//    SMs: every warp runs the same number of 32-stream groups.
 //  * Malformed metadata never causes an out-of-bounds access: offsets, states
 //    and table entries are validated or masked in-kernel and reported through
 //    an optional device status word.
@@ -405,6 +406,7 @@ __device__ __forceinline__ void cp_async_wait() {
 // (cp.async.wait_group kRingLag: groups kRingLag tiles old); otherwise the
 // tile refills from global memory, which is always exact.
 constexpr int kRingLag = 2;
+constexpr int32_t kNoRow = -(1 << 30);  // row reported by lanes without a stream
 constexpr int kRingBurst = 12;  // rows filled when a group starts
 constexpr int kRingPerTile = 2; // rows filled per tile after that
 
@@ -435,7 +437,8 @@ template <int R>
 __device__ __forceinline__ int32_t ring_fill(Ring &rg, const Chain &ch, bool live) {
     const int32_t row = ch.v >> 7;
     const int32_t r_fast = __reduce_min_sync(0xffffffffu, live ? row : INT_MAX);
-    const int32_t r_slow = __reduce_max_sync(0xffffffffu, live ? row : INT_MIN);
+    // lanes without a stream report a far-negative row (no overflow in r_slow - R)
+    const int32_t r_slow = __reduce_max_sync(0xffffffffu, live ? row : kNoRow);
     const int32_t lim = r_slow - R;
 #pragma unroll
     for (int k = 0; k < kRingPerTile; k++) {
@@ -606,92 +609,156 @@ struct FusedArgs {
     Opq q;
 };
 
+// Fused kernel, split form: each 32-stream group is handled by a pair of
+// warps, one decoding input A and one input B (one tANS chain per lane each),
+// so the SM holds twice as many warps for the same streams.  Per 8-pair tile
+// the two warps swap packed pair symbols through a small double-buffered
+// shared-memory slot (one 64-thread named barrier per tile); the A warp then
+// composes, adds and stores pairs 0-3 of the tile, the B warp pairs 4-7.
+constexpr int kSplitMaxPairs = 15;  // named barriers 1..15
+
+__device__ __forceinline__ bool block_ok(const int32_t *__restrict__ offsets, int64_t comp_bytes,
+                                         int64_t sid) {
+    const int64_t b = sid / kBlk;
+    const int64_t base = __ldg(offsets + b), next = __ldg(offsets + b + 1);
+    return base >= 0 && next > base && next <= comp_bytes && ((next - base) % 512) == 0 &&
+           (base % 4) == 0;
+}
+
+__device__ __forceinline__ uint32_t ld_stream_u32(const void *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_stream_v2(void *p, uint32_t x, uint32_t y) {
+    asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(x), "r"(y) : "memory");
+}
+
+// Two predicated 4-byte copies (rows r and r-1 of this lane's column) into
+// the row ring; the predicates are formed in PTX from the warp-uniform count.
+__device__ __forceinline__ void ring_copy2(uint32_t dst0, uint32_t dst1, const uint32_t *src0,
+                                           int32_t n, bool live) {
+    asm volatile(
+        "{\n\t.reg .pred p0, p1, lv;\n\t"
+        "setp.ne.u32 lv, %5, 0;\n\t"
+        "setp.gt.and.s32 p0, %4, 0, lv;\n\t"
+        "setp.gt.and.s32 p1, %4, 1, lv;\n\t"
+        "@p0 cp.async.ca.shared.global [%0], [%2], 4;\n\t"
+        "@p1 cp.async.ca.shared.global [%1], [%3], 4;\n\t}" ::"r"(dst0),
+        "r"(dst1), "l"(src0), "l"(src0 - kBlk), "r"(n), "r"((uint32_t)live)
+        : "memory");
+}
+
+// Per-tile ring upkeep for a warp with one chain: up to two rows filled
+// (never over a slot the slowest lane still needs), and a warp vote on
+// whether every row any lane can reach this tile is already complete.
 template <int R>
-__global__ void __launch_bounds__(kMaxWarps * 32, 1) fused_kernel(const FusedArgs p) {
+__device__ __forceinline__ bool ring_tile(Ring &rg, const Chain &ch, bool live) {
+    const int32_t row = ch.v >> 7;
+    const int32_t r_slow = __reduce_max_sync(0xffffffffu, live ? row : kNoRow);
+    const bool fast = __all_sync(0xffffffffu, !live || max(row - 2, 0) >= rg.done[kRingLag]);
+    int32_t n = min(rg.fill + 1, rg.fill - (r_slow - R));
+    n = max(min(n, kRingPerTile), 0);
+    const uint32_t f = (uint32_t)rg.fill;
+    ring_copy2(rg.lane_base + ((f & (R - 1)) << 7), rg.lane_base + (((f - 1) & (R - 1)) << 7),
+               ch.src + (int64_t)rg.fill * kBlk, n, live);
+    rg.fill -= n;
+#pragma unroll
+    for (int i = kRingLag; i > 0; i--) rg.done[i] = rg.done[i - 1];
+    rg.done[0] = rg.fill + 1;
+    return fast;
+}
+
+template <int R>
+__global__ void __launch_bounds__(kSplitMaxPairs * 64, 1) fused_split_kernel(const FusedArgs p) {
     extern __shared__ __align__(16) uint8_t smem[];
     load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
     __syncthreads();
     const uint8_t *tb = smem;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int pair = warp >> 1, side = warp & 1;  // side 0 decodes A, side 1 decodes B
+    const int pairs = blockDim.x >> 6;
     const uint32_t lane_off = 4u * (lane % kCopies);
     const uint32_t mask = (uint32_t)(R - 1) << 7;
-    Ring ra, rb;
-    ra.lane_base = ring_area<R>(smem, warp, 2) + 4u * lane;
-    rb.lane_base = ra.lane_base + R * 128u;
-    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    // exchange slots: [buffer][sender side][lane] x (pair symbols, sm half)
+    uint2 *xch = reinterpret_cast<uint2 *>(smem + kTableBytes) + pair * 128;
+    Ring rg;
+    {
+        const uint32_t bytes = R * 128u;
+        const uint32_t first =
+            (smem_addr(smem) + kTableBytes + (uint32_t)pairs * 1024u + bytes - 1) & ~(bytes - 1);
+        rg.lane_base = first + (uint32_t)warp * bytes + 4u * lane;
+    }
+    const uint32_t *comp = side ? p.b_comp : p.a_comp;
+    const int64_t comp_bytes = side ? p.b_bytes : p.a_bytes;
+    const int32_t *off = side ? p.b_off : p.a_off;
+    const uint16_t *st = side ? p.b_st : p.a_st;
+    const uint8_t *part = side ? p.b_part : p.a_part;
+    const uint8_t *smv = side ? p.b_sm : p.a_sm;
     const int64_t n_groups = (p.K + 31) / 32;
-    const int64_t n_tiles = p.N / 16, K = p.K;
-    for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; g < n_groups; g += warps) {
+    const int32_t n_tiles = (int32_t)(p.N / 16);
+    const int64_t K = p.K, tstep = K * 8, ostep = K * 16;
+    uint2 *my_slot = xch + side * 32 + lane, *their_slot = xch + (side ^ 1) * 32 + lane;
+    for (int64_t g = (int64_t)blockIdx.x * pairs + pair; g < n_groups;
+         g += (int64_t)gridDim.x * pairs) {
         const int64_t sid = g * 32 + lane;
         const bool active = sid < K;
-        Chain ca, cb;
-        chain_idle(ca, p.a_comp);
-        chain_idle(cb, p.b_comp);
-        int32_t ga = 0, gb = 0;
+        Chain ch;
+        chain_idle(ch, comp);
+        int32_t G = 0;
+        bool ok = false;
         if (active) {
-            ga = chain_init(ca, p.a_comp, p.a_bytes, p.a_off, p.a_st, p.a_part, sid, lane_off,
-                            p.status);
-            gb = chain_init(cb, p.b_comp, p.b_bytes, p.b_off, p.b_st, p.b_part, sid, lane_off,
-                            p.status);
+            G = chain_init(ch, comp, comp_bytes, off, st, part, sid, lane_off, p.status);
+            ok = block_ok(p.a_off, p.a_bytes, sid) && block_ok(p.b_off, p.b_bytes, sid);
         }
-        const bool live = active && ga > 0 && gb > 0;
-        if (!live) {
-            chain_idle(ca, p.a_comp);
-            chain_idle(cb, p.b_comp);
-        }
-        ring_start<R>(ra, ca, __reduce_max_sync(0xffffffffu, live ? ga : 0), live);
-        ring_start<R>(rb, cb, __reduce_max_sync(0xffffffffu, live ? gb : 0), live);
+        const bool live = active && ok && G > 0;
+        if (!live) chain_idle(ch, comp);
+        ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, live ? G : 0), live);
         cp_async_commit();
         cp_async_wait<0>();
-        uint2 sa_n = make_uint2(0, 0), sb_n = make_uint2(0, 0);
-        if (live && n_tiles > 0) {
-            sa_n = ld_stream_v2(p.a_sm + sid * 8);
-            sb_n = ld_stream_v2(p.b_sm + sid * 8);
-            for (int64_t t = 1; t < 4 && t < n_tiles; t++) {
-                prefetch_l2(p.a_sm + (t * K + sid) * 8);
-                prefetch_l2(p.b_sm + (t * K + sid) * 8);
-            }
-        }
-        for (int64_t t = 0; t < n_tiles; t++) {
-            const uint2 sa = sa_n, sb = sb_n;
-            if (live && t + 1 < n_tiles) {
-                sa_n = ld_stream_v2(p.a_sm + ((t + 1) * K + sid) * 8);
-                sb_n = ld_stream_v2(p.b_sm + ((t + 1) * K + sid) * 8);
-            }
-            if (live && t + 4 < n_tiles) {
-                prefetch_l2(p.a_sm + ((t + 4) * K + sid) * 8);
-                prefetch_l2(p.b_sm + ((t + 4) * K + sid) * 8);
-            }
-            const int32_t need_a = ring_fill<R>(ra, ca, live);
-            const int32_t need_b = ring_fill<R>(rb, cb, live);
+        // this warp's input: 8 sign/mantissa bytes per tile, loaded a tile
+        // ahead; this side prefetches its own input four tiles ahead
+        const uint8_t *sp = smv + sid * 8;
+        uint8_t *op = p.out + sid * 16 + 8 * side;
+        uint2 m_n = make_uint2(0, 0);
+        if (live && n_tiles > 0) m_n = ld_stream_v2(sp);
+        for (int32_t t = 0; t < n_tiles; t++) {
+            const uint2 m = m_n;
+            sp += tstep;
+            if (live && t + 1 < n_tiles) m_n = ld_stream_v2(sp);
+            if (live && t + 4 < n_tiles) prefetch_l2(sp + 3 * tstep);
+            const bool fast = ring_tile<R>(rg, ch, live);
             cp_async_commit();
             cp_async_wait<kRingLag>();
-            uint32_t ea[kTablePairs], eb[kTablePairs];
-            if (need_a >= ra.done[kRingLag] && need_b >= rb.done[kRingLag]) {
+            uint32_t e[kTablePairs];
+            if (fast) {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++) {
-                    ea[j] = chain_step_ring(ca, tb, ra.lane_base, mask, p.q);
-                    eb[j] = chain_step_ring(cb, tb, rb.lane_base, mask, p.q);
-                }
+                for (int j = 0; j < kTablePairs; j++)
+                    e[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
             } else {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++) {
-                    ea[j] = chain_step_global(ca, tb, p.q);
-                    eb[j] = chain_step_global(cb, tb, p.q);
-                }
+                for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_global(ch, tb, p.q);
             }
-            const uint32_t SA0 = gather_syms(ea[0], ea[1], ea[2], ea[3]);
-            const uint32_t SA1 = gather_syms(ea[4], ea[5], ea[6], ea[7]);
-            const uint32_t SB0 = gather_syms(eb[0], eb[1], eb[2], eb[3]);
-            const uint32_t SB1 = gather_syms(eb[4], eb[5], eb[6], eb[7]);
-            const uint32_t re0 = add_e4m3x4(compose_even(SA0, sa.x, p.q), compose_even(SB0, sb.x, p.q));
-            const uint32_t ro0 = add_e4m3x4(compose_odd(SA0, sa.x, p.q), compose_odd(SB0, sb.x, p.q));
-            const uint32_t re1 = add_e4m3x4(compose_even(SA1, sa.y, p.q), compose_even(SB1, sb.y, p.q));
-            const uint32_t ro1 = add_e4m3x4(compose_odd(SA1, sa.y, p.q), compose_odd(SB1, sb.y, p.q));
-            uint4 o = make_uint4(__byte_perm(re0, ro0, 0x5140), __byte_perm(re0, ro0, 0x7362),
-                                 __byte_perm(re1, ro1, 0x5140), __byte_perm(re1, ro1, 0x7362));
-            if (!live) o = make_uint4(0, 0, 0, 0);
-            if (active) st_stream_v4(p.out + (t * K + sid) * 16, o);
+            const uint32_t lo = gather_syms(e[0], e[1], e[2], e[3]);
+            const uint32_t hi = gather_syms(e[4], e[5], e[6], e[7]);
+            // side 0 keeps pairs 0-3 and sends 4-7; side 1 keeps 4-7, sends 0-3
+            const int buf = (t & 1) * 64;
+            my_slot[buf] = side ? make_uint2(lo, m.x) : make_uint2(hi, m.y);
+            asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
+            const uint2 o = their_slot[buf];
+            uint32_t SA, SB, MA, MB;
+            if (side) {
+                SA = o.x; MA = o.y; SB = hi; MB = m.y;
+            } else {
+                SA = lo; MA = m.x; SB = o.x; MB = o.y;
+            }
+            const uint32_t re = add_e4m3x4(compose_even(SA, MA, p.q), compose_even(SB, MB, p.q));
+            const uint32_t ro = add_e4m3x4(compose_odd(SA, MA, p.q), compose_odd(SB, MB, p.q));
+            uint32_t ox = __byte_perm(re, ro, 0x5140), oy = __byte_perm(re, ro, 0x7362);
+            if (!live) ox = oy = 0;
+            if (active) st_stream_v2(op, ox, oy);
+            op += ostep;
         }
         cp_async_wait<0>();
     }
@@ -997,6 +1064,19 @@ int stream_grid(int64_t n_vec, int sms) {
 
 }  // namespace
 
+template <int R>
+int launch_fused_split(const FusedArgs &args, int64_t n_streams, int sms, cudaStream_t stream) {
+    const int per_pair = 2 * R * 128 + 1024;
+    int max_p = (kSmemMax - kTableBytes - R * 128) / per_pair;
+    if (max_p > kSplitMaxPairs) max_p = kSplitMaxPairs;
+    const Geometry geo = balance((n_streams + 31) / 32, sms, max_p);
+    const int smem = kTableBytes + R * 128 + geo.warps_per_cta * per_pair;
+    int rc = set_smem(fused_split_kernel<R>, smem);
+    if (rc) return rc;
+    fused_split_kernel<R><<<geo.grid, geo.warps_per_cta * 64, smem, stream>>>(args);
+    return launch_status("fused_split_kernel");
+}
+
 extern "C" int tans_b200_sm_count(int *sm_count) {
     if (!sm_count) return fail(TANS_B200_ERR_INVALID, "sm_count: null");
     return device_setup(sm_count);
@@ -1117,10 +1197,10 @@ extern "C" int tans_b200_fp8_vecadd_fused(
                    n_fp8_per_stream, status, make_opq()};
     cudaStream_t st = (cudaStream_t)stream;
     switch (ring_rows(n_fp8_per_stream / 2)) {
-        case 16: return launch_ring_kernel<16>(fused_kernel<16>, args, 2, n_streams, sms, st, "fused_kernel");
-        case 32: return launch_ring_kernel<32>(fused_kernel<32>, args, 2, n_streams, sms, st, "fused_kernel");
-        case 64: return launch_ring_kernel<64>(fused_kernel<64>, args, 2, n_streams, sms, st, "fused_kernel");
-        default: return launch_ring_kernel<128>(fused_kernel<128>, args, 2, n_streams, sms, st, "fused_kernel");
+        case 16: return launch_fused_split<16>(args, n_streams, sms, st);
+        case 32: return launch_fused_split<32>(args, n_streams, sms, st);
+        case 64: return launch_fused_split<64>(args, n_streams, sms, st);
+        default: return launch_fused_split<128>(args, n_streams, sms, st);
     }
 }
 
