@@ -391,7 +391,7 @@ def run_stack(args, ws, rank, dev, barrier):
     rows sharded over the ranks, NCCL all-gather of each y; one step = one
     forward through the stack at batch `batch`."""
     import torch.distributed as dist
-    from rans_vectoradd import tans_gemv
+    from rans_vectoradd import shard, tans_gemv
     H, F, B = 5120, 17408, args.batch
     assert F % (16 * ws) == 0 and H % (16 * ws) == 0
     fr, hr = F // ws, H // ws
@@ -406,8 +406,8 @@ def run_stack(args, ws, rank, dev, barrier):
     x0 = x0.to(torch.bfloat16)
     yf = torch.empty((B, fr), dtype=torch.bfloat16, device=dev)
     yh = torch.empty((B, hr), dtype=torch.bfloat16, device=dev)
-    gf = torch.empty((ws, B, fr), dtype=torch.bfloat16, device=dev)
-    gh = torch.empty((ws, B, hr), dtype=torch.bfloat16, device=dev)
+    gf = torch.empty((ws * B, fr), dtype=torch.bfloat16, device=dev)
+    gh = torch.empty((ws * B, hr), dtype=torch.bfloat16, device=dev)
     pu = torch.empty((ups[0].col_splits, B, fr), dtype=torch.float32, device=dev)
     pd = torch.empty((downs[0].col_splits, B, hr), dtype=torch.float32, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -416,7 +416,7 @@ def run_stack(args, ws, rank, dev, barrier):
         if ws == 1:
             return y
         dist.all_gather_into_tensor(g_, y)
-        return g_.permute(1, 0, 2).reshape(B, full)
+        return shard.gather_rows(g_.view(ws, B, full // ws))
 
     def forward():
         x = x0
