@@ -243,6 +243,33 @@ def cpu_decode_add(a, b, tbl, N, n_total, budget_s=10.0):
                                        f"{t_used:.1f} s")
 
 
+def cpu_encode_rates(x, N, hist):
+    """Host encode throughput (input GB/s, 2^24 e4m3 of the workload): the
+    reference's own compiled encoder (oracle/_ref, csrc/tans_codec.cpp) and
+    this library's, on the same pair symbols and table."""
+    sys.path.insert(0, ROOT)
+    import oracle
+    from rans_vectoradd import _C, tans_codec
+    n = min(x.numel(), 1 << 24)
+    syms, _, _ = tans_codec.split_fp8(x[:n].view(n // N, N))
+    pf = torch.from_numpy(tans_codec.pair_freqs_from_exponents(hist))
+    sp = torch.from_numpy(tans_codec.build_spread(pf.numpy()))
+    out = {"sample_elements": n}
+    ref = oracle.load_ref_ext()
+    for name, fn in (("reference", ref.tans_encode_interleaved if ref else None),
+                     ("ours", _C.tans_encode_interleaved)):
+        if fn is None:
+            continue
+        fn(syms, pf, sp)
+        t0 = time.perf_counter()
+        reps = 0
+        while time.perf_counter() - t0 < 2.0:
+            fn(syms, pf, sp)
+            reps += 1
+        out[f"encode_{name}_gbs"] = round(n * reps / (time.perf_counter() - t0) / 1e9, 3)
+    return out
+
+
 def run_reference_arm(args, ws, rank):
     """--impl reference: the reference's CPU implementation of the path on the
     host cores.  The reference has no CPU decoder, so decode+add is the oracle
@@ -559,6 +586,8 @@ def main():
         gbs, threads, desc = cpu_decode_add(a, b, tbl, N, n)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": desc}
+        from rans_vectoradd.data import exponent_histogram
+        cpu["encode"] = cpu_encode_rates(x, N, exponent_histogram(x, y).double())
 
     same_all = sum_over_ranks(1.0 if same else 0.0, ws, dev) == ws
     if rank == 0:
