@@ -26,9 +26,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 import torch
@@ -43,7 +41,7 @@ FALLBACK_HBM_GBS = 6650.0
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--n-fp8", type=int, default=8192, help="fp8 bytes per stream")
@@ -116,60 +114,61 @@ def alg_bytes(a, b, n):
 
 
 class Clocks:
-    """nvidia-smi sampler over the timed region (index = this GPU)."""
+    """SM clock and throttle-reason sampler (NVML, read-only) running in a
+    thread while the timed region executes; one sample every ~2 ms."""
+
+    NAMES = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+             "sw_power_cap": 0x4}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.path = None
+        self.samples = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
 
     def __enter__(self):
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
-        os.close(fd)
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
         except Exception:
-            self.proc = None
-        time.sleep(0.3)
+            return self
+        self._stop = threading.Event()
+        reasons_fn = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    why = reasons_fn(h)
+                    watts = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    self.samples.append((mhz, why, watts))
+                except Exception:
+                    pass
+                time.sleep(0.002)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            time.sleep(0.2)
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        if self.proc is None or not self.path:
+        if not self.samples:
             return None
-        rows = []
-        for line in open(self.path):
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
-            except ValueError:
-                continue
-        os.unlink(self.path)
-        if not rows:
-            return None
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3])
-                          if v.lower() == "active"})
-        loaded = [r for r in rows if r[2] > 200.0] or rows
-        return {"sm_mhz": statistics.median(r[0] for r in loaded),
-                "sm_max_mhz": max(r[1] for r in rows), "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(r[2] for r in rows)}
+        reasons = sorted(n for n, bit in self.NAMES.items()
+                         if any(w & bit for _, w, _ in self.samples))
+        return {"sm_mhz": statistics.median(m for m, _, _ in self.samples),
+                "sm_max_mhz": self.max_mhz, "reasons": reasons, "samples": len(self.samples),
+                "power_w_max": round(max(p for _, _, p in self.samples), 1),
+                "source": "NVML, sampled during the timed region"}
 
 
 def timed(fn, steps, warmup, stream, barrier):
@@ -232,7 +231,7 @@ def cpu_decode_add(a, b, tbl, N, n_total, budget_s=10.0):
     elems = k_s * N
     reps, t_used = 0, 0.0
     t_start = time.perf_counter()
-    while t_used < budget_s and reps < 1000:
+    while t_used < budget_s and reps < 100000:
         out, ok = oracle.vecadd_fused(sa, sb, tbl, N)
         assert ok
         reps += 1
@@ -609,7 +608,7 @@ def main():
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "peak_source": peak_kind,
-                         "kernel": "fused_kernel"},
+                         "kernel": "fused_split_kernel"},
             "gpu_launches": args.steps,
             "clocks": clocks,
             "e2e": e2e,
