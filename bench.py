@@ -77,14 +77,19 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
-def profile_traffic(n_fp8: int):
-    """Per-launch DRAM bytes of the fused kernel from the committed ncu summary
-    (profiles/fused_kernel_traffic.json), scaled to this launch, or None."""
+def profile_traffic(n_fp8: int, n_elems: int):
+    """Per-launch DRAM bytes (read + write) of the fused kernel from the
+    committed ncu capture (profiles/fused_kernel_traffic.json), scaled by
+    elements to this launch; None when the capture is for another stream
+    length or is missing."""
     path = os.path.join(ROOT, "profiles", "fused_kernel_traffic.json")
     try:
         with open(path) as f:
             d = json.load(f)
-        return d.get(str(n_fp8))
+        if int(d["n_fp8_per_stream"]) != n_fp8:
+            return None
+        scale = n_elems / float(d["elements_per_input"])
+        return int(round((d["dram_bytes_read"] + d["dram_bytes_write"]) * scale))
     except Exception:
         return None
 
@@ -590,7 +595,7 @@ def main():
 
     same_all = sum_over_ranks(1.0 if same else 0.0, ws, dev) == ws
     if rank == 0:
-        traffic = profile_traffic(N)
+        traffic = profile_traffic(N, n)
         line = {
             "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step, 4),

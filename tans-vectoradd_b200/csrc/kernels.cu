@@ -91,6 +91,20 @@ __device__ __forceinline__ void prefetch_l2(const void *p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
+__device__ __forceinline__ uint32_t ld_stream_u32(const void *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_stream_v2(void *p, uint32_t x, uint32_t y) {
+    asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(x), "r"(y) : "memory");
+}
+
+__device__ __forceinline__ void st_stream_u32(void *p, uint32_t x) {
+    asm volatile("st.global.cs.u32 [%0], %1;" ::"l"(p), "r"(x) : "memory");
+}
+
 // Four e4m3 additions: byte i of the result = satfinite_e4m3(a_i + b_i).
 __device__ __forceinline__ uint32_t add_e4m3x4(uint32_t a, uint32_t b) {
     uint32_t r;
@@ -517,7 +531,19 @@ struct DecodeArgs {
     int64_t K, N;
     int32_t *status;
     Opq q;
+    int32_t word_rows;  // K % 4 == 0 and sm/out 4-byte aligned: word path allowed
 };
+
+// 4x4 byte transpose across the four lanes of a quad (lane = 4a + b):
+// lane b ends with byte b of each quad lane's word, in lane order.  Two
+// exchange rounds (halves with lane b^2, bytes with lane b^1), each one
+// shuffle and one byte permute whose selector depends on the lane.
+__device__ __forceinline__ uint32_t quad_transpose(uint32_t v, uint32_t sel1, uint32_t sel2) {
+    const uint32_t h = __shfl_xor_sync(0xffffffffu, v, 2);
+    const uint32_t t = __byte_perm(v, h, sel1);
+    const uint32_t u = __shfl_xor_sync(0xffffffffu, t, 1);
+    return __byte_perm(t, u, sel2);
+}
 
 template <int R>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeArgs p) {
@@ -526,6 +552,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
     __syncthreads();
     const uint8_t *tb = smem;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int qa = lane >> 2, qb = lane & 3;
+    const uint32_t sel1 = (qb & 2) ? 0x3276u : 0x5410u;
+    const uint32_t sel2 = (qb & 1) ? 0x3715u : 0x6240u;
     const uint32_t lane_off = 4u * (lane % kCopies);
     const uint32_t mask = (uint32_t)(R - 1) << 7;
     Ring rg;
@@ -546,44 +575,81 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
         ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, G), live);
         cp_async_commit();
         cp_async_wait<0>();
-        // sign/mantissa bytes of the next tile are loaded one tile ahead, the
-        // rows three tiles ahead are prefetched into L2
-        uint32_t mn[kTablePairs];
-#pragma unroll
-        for (int j = 0; j < kTablePairs; j++)
-            mn[j] = (live && j < P) ? __ldg(p.sm + j * K + sid) : 0u;
-        if (live)
-            for (int64_t r = kTablePairs; r < 4 * kTablePairs && r < P; r++)
-                prefetch_l2(p.sm + r * K + sid);
-        for (int64_t i = 0; i < P; i += kTablePairs) {
-            uint32_t m[kTablePairs];
-#pragma unroll
-            for (int j = 0; j < kTablePairs; j++) {
-                m[j] = mn[j];
-                const int64_t r = i + kTablePairs + j;
-                mn[j] = (live && r < P) ? __ldg(p.sm + r * K + sid) : 0u;
-                if (live && r + 3 * kTablePairs < P) prefetch_l2(p.sm + (r + 3 * kTablePairs) * K + sid);
+        // Word path, for full warps when rows are 4-byte aligned: the
+        // sign/mantissa bytes of 4 streams x 1 pair arrive as one word and are
+        // transposed across the lane quad; the composed even/odd output words
+        // are transposed back and stored 4 bytes (4 streams) at a time, each
+        // warp store covering four full 32-byte row segments.
+        const bool words = p.word_rows && g * 32 + 32 <= K;
+        const int32_t full_tiles = words ? (int32_t)(P / kTablePairs) : 0;
+        const uint8_t *smw = p.sm + qb * K + g * 32 + 4 * qa;
+        uint8_t *ow = p.out + 2 * qb * K + g * 32 + 4 * qa;
+        const int64_t srow = kTablePairs * K, orow = 2 * kTablePairs * K;
+        uint32_t w0n = 0, w1n = 0;
+        if (full_tiles > 0) {
+            w0n = ld_stream_u32(smw);
+            w1n = ld_stream_u32(smw + 4 * K);
+        }
+        for (int32_t t = 0; t < full_tiles; t++) {
+            const uint32_t w0 = w0n, w1 = w1n;
+            smw += srow;
+            if (t + 1 < full_tiles) {
+                w0n = ld_stream_u32(smw);
+                w1n = ld_stream_u32(smw + 4 * K);
             }
+            if (t + 4 < full_tiles) prefetch_l2(smw + 3 * srow + (qa & 1) * 4 * K);
             const int32_t need = ring_fill<R>(rg, ch, live);
             cp_async_commit();
             cp_async_wait<kRingLag>();
-            uint32_t s[kTablePairs];
+            uint32_t e[kTablePairs];
             if (need >= rg.done[kRingLag]) {
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j++)
-                    s[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
+                    e[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
             } else {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++) s[j] = chain_step_global(ch, tb, p.q);
+                for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_global(ch, tb, p.q);
+            }
+            const uint32_t M0 = quad_transpose(w0, sel1, sel2);
+            const uint32_t M1 = quad_transpose(w1, sel1, sel2);
+            const uint32_t S0 = gather_syms(e[0], e[1], e[2], e[3]);
+            const uint32_t S1 = gather_syms(e[4], e[5], e[6], e[7]);
+            uint32_t E0 = compose_even(S0, M0, p.q), O0 = compose_odd(S0, M0, p.q);
+            uint32_t E1 = compose_even(S1, M1, p.q), O1 = compose_odd(S1, M1, p.q);
+            if (!live) E0 = O0 = E1 = O1 = 0;
+            E0 = quad_transpose(E0, sel1, sel2);
+            O0 = quad_transpose(O0, sel1, sel2);
+            E1 = quad_transpose(E1, sel1, sel2);
+            O1 = quad_transpose(O1, sel1, sel2);
+            st_stream_u32(ow, E0);          // element 2b
+            st_stream_u32(ow + K, O0);      // element 2b + 1
+            st_stream_u32(ow + 8 * K, E1);  // element 8 + 2b
+            st_stream_u32(ow + 9 * K, O1);  // element 9 + 2b
+            ow += orow;
+        }
+        // Byte path: the rest of the stream (all of it for a partial warp or
+        // unaligned rows), one pair at a time.
+        for (int64_t i = (int64_t)full_tiles * kTablePairs; i < P; i += kTablePairs) {
+            const int32_t need = ring_fill<R>(rg, ch, live);
+            cp_async_commit();
+            cp_async_wait<kRingLag>();
+            uint32_t s8[kTablePairs];
+            if (need >= rg.done[kRingLag]) {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++)
+                    s8[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
+            } else {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++) s8[j] = chain_step_global(ch, tb, p.q);
             }
             if (active) {
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j++) {
                     if (i + j >= P) break;
-                    const uint32_t sy = (s[j] >> 8) & 0xFFu;
-                    const uint32_t v0 = ((m[j] & 8u) << 4) | ((sy >> 4) << 3) | (m[j] & 7u);
-                    const uint32_t v1 =
-                        (((m[j] >> 4) & 8u) << 4) | ((sy & 15u) << 3) | ((m[j] >> 4) & 7u);
+                    const uint32_t m = live ? __ldg(p.sm + (i + j) * K + sid) : 0u;
+                    const uint32_t sy = (s8[j] >> 8) & 0xFFu;
+                    const uint32_t v0 = ((m & 8u) << 4) | ((sy >> 4) << 3) | (m & 7u);
+                    const uint32_t v1 = (((m >> 4) & 8u) << 4) | ((sy & 15u) << 3) | ((m >> 4) & 7u);
                     p.out[(2 * (i + j)) * K + sid] = live ? (uint8_t)v0 : 0;
                     p.out[(2 * (i + j) + 1) * K + sid] = live ? (uint8_t)v1 : 0;
                 }
@@ -623,16 +689,6 @@ __device__ __forceinline__ bool block_ok(const int32_t *__restrict__ offsets, in
     const int64_t base = __ldg(offsets + b), next = __ldg(offsets + b + 1);
     return base >= 0 && next > base && next <= comp_bytes && ((next - base) % 512) == 0 &&
            (base % 4) == 0;
-}
-
-__device__ __forceinline__ uint32_t ld_stream_u32(const void *p) {
-    uint32_t v;
-    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
-    return v;
-}
-
-__device__ __forceinline__ void st_stream_v2(void *p, uint32_t x, uint32_t y) {
-    asm volatile("st.global.cs.v2.u32 [%0], {%1,%2};" ::"l"(p), "r"(x), "r"(y) : "memory");
 }
 
 // Two predicated 4-byte copies (rows r and r-1 of this lane's column) into
@@ -1153,7 +1209,8 @@ extern "C" int tans_b200_decode(const uint8_t *compressed, int64_t compressed_by
     if (rc) return rc;
     DecodeArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets,
                     states, partial, sign_mantissa, decode_table, out, n_streams,
-                    n_fp8_per_stream, status, make_opq()};
+                    n_fp8_per_stream, status, make_opq(),
+                    (int32_t)(n_streams % 4 == 0 && aligned(sign_mantissa, 4) && aligned(out, 4))};
     cudaStream_t st = (cudaStream_t)stream;
     switch (ring_rows(n_fp8_per_stream / 2)) {
         case 16: return launch_ring_kernel<16>(decode_kernel<16>, args, 1, n_streams, sms, st, "decode_kernel");
@@ -1344,7 +1401,8 @@ extern "C" int tans_b200_decode_noalloc(const uint8_t *compressed, int64_t compr
     if (rc) return rc;
     DecodeArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets,
                     states, partial, sign_mantissa, table, out, n_streams,
-                    n_fp8_per_stream, status, make_opq()};
+                    n_fp8_per_stream, status, make_opq(),
+                    (int32_t)(n_streams % 4 == 0 && aligned(sign_mantissa, 4) && aligned(out, 4))};
     switch (ring_rows(n_fp8_per_stream / 2)) {
         case 16: return launch_ring_kernel<16>(decode_kernel<16>, args, 1, n_streams, sms, st, "decode_kernel");
         case 32: return launch_ring_kernel<32>(decode_kernel<32>, args, 1, n_streams, sms, st, "decode_kernel");

@@ -119,7 +119,8 @@ def test_device_table_build_matches_host(cuda):
         assert np.array_equal(got.cpu().numpy(), t[f"{src}_table"]), src
 
 
-@pytest.mark.parametrize("K,N", [(1, 2), (33, 16), (129, 8192), (4096, 2), (517, 1000)])
+@pytest.mark.parametrize("K,N", [(1, 2), (33, 16), (129, 8192), (4096, 2), (517, 1000),
+                                 (132, 1002), (96, 18), (256, 4100)])
 def test_decode_ragged_vs_oracle(cuda, K, N):
     gen = torch.Generator().manual_seed(K + N)
     fp8 = random_fp8_bytes(K * N, device="cpu", generator=gen).reshape(K, N)
