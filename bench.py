@@ -50,10 +50,12 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--out", default=None, help="also append the JSON line(s) to this file")
-    ap.add_argument("--workload", choices=["vecadd", "decode", "gemv", "stack"],
+    ap.add_argument("--workload", choices=["vecadd", "decode", "encode", "gemv", "stack"],
                     default="vecadd", help="vecadd (cfg1, headline), decode (cfg2), "
-                    "gemv (cfg3), stack (cfg4: 40-layer row-sharded GEMV + all-gather)")
-    ap.add_argument("--decode-log2", type=int, default=32, help="log2 fp8 elements (decode)")
+                    "encode (device encoder on the cfg2 input), gemv (cfg3), "
+                    "stack (cfg4: 40-layer row-sharded GEMV + all-gather)")
+    ap.add_argument("--decode-log2", type=int, default=32,
+                    help="log2 fp8 elements (decode, encode)")
     ap.add_argument("--layers", type=int, default=40, help="layers of the GEMV stack")
     ap.add_argument("--batch", type=int, default=8, help="GEMV batch (1..8)")
     return ap.parse_args()
@@ -320,38 +322,73 @@ def emit(line, args):
 
 # -------------------------------------------------------------- other configs
 
-def encode_chunked(n: int, N: int, seed: int, dev, chunk_log2: int = 28):
-    """cfg2 input: n e4m3 bytes of N(0,1)*448/absmax (generated on the GPU,
-    seeded), encoded in chunks of whole encoder blocks with one table (from
-    the first chunk's exponent histogram, empty bins weighted 1); offsets of
-    later chunks are rebased.  Returns host tensors for tans_b200_decode and
-    the raw bytes on the device (for the round-trip check)."""
-    from rans_vectoradd import tans_codec
+def cfg2_input(n: int, N: int, seed: int, dev, chunk_log2: int = 28):
+    """cfg2 input: n e4m3 bytes of N(0,1)*448/absmax, generated on the GPU in
+    seeded chunks of 2^chunk_log2 (each scaled by its own absmax), and the
+    exponent histogram of the first chunk with empty bins weighted 1 (the
+    one table of the whole input)."""
     from rans_vectoradd.data import exponent_histogram
     g = torch.Generator(device=dev).manual_seed(seed)
     chunk = min(n, 1 << chunk_log2)
-    parts, raw = [], torch.empty(n, dtype=torch.uint8, device=dev)
-    hist = None
+    raw = torch.empty(n, dtype=torch.uint8, device=dev)
     for off in range(0, n, chunk):
         v = torch.randn(chunk, device=dev, generator=g)
         raw[off:off + chunk] = (v * (448.0 / v.abs().max())).to(torch.float8_e4m3fn).view(torch.uint8)
-        host = raw[off:off + chunk].cpu()
-        if hist is None:
-            hist = exponent_histogram(host).clamp_min(1).double()
-        parts.append(tans_codec.encode(host.view(chunk // N, N), hist, tile=0))
-    comp, offs, states, part, sm = [], [], [], [], []
-    base = 0
-    for e in parts:
-        comp.append(e[0]); states.append(e[1]); part.append(e[3]); sm.append(e[4])
-        o = e[2].to(torch.int64) + base
-        offs.append(o[:-1] if e is not parts[-1] else o)
-        base += e[0].numel()
+        del v
+    hist = exponent_histogram(raw[:chunk].cpu()).clamp_min(1).double()
+    return raw, hist
+
+
+def encode_cfg2(n: int, N: int, seed: int, dev):
+    """cfg2 input encoded on the device (tile 0) with the public encoder.
+    Returns (comp, offsets, states, partial, sm, decode table, K, raw)."""
+    from rans_vectoradd import tans_codec
+    raw, hist = cfg2_input(n, N, seed, dev)
     K = n // N
-    sm_all = torch.cat([s_.view(N // 2, -1) for s_ in sm], dim=1).contiguous()
-    table = tans_codec.build_decode_table(parts[0][6].numpy(), parts[0][5].numpy())
-    assert base < 2 ** 31, "compressed size exceeds the format's int32 offsets"
-    return (torch.cat(comp), torch.cat(offs).to(torch.int32), torch.cat(states), torch.cat(part),
-            sm_all, table, K, raw)
+    comp, states, offsets, part, sm, pf, sp = tans_codec.encode(raw.view(K, N), hist, tile=0)
+    table = tans_codec.build_decode_table(sp.numpy(), pf.numpy()).to(dev)
+    return comp, offsets, states, part, sm, table, K, raw
+
+
+def run_encode(args, dev, barrier):
+    """Device slab encoder on the cfg2 input (2^decode_log2 e4m3 bytes,
+    n_fp8 per stream, tile 0): one step = tans_codec's device path minus the
+    table build: split + pass 1 + scan, the 16-byte header read, pass 2.
+    Checked by a device decode round trip; the host encoders (the
+    reference's compiled one and ours) are timed beside it."""
+    from rans_vectoradd import _C, gpu_tans_decode, tans_codec
+    from rans_vectoradd._lib import ENC_INPUT_FP8
+    n = 1 << args.decode_log2
+    N = args.n_fp8
+    K = n // N
+    raw, hist = cfg2_input(n, N, 0, dev)
+    x = raw.view(K, N)
+    pf = torch.from_numpy(tans_codec.pair_freqs_from_exponents(hist))
+    sp = torch.from_numpy(tans_codec.build_spread(pf.numpy()))
+    stream = torch.cuda.current_stream(dev)
+    res = {}
+
+    def step():
+        res["out"] = None  # release the previous outputs to the caching allocator first
+        res["out"] = _C.encode_device(x, ENC_INPUT_FP8, pf, sp, 0)
+    step()
+    comp, st, off, part, sm = res["out"]
+    dec = gpu_tans_decode(comp, off, st, part, sm, sp.to(dev), pf.to(dev), N)
+    ok = bool(torch.equal(dec.t(), x))
+    del dec
+    ms = timed(step, args.steps, args.warmup, stream, barrier) / args.steps
+    comp, st, off, part, sm = res["out"]
+    out_bytes = sum(t.numel() * t.element_size() for t in (comp, st, off, part, sm))
+    alg = n + out_bytes
+    peak, kind = measured_peak()
+    line = {"workload": "encode (device, cfg2 input)", "elements": n, "n_fp8_per_stream": N,
+            "streams": K, "ms": round(ms, 4), "input_gbs": round(n / (ms / 1e3) / 1e9, 2),
+            "hbm_frac_algorithmic": round(alg / (ms / 1e3) / 1e9 / peak, 4),
+            "algorithmic_bytes": alg, "bits_per_fp8": round(out_bytes * 8 / n, 4),
+            "bit_exact_round_trip": ok, "peak_source": kind}
+    if not args.no_cpu:
+        line["cpu_encode"] = cpu_encode_rates(raw[:1 << 24].cpu(), N, hist)
+    emit(line, args)
 
 
 def run_decode(args, dev, barrier):
@@ -360,7 +397,7 @@ def run_decode(args, dev, barrier):
     from rans_vectoradd._lib import LIB, check
     n = 1 << args.decode_log2
     N = args.n_fp8
-    comp, off, st, part, sm, tbl, K, raw = encode_chunked(n, N, 0, dev)
+    comp, off, st, part, sm, tbl, K, raw = encode_cfg2(n, N, 0, dev)
     d = [t.to(dev) for t in (comp, off, st, part, sm, tbl)]
     out = torch.empty((N, K), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -387,7 +424,7 @@ def make_gemv_weight(R, C, seed, dev, col_splits):
     g = torch.Generator(device=dev).manual_seed(seed)
     w = torch.randn(R, C, device=dev, generator=g) * 0.02
     w8, s = tans_gemv.quantize_rows(w)
-    return tans_gemv.encode_weight(w8.cpu(), s.cpu(), col_splits=col_splits).to(dev), w8, s
+    return tans_gemv.encode_weight(w8, s, col_splits=col_splits).to(dev), w8, s
 
 
 def run_gemv(args, dev, barrier):
@@ -517,7 +554,8 @@ def main():
         if args.workload == "stack":
             run_stack(args, ws, rank, dev, barrier)
         elif rank == 0 and ws == 1:
-            run_decode(args, dev, barrier) if args.workload == "decode" else run_gemv(args, dev, barrier)
+            {"decode": run_decode, "encode": run_encode,
+             "gemv": run_gemv}[args.workload](args, dev, barrier)
         if ws > 1:
             import torch.distributed as dist
             dist.barrier(device_ids=[local])

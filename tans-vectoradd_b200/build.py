@@ -2,8 +2,9 @@
 
     python tans-vectoradd_b200/build.py [--force] [--verbose]
 
-Sources: csrc/kernels.cu (device kernels + device entry points) and
-csrc/host.cpp (CPU encoder, host table builder, FP8 splitter, errors).
+Sources: csrc/kernels.cu (decode/add/GEMV kernels + their entry points),
+csrc/encode.cu (device slab encoder) and csrc/host.cpp (CPU encoder, host
+table builders, FP8 splitter, errors).
 Output: rans_vectoradd/libtans_b200.so next to the Python package that loads
 it, so the built file travels with the source tree.  No torch headers are
 involved; the library depends only on the CUDA runtime and OpenMP.
@@ -21,8 +22,10 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 OUT = os.path.join(HERE, "rans_vectoradd", "libtans_b200.so")
-SOURCES = [os.path.join(CSRC, "kernels.cu"), os.path.join(CSRC, "host.cpp"),
-           os.path.join(INCLUDE, "tans_b200.h")]
+CU_SOURCES = [os.path.join(CSRC, "kernels.cu"), os.path.join(CSRC, "encode.cu")]
+HOST_SOURCE = os.path.join(CSRC, "host.cpp")
+SOURCES = CU_SOURCES + [HOST_SOURCE, os.path.join(INCLUDE, "tans_b200.h"),
+                        os.path.join(CSRC, "internal.h")]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
@@ -51,12 +54,14 @@ def build(force: bool = False, verbose: bool = False) -> str:
     # the system g++ carries OpenMP; some images point CXX at a compiler without it
     cxx = shutil.which("g++") or "g++"
     with tempfile.TemporaryDirectory() as tmp:
-        k_obj = os.path.join(tmp, "kernels.o")
+        cu_objs = [os.path.join(tmp, os.path.basename(s) + ".o") for s in CU_SOURCES]
         h_obj = os.path.join(tmp, "host.o")
         cmds = [
-            [nvcc, "-c", SOURCES[0], "-o", k_obj, *ARCH, "-O3", "-lineinfo", "-std=c++17",
-             "-Xcompiler", "-fPIC", "-ccbin", cxx, "-Xptxas", "-v" if verbose else "-O3"],
-            [cxx, "-c", SOURCES[1], "-o", h_obj, "-O3", "-fPIC", "-fopenmp", "-std=c++17",
+            [nvcc, "-c", src, "-o", obj, *ARCH, "-O3", "-lineinfo", "-std=c++17",
+             "-Xcompiler", "-fPIC", "-ccbin", cxx, "-Xptxas", "-v" if verbose else "-O3"]
+            for src, obj in zip(CU_SOURCES, cu_objs)
+        ] + [
+            [cxx, "-c", HOST_SOURCE, "-o", h_obj, "-O3", "-fPIC", "-fopenmp", "-std=c++17",
              "-Wall", "-Wextra"],
         ]
         procs = [subprocess.Popen(c, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
@@ -68,7 +73,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
             if p.returncode:
                 raise RuntimeError(f"build failed: {' '.join(cmd)}")
         tmp_out = os.path.join(tmp, "libtans_b200.so")
-        link = [nvcc, "-shared", *ARCH, "-ccbin", cxx, k_obj, h_obj, "-o", tmp_out,
+        link = [nvcc, "-shared", *ARCH, "-ccbin", cxx, *cu_objs, h_obj, "-o", tmp_out,
                 "-Xcompiler", "-fopenmp", "-lgomp", "-cudart", "shared"]
         r = subprocess.run(link, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
         if r.returncode:

@@ -1,0 +1,467 @@
+// encode.cu — sm_100a slab encoder: the device twin of the CPU encoder
+// (host.cpp) and of the reference's tans_encode_interleaved
+// (csrc/tans_codec.cpp:69-196), with the FP8 nibble split of
+// rans_vectoradd/tans_codec.py:106-124 fused in.  Output bytes are identical
+// to both.  The reference has no device encoder; this is the GPU side of the
+// same wire format.
+//
+// Work split.  The format is serial inside a stream (each step's state
+// depends on the previous one) and independent across streams, so one
+// thread encodes one stream and a CTA of 128 threads is one encoder block.
+// The block layout (slab count G_b of every block, top-aligned streams) must
+// be known before any slab can be placed, so the encoder runs the state
+// machine twice:
+//   enc_setup_kernel  copies the alphabet tables into the workspace;
+//   enc_count_kernel  pass 1: reads the input back to front, writes the
+//                     sign/mantissa bytes (FP8 input), the final state and
+//                     the slab count of every stream and G_b of its block;
+//   enc_scan_kernel   exclusive scan of G_b * 512 into the int32 offsets;
+//   enc_emit_kernel   pass 2: re-runs the state machine and stores every
+//                     completed slab straight into its final slot (zero slabs
+//                     below a short stream are written too, so the output
+//                     needs no memset).
+// The host reads the 16-byte workspace header between the two calls to size
+// the compressed buffer.
+//
+// Step (pair symbol s, state x in [4096, 8192), tables in shared memory):
+//     k  = (x + delta[s]) >> 16          bits to emit
+//     emit x & (2^k - 1), LSB-first
+//     x  = next[base[s] + (x >> k)]
+// delta/base depend only on s, so their lookup is off the x dependency
+// chain; the chain is add, shift, shift, address, one 16-bit shared load.
+
+#include "../../include/tans_b200.h"
+#include "internal.h"
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <climits>
+
+using tans_b200::EncoderTables;
+using tans_b200::fail;
+
+namespace {
+
+constexpr int kL = TANS_B200_TABLE_SIZE;
+constexpr int kBlk = TANS_B200_BLOCK_STREAMS;
+constexpr int kScanThreads = 1024;
+
+// Workspace layout (bytes).  The header is the public tans_b200_enc_header.
+constexpr size_t kWsInfo = 16;                    // int2[256] {delta, base}
+constexpr size_t kWsNext = kWsInfo + 256 * 8;     // uint16[4096]
+constexpr size_t kWsSlabs = 10496;                // uint32[K]: slabs per stream
+static_assert(kWsNext + kL * 2 <= kWsSlabs, "workspace tables overlap");
+
+__host__ __device__ __forceinline__ size_t ws_blocks_offset(int64_t K) { return (kWsSlabs + 4 * (size_t)K + 255) & ~(size_t)255; }
+
+struct EncArgs {
+    const uint8_t *in;    // FP8 bytes [K][2P] or pair symbols [K][P]
+    int64_t K, P;         // streams, pair symbols per stream
+    int64_t tile;         // sm layout: 0 -> [P][K], t -> [P/t][K][t]
+    int32_t vec;          // 16-byte (FP8) / 8-byte (symbols) chunk loads allowed
+    int32_t sm_vec;       // tile 8 and sm 8-byte aligned: one 8-byte store per chunk
+    uint8_t *sm;          // FP8 input only
+    uint16_t *states;
+    const int32_t *offsets;
+    int32_t *offsets_out;
+    uint8_t *compressed;
+    uint8_t *partial;
+    uint8_t *ws;
+};
+
+__device__ __forceinline__ tans_b200_enc_header *header(uint8_t *ws) {
+    return reinterpret_cast<tans_b200_enc_header *>(ws);
+}
+__device__ __forceinline__ uint32_t *slabs_of(uint8_t *ws) {
+    return reinterpret_cast<uint32_t *>(ws + kWsSlabs);
+}
+
+__device__ __forceinline__ uint4 ld_nc_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ld_nc_v2(const void *p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+// Exponent pair symbols of one word of 4 e4m3 bytes: byte 0 = pair (b0, b1),
+// byte 2 = pair (b2, b3), each exp(first) << 4 | exp(second).
+__device__ __forceinline__ uint32_t pair_syms_of(uint32_t w) {
+    const uint32_t e = (w >> 3) & 0x0F0F0F0Fu;
+    return ((e << 4) | (e >> 8)) & 0x00FF00FFu;
+}
+// Sign/mantissa pairs of the same word in bytes 0 and 2:
+// sm(first) | sm(second) << 4 with sm(b) = (b >> 4 & 8) | (b & 7).
+__device__ __forceinline__ uint32_t sm_pairs_of(uint32_t w) {
+    const uint32_t m = ((w >> 4) & 0x08080808u) | (w & 0x07070707u);
+    return m | (m >> 4);
+}
+
+// Byte j (0..3) of w, zero-extended.
+__device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return (w >> (8 * j)) & 0xFFu; }
+
+struct EncTables {
+    const int2 *info;
+    const uint16_t *next;
+};
+
+// Pass-1 state: state, bit count and the largest k seen (13 marks a symbol
+// that cannot be coded).
+struct Counter {
+    uint32_t x, bits, kmax;
+    __device__ __forceinline__ void step(const EncTables &t, uint32_t s) {
+        const int2 inf = t.info[s];
+        const uint32_t k = (x + (uint32_t)inf.x) >> 16;
+        bits += k;
+        kmax = max(kmax, k);
+        x = t.next[inf.y + (int32_t)(x >> k)];
+    }
+};
+
+// Pass-2 state: state plus the pending slab lo (fill bits) and a running
+// pointer to the next slab slot of this stream (stride 512 bytes).
+struct Emitter {
+    uint32_t x, lo, fill;
+    uint32_t *out;
+    __device__ __forceinline__ void step(const EncTables &t, uint32_t s) {
+        const int2 inf = t.info[s];
+        const uint32_t k = (x + (uint32_t)inf.x) >> 16;
+        const uint32_t v = x & ((1u << k) - 1u);
+        const uint32_t hi = __funnelshift_l(v, 0u, fill);  // bits that spill past 32
+        lo |= v << fill;
+        fill += k;
+        if (fill >= 32) {
+            *out = lo;
+            out += kBlk;
+            lo = hi;
+            fill -= 32;
+        }
+        x = t.next[inf.y + (int32_t)(x >> k)];
+    }
+};
+
+__device__ __forceinline__ void store_sm_byte(const EncArgs &a, int64_t k, int64_t i, uint32_t v) {
+    if (a.tile == 0)
+        a.sm[i * a.K + k] = (uint8_t)v;
+    else
+        a.sm[((i / a.tile) * a.K + k) * a.tile + (i % a.tile)] = (uint8_t)v;
+}
+
+// Symbol i of stream k read without chunking (ragged tail, unaligned rows);
+// writes the sign/mantissa byte in pass 1.
+template <bool kFp8, bool kPass1>
+__device__ __forceinline__ uint32_t scalar_symbol(const EncArgs &a, const uint8_t *row, int64_t k,
+                                                  int64_t i) {
+    if (!kFp8) return row[i];
+    const uint32_t b0 = row[2 * i], b1 = row[2 * i + 1];
+    if (kPass1) {
+        const uint32_t m0 = ((b0 >> 4) & 8u) | (b0 & 7u), m1 = ((b1 >> 4) & 8u) | (b1 & 7u);
+        store_sm_byte(a, k, i, m0 | (m1 << 4));
+    }
+    return (((b0 >> 3) & 15u) << 4) | ((b1 >> 3) & 15u);
+}
+
+// Run `m` over stream k from its last pair symbol to its first.
+template <bool kFp8, bool kPass1, typename Machine>
+__device__ __forceinline__ void run_stream(const EncArgs &a, const EncTables &t, int64_t k,
+                                           Machine &m) {
+    const int64_t P = a.P;
+    const uint8_t *row = a.in + k * P * (kFp8 ? 2 : 1);
+    const int64_t chunks = a.vec ? P / 8 : 0;
+    for (int64_t i = P - 1; i >= chunks * 8; i--) m.step(t, scalar_symbol<kFp8, kPass1>(a, row, k, i));
+    if (chunks == 0) return;
+    if (kFp8) {
+        const uint8_t *cp = row + (chunks - 1) * 16;
+        uint4 w = ld_nc_v4(cp);
+        for (int64_t c = chunks - 1; c >= 0; c--) {
+            const uint4 cur = w;
+            if (c > 0) w = ld_nc_v4(cp - 16);
+            cp -= 16;
+            const uint32_t s0 = pair_syms_of(cur.x), s1 = pair_syms_of(cur.y);
+            const uint32_t s2 = pair_syms_of(cur.z), s3 = pair_syms_of(cur.w);
+            if (kPass1) {
+                const uint32_t lo = __byte_perm(sm_pairs_of(cur.x), sm_pairs_of(cur.y), 0x6420);
+                const uint32_t hi = __byte_perm(sm_pairs_of(cur.z), sm_pairs_of(cur.w), 0x6420);
+                if (a.sm_vec) {
+                    *reinterpret_cast<uint2 *>(a.sm + (c * a.K + k) * 8) = make_uint2(lo, hi);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 8; j++)
+                        store_sm_byte(a, k, c * 8 + j, byte_of(j < 4 ? lo : hi, j & 3));
+                }
+            }
+            m.step(t, s3 >> 16);
+            m.step(t, s3 & 0xFFu);
+            m.step(t, s2 >> 16);
+            m.step(t, s2 & 0xFFu);
+            m.step(t, s1 >> 16);
+            m.step(t, s1 & 0xFFu);
+            m.step(t, s0 >> 16);
+            m.step(t, s0 & 0xFFu);
+        }
+    } else {
+        const uint8_t *cp = row + (chunks - 1) * 8;
+        uint2 w = ld_nc_v2(cp);
+        for (int64_t c = chunks - 1; c >= 0; c--) {
+            const uint2 cur = w;
+            if (c > 0) w = ld_nc_v2(cp - 8);
+            cp -= 8;
+#pragma unroll
+            for (int j = 7; j >= 0; j--) m.step(t, byte_of(j < 4 ? cur.x : cur.y, j & 3));
+        }
+    }
+}
+
+__device__ __forceinline__ EncTables load_tables(uint8_t *smem, const uint8_t *ws) {
+    // 2 KB of {delta, base} and 8 KB of next states, copied as 16-byte words
+    const uint4 *src = reinterpret_cast<const uint4 *>(ws + kWsInfo);
+    uint4 *dst = reinterpret_cast<uint4 *>(smem);
+    for (int i = threadIdx.x; i < (int)((kWsNext - kWsInfo + kL * 2) / 16); i += blockDim.x)
+        dst[i] = src[i];
+    __syncthreads();
+    return EncTables{reinterpret_cast<const int2 *>(smem),
+                     reinterpret_cast<const uint16_t *>(smem + (kWsNext - kWsInfo))};
+}
+
+constexpr int kTableSmem = (int)(kWsNext - kWsInfo) + kL * 2;
+
+__global__ void enc_setup_kernel(const __grid_constant__ EncoderTables t, uint8_t *ws) {
+    const int i = threadIdx.x;
+    if (i == 0) {
+        tans_b200_enc_header *h = header(ws);
+        h->error_bits = 0;
+        h->bad_symbol = INT_MAX;
+        h->total_bytes = 0;
+    }
+    int2 *info = reinterpret_cast<int2 *>(ws + kWsInfo);
+    for (int s = i; s < 256; s += blockDim.x) info[s] = make_int2(t.delta[s], t.base[s]);
+    uint16_t *next = reinterpret_cast<uint16_t *>(ws + kWsNext);
+    for (int j = i; j < kL; j += blockDim.x) next[j] = t.next[j];
+}
+
+template <bool kFp8>
+__global__ void __launch_bounds__(kBlk) enc_count_kernel(const EncArgs a) {
+    __shared__ __align__(16) uint8_t smem[kTableSmem];
+    __shared__ uint32_t warp_max[kBlk / 32];
+    const EncTables t = load_tables(smem, a.ws);
+    const int64_t k = (int64_t)blockIdx.x * kBlk + threadIdx.x;
+    uint32_t slabs = 0;
+    if (k < a.K) {
+        Counter c{(uint32_t)kL, 0u, 0u};
+        run_stream<kFp8, true>(a, t, k, c);
+        a.states[k] = (uint16_t)c.x;
+        slabs = (c.bits + 31) >> 5;
+        slabs_of(a.ws)[k] = slabs;
+        if (c.kmax >= (uint32_t)tans_b200::kEncoderBadBits) {
+            // error path: find the symbols that have no slot and report the smallest
+            tans_b200_enc_header *h = header(a.ws);
+            atomicOr(&h->error_bits, TANS_B200_ENC_BAD_SYMBOL);
+            const uint8_t *row = a.in + k * a.P * (kFp8 ? 2 : 1);
+            for (int64_t i = 0; i < a.P; i++) {
+                uint32_t s;
+                if (kFp8)
+                    s = (((row[2 * i] >> 3) & 15u) << 4) | ((row[2 * i + 1] >> 3) & 15u);
+                else
+                    s = row[i];
+                if (t.info[s].x == (tans_b200::kEncoderBadBits << 16)) atomicMin(&h->bad_symbol, (int)s);
+            }
+        }
+    }
+    const uint32_t m = __reduce_max_sync(0xffffffffu, slabs);
+    if ((threadIdx.x & 31) == 0) warp_max[threadIdx.x >> 5] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint32_t g = 1;  // an all-empty block still has one slab per stream
+        for (int w = 0; w < kBlk / 32; w++) g = max(g, warp_max[w]);
+        reinterpret_cast<uint32_t *>(a.ws + ws_blocks_offset(a.K))[blockIdx.x] = g;
+    }
+}
+
+// offsets[b] = 512 * sum_{c<b} G_c (int64 running sum; a total above
+// INT32_MAX is flagged and the offsets are not used).
+__global__ void __launch_bounds__(kScanThreads) enc_scan_kernel(const EncArgs a, int64_t B) {
+    __shared__ int64_t warp_sum[kScanThreads / 32];
+    __shared__ int64_t carry_s;
+    const uint32_t *g = reinterpret_cast<const uint32_t *>(a.ws + ws_blocks_offset(a.K));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) carry_s = 0;
+    __syncthreads();
+    for (int64_t base = 0; base < B; base += kScanThreads) {
+        const int64_t b = base + threadIdx.x;
+        const int64_t v = b < B ? (int64_t)g[b] * (kBlk * 4) : 0;
+        int64_t incl = v;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+            const int64_t o = __shfl_up_sync(0xffffffffu, incl, d);
+            if (lane >= d) incl += o;
+        }
+        if (lane == 31) warp_sum[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            int64_t w = warp_sum[lane];
+#pragma unroll
+            for (int d = 1; d < 32; d <<= 1) {
+                const int64_t o = __shfl_up_sync(0xffffffffu, w, d);
+                if (lane >= d) w += o;
+            }
+            warp_sum[lane] = w;  // inclusive over warps
+        }
+        __syncthreads();
+        const int64_t carry = carry_s;
+        const int64_t excl = carry + (warp ? warp_sum[warp - 1] : 0) + incl - v;
+        if (b < B) a.offsets_out[b] = (int32_t)excl;
+        __syncthreads();
+        if (threadIdx.x == 0) carry_s = carry + warp_sum[kScanThreads / 32 - 1];
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        const int64_t total = carry_s;
+        a.offsets_out[B] = (int32_t)total;
+        tans_b200_enc_header *h = header(a.ws);
+        h->total_bytes = total;
+        if (total > INT32_MAX) atomicOr(&h->error_bits, TANS_B200_ENC_TOO_LARGE);
+    }
+}
+
+template <bool kFp8>
+__global__ void __launch_bounds__(kBlk) enc_emit_kernel(const EncArgs a) {
+    __shared__ __align__(16) uint8_t smem[kTableSmem];
+    const EncTables t = load_tables(smem, a.ws);
+    if (header(a.ws)->error_bits != 0) return;  // layout not valid: write nothing
+    const int64_t k = (int64_t)blockIdx.x * kBlk + threadIdx.x;
+    const int64_t off = a.offsets[blockIdx.x];
+    const uint32_t g_b = (uint32_t)((a.offsets[blockIdx.x + 1] - off) / (kBlk * 4));
+    // columns past the last stream of a partial block are zero, like the slabs
+    // below a short stream
+    const uint32_t g_s = k < a.K ? slabs_of(a.ws)[k] : 0u;
+    uint32_t *out = reinterpret_cast<uint32_t *>(a.compressed + off) + threadIdx.x;
+    for (uint32_t g = g_s; g < g_b; g++, out += kBlk) *out = 0u;  // slabs below a short stream
+    if (k >= a.K) return;
+    Emitter e{(uint32_t)kL, 0u, 0u, out};
+    run_stream<kFp8, false>(a, t, k, e);
+    if (e.fill > 0) *e.out = e.lo;
+    a.partial[k] = (uint8_t)e.fill;
+}
+
+int launch_status(const char *what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(TANS_B200_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+    return TANS_B200_OK;
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// 12 bits per pair symbol at most: the per-stream bit count stays in 32 bits.
+constexpr int64_t kMaxPairsPerStream = (int64_t)(UINT32_MAX / 12);
+
+int check_shape(int input_kind, int64_t K, int64_t n, int64_t *P) {
+    if (input_kind != TANS_B200_ENC_INPUT_FP8 && input_kind != TANS_B200_ENC_INPUT_SYMBOLS)
+        return fail(TANS_B200_ERR_INVALID, "encode_device: unknown input kind %d", input_kind);
+    if (K < 0 || n < 0) return fail(TANS_B200_ERR_INVALID, "encode: bad arguments");
+    if (input_kind == TANS_B200_ENC_INPUT_FP8 && n % 2 != 0)
+        return fail(TANS_B200_ERR_INVALID, "encode_device: FP8 bytes per stream must be even");
+    *P = input_kind == TANS_B200_ENC_INPUT_FP8 ? n / 2 : n;
+    if (*P > kMaxPairsPerStream)
+        return fail(TANS_B200_ERR_INVALID, "encode_device: more than %lld symbols per stream",
+                    (long long)kMaxPairsPerStream);
+    return TANS_B200_OK;
+}
+
+}  // namespace
+
+extern "C" int tans_b200_encode_device_workspace_bytes(int64_t K, int64_t *bytes) {
+    tans_b200::clear_error();
+    if (K < 0 || !bytes) return fail(TANS_B200_ERR_INVALID, "encode_device_workspace_bytes: bad arguments");
+    const int64_t B = (K + kBlk - 1) / kBlk;
+    *bytes = (int64_t)ws_blocks_offset(K) + 4 * B + 4;
+    return TANS_B200_OK;
+}
+
+extern "C" int tans_b200_encode_device_plan(const uint8_t *in, int input_kind, int64_t K,
+                                            int64_t n, int64_t tile, const int32_t *freqs,
+                                            int64_t n_syms, const int32_t *spread,
+                                            uint8_t *sm_out, uint16_t *states_out,
+                                            int32_t *offsets_out, void *workspace, void *stream) {
+    tans_b200::clear_error();
+    int64_t P;
+    int rc = check_shape(input_kind, K, n, &P);
+    if (rc) return rc;
+    const bool fp8 = input_kind == TANS_B200_ENC_INPUT_FP8;
+    if (fp8 && tile < 0) return fail(TANS_B200_ERR_INVALID, "encode_device: tile must be >= 0");
+    if (fp8 && tile > 0 && P % tile != 0)
+        return fail(TANS_B200_ERR_INVALID, "n_pairs=%lld not divisible by tile=%lld", (long long)P,
+                    (long long)tile);
+    if (!workspace || !offsets_out || (K > 0 && !states_out) ||
+        (K > 0 && P > 0 && (!in || (fp8 && !sm_out))))
+        return fail(TANS_B200_ERR_INVALID, "encode_device: null pointer");
+    if (!aligned(workspace, 256) || !aligned(offsets_out, 4) || !aligned(states_out, 2))
+        return fail(TANS_B200_ERR_INVALID, "encode_device: misaligned output or workspace");
+    EncoderTables tables;
+    rc = tans_b200::encoder_tables(freqs, n_syms, spread, &tables);
+    if (rc) return rc;
+    cudaStream_t st = (cudaStream_t)stream;
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    enc_setup_kernel<<<1, 256, 0, st>>>(tables, ws);
+    if ((rc = launch_status("enc_setup_kernel"))) return rc;
+    const int64_t B = (K + kBlk - 1) / kBlk;
+    EncArgs a{};
+    a.in = in;
+    a.K = K;
+    a.P = P;
+    a.tile = fp8 ? tile : 0;
+    a.vec = fp8 ? (aligned(in, 16) && (2 * P) % 16 == 0) : (aligned(in, 8) && P % 8 == 0);
+    a.sm = sm_out;
+    a.sm_vec = fp8 && tile == 8 && aligned(sm_out, 8);
+    a.states = states_out;
+    a.offsets_out = offsets_out;
+    a.ws = ws;
+    if (B > 0) {
+        if (B > INT_MAX) return fail(TANS_B200_ERR_INVALID, "encode_device: too many streams");
+        if (fp8)
+            enc_count_kernel<true><<<(unsigned)B, kBlk, 0, st>>>(a);
+        else
+            enc_count_kernel<false><<<(unsigned)B, kBlk, 0, st>>>(a);
+        if ((rc = launch_status("enc_count_kernel"))) return rc;
+    }
+    enc_scan_kernel<<<1, kScanThreads, 0, st>>>(a, B);
+    return launch_status("enc_scan_kernel");
+}
+
+extern "C" int tans_b200_encode_device_emit(const uint8_t *in, int input_kind, int64_t K,
+                                            int64_t n, const int32_t *offsets,
+                                            const void *workspace, uint8_t *compressed,
+                                            uint8_t *partial_out, void *stream) {
+    tans_b200::clear_error();
+    int64_t P;
+    int rc = check_shape(input_kind, K, n, &P);
+    if (rc) return rc;
+    if (K == 0) return TANS_B200_OK;
+    if (!workspace || !offsets || !compressed || !partial_out || (P > 0 && !in))
+        return fail(TANS_B200_ERR_INVALID, "encode_device: null pointer");
+    if (!aligned(workspace, 256) || !aligned(offsets, 4) || !aligned(compressed, 4))
+        return fail(TANS_B200_ERR_INVALID, "encode_device: misaligned compressed or workspace");
+    const bool fp8 = input_kind == TANS_B200_ENC_INPUT_FP8;
+    const int64_t B = (K + kBlk - 1) / kBlk;
+    if (B > INT_MAX) return fail(TANS_B200_ERR_INVALID, "encode_device: too many streams");
+    EncArgs a{};
+    a.in = in;
+    a.K = K;
+    a.P = P;
+    a.vec = fp8 ? (aligned(in, 16) && (2 * P) % 16 == 0) : (aligned(in, 8) && P % 8 == 0);
+    a.offsets = offsets;
+    a.compressed = compressed;
+    a.partial = partial_out;
+    a.ws = static_cast<uint8_t *>(const_cast<void *>(workspace));
+    cudaStream_t st = (cudaStream_t)stream;
+    if (fp8)
+        enc_emit_kernel<true><<<(unsigned)B, kBlk, 0, st>>>(a);
+    else
+        enc_emit_kernel<false><<<(unsigned)B, kBlk, 0, st>>>(a);
+    return launch_status("enc_emit_kernel");
+}

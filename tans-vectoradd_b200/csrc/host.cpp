@@ -20,6 +20,7 @@
 // Both passes are OpenMP-parallel over streams.
 
 #include "../../include/tans_b200.h"
+#include "internal.h"
 
 #include <omp.h>
 
@@ -305,6 +306,45 @@ extern "C" int tans_b200_encoded_export(const tans_b200_encoded *e, uint8_t *com
 }
 
 extern "C" void tans_b200_encoded_free(tans_b200_encoded *e) { delete e; }
+
+// Tables of the device encoder (layout and meaning in internal.h).
+int tans_b200::encoder_tables(const int32_t *freqs, int64_t n_syms, const int32_t *spread,
+                              EncoderTables *t) {
+    if (!freqs || !spread || !t || n_syms <= 0)
+        return fail(TANS_B200_ERR_INVALID, "encode: bad arguments");
+    std::vector<uint32_t> cum(n_syms + 1, 0u);
+    uint64_t sum = 0;
+    for (int64_t s = 0; s < n_syms; s++) {
+        if (freqs[s] < 0)
+            return fail(TANS_B200_ERR_INVALID, "encode: freqs[%lld] is negative", (long long)s);
+        cum[s] = static_cast<uint32_t>(std::min<uint64_t>(sum, kL));
+        sum += static_cast<uint32_t>(freqs[s]);
+    }
+    if (sum != kL)
+        return fail(TANS_B200_ERR_INVALID, "freqs must sum to L=%u; got %llu", kL,
+                    (unsigned long long)sum);
+    std::vector<uint32_t> seen(n_syms, 0u);
+    for (uint32_t slot = 0; slot < kL; slot++) {
+        int32_t s = spread[slot];
+        if (s < 0 || s >= n_syms || seen[s] >= static_cast<uint32_t>(freqs[s]))
+            return fail(TANS_B200_ERR_INVALID,
+                        "encode: spread[%u]=%d inconsistent with freqs (alphabet %lld)", slot, s,
+                        (long long)n_syms);
+        t->next[cum[s] + seen[s]++] = static_cast<uint16_t>(kL + slot);
+    }
+    for (int s = 0; s < 256; s++) {
+        const uint32_t f = s < n_syms ? static_cast<uint32_t>(freqs[s]) : 0u;
+        if (f == 0) {
+            t->delta[s] = kEncoderBadBits << 16;
+            t->base[s] = 0;
+            continue;
+        }
+        const uint32_t k1 = 12u - std::min(31u - static_cast<uint32_t>(__builtin_clz(f)), 12u);
+        t->delta[s] = static_cast<int32_t>((k1 << 16) - (f << k1));
+        t->base[s] = static_cast<int32_t>(cum[s]) - static_cast<int32_t>(f);
+    }
+    return TANS_B200_OK;
+}
 
 // ------------------------------------------------------------ FP8 splitter
 

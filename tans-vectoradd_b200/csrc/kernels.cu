@@ -502,7 +502,7 @@ Geometry balance(int64_t n_groups, int sms, int max_warps_per_cta) {
 }
 
 constexpr int kTableBytes = kL * kCopies * 4;
-constexpr int kMaxWarps = 16;  // 512 threads per CTA, one CTA per SM
+constexpr int kMaxWarps = 16;  // 512 threads per CTA, one CTA per SM (24 measured slower on cfg2)
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);

@@ -98,14 +98,71 @@ def _streams_per_block_from_env() -> int:
 
 # ------------------------------------------------------------------ encoder
 
+def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: torch.Tensor,
+                  tile: int = 0):
+    """Device slab encoder (csrc/encode.cu) on a contiguous CUDA uint8 input
+    [K, n]: kind ENC_INPUT_FP8 (e4m3 bytes, n even; also returns the
+    sign/mantissa pairs in the `tile` layout) or ENC_INPUT_SYMBOLS (pair
+    symbols).  freqs/spread may live on any device.  Returns (compressed u8,
+    states u16[K], offsets i32[B+1], partial u8[K], sm u8 or None), all on
+    inp's device; bytes identical to the CPU encoder's."""
+    from . import _lib
+    _req(inp.is_cuda and inp.dtype == torch.uint8 and inp.dim() == 2 and inp.is_contiguous(),
+         "input must be a contiguous CUDA uint8 [K, n] tensor")
+    _req(freqs.dtype == torch.int32, "freqs must be int32")
+    _req(spread.dtype == torch.int32, "spread must be int32")
+    _req(spread.numel() == _L, f"spread must have {_L} entries")
+    fr = freqs.detach().to("cpu").contiguous()
+    sp = spread.detach().to("cpu").contiguous()
+    K, n = inp.shape
+    dev = inp.device
+    fp8 = kind == _lib.ENC_INPUT_FP8
+    P = n // 2 if fp8 else n
+    nblocks = (K + _BLOCK - 1) // _BLOCK
+    with torch.cuda.device(dev):
+        wsb = ctypes.c_int64()
+        check(LIB.tans_b200_encode_device_workspace_bytes(K, ctypes.byref(wsb)))
+        ws = torch.empty(wsb.value, dtype=torch.uint8, device=dev)
+        states = torch.empty(K, dtype=torch.uint16, device=dev)
+        offsets = torch.empty(nblocks + 1, dtype=torch.int32, device=dev)
+        sm = None
+        if fp8:
+            shape = (P // tile, K, tile) if tile > 0 and P % tile == 0 else (P, K)
+            sm = torch.empty(shape, dtype=torch.uint8, device=dev)
+        st = _stream(dev)
+        check(LIB.tans_b200_encode_device_plan(
+            inp.data_ptr(), kind, K, n, tile, fr.data_ptr(), fr.numel(), sp.data_ptr(),
+            sm.data_ptr() if sm is not None else None, states.data_ptr(), offsets.data_ptr(),
+            ws.data_ptr(), st))
+        hdr = ws[:16].cpu()
+        err, bad = (int(v) for v in hdr[:8].view(torch.int32))
+        total = int(hdr[8:].view(torch.int64)[0])
+        if err & _lib.ENC_BAD_SYMBOL:
+            raise RuntimeError(f"encode: symbol {bad} occurs but has zero frequency")
+        if err & _lib.ENC_TOO_LARGE:
+            raise RuntimeError("encode: compressed size exceeds the int32 offsets of the format")
+        comp = torch.empty(total, dtype=torch.uint8, device=dev)
+        partial = torch.empty(K, dtype=torch.uint8, device=dev)
+        check(LIB.tans_b200_encode_device_emit(inp.data_ptr(), kind, K, n, offsets.data_ptr(),
+                                               ws.data_ptr(), comp.data_ptr(),
+                                               partial.data_ptr(), st))
+    return comp, states, offsets, partial, sm
+
+
 def tans_encode_interleaved(symbols: torch.Tensor, freqs: torch.Tensor, spread: torch.Tensor):
-    """CPU tANS encoder -> GPU-ready interleaved slab layout
+    """tANS encoder -> GPU-ready interleaved slab layout
     (csrc/tans_codec.cpp:69-196).  Returns (compressed u8, states u16[K],
-    offsets i32[B+1], partial u8[K]), all CPU tensors."""
+    offsets i32[B+1], partial u8[K]): CPU tensors from CPU symbols (as the
+    reference), or tensors on the symbols' device from CUDA symbols (device
+    encoder, same bytes)."""
     _req(symbols.dim() == 2, "symbols must be [K, N]")
     _req(symbols.dtype == torch.uint8, "symbols must be uint8")
     _req(freqs.dtype == torch.int32, "freqs must be int32")
     _req(spread.dtype == torch.int32, "spread must be int32")
+    if symbols.is_cuda:
+        from ._lib import ENC_INPUT_SYMBOLS
+        _req(symbols.is_contiguous(), "symbols must be contiguous")
+        return encode_device(symbols, ENC_INPUT_SYMBOLS, freqs, spread)[:4]
     _req(symbols.is_contiguous() and not symbols.is_cuda, "symbols must be contiguous CPU")
     _req(freqs.is_contiguous() and not freqs.is_cuda, "freqs must be contiguous CPU")
     _req(spread.is_contiguous() and not spread.is_cuda, "spread must be contiguous CPU")

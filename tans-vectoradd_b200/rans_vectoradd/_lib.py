@@ -15,6 +15,10 @@ OK = 0
 DATA_BAD_OFFSETS = 1
 DATA_BAD_STATE = 2
 DATA_BAD_TABLE = 4
+ENC_INPUT_FP8 = 0
+ENC_INPUT_SYMBOLS = 1
+ENC_TOO_LARGE = 1
+ENC_BAD_SYMBOL = 2
 
 
 def _load() -> ctypes.CDLL:
@@ -42,6 +46,9 @@ def _load() -> ctypes.CDLL:
                                              i64, i64, p, p]),
         "tans_b200_decode_noalloc": (i32, [p, i64, p, p, p, p, p, p, i64, p, i64, i64, p, p]),
         "tans_b200_gemv": (i32, [p, i64, p, p, p, p, p, p, p, p, p, i64, i64, i64, i64, p, p]),
+        "tans_b200_encode_device_workspace_bytes": (i32, [i64, ctypes.POINTER(i64)]),
+        "tans_b200_encode_device_plan": (i32, [p, i32, i64, i64, i64, p, i64, p, p, p, p, p, p]),
+        "tans_b200_encode_device_emit": (i32, [p, i32, i64, i64, p, p, p, p, p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

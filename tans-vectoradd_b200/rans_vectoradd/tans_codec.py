@@ -136,6 +136,9 @@ def encode(
 
     Returns compressed [bytes], final_states [K], block_offsets
     [n_blocks+1], partial_cnts [K] (uint8), sm_packed, pair_freqs, spread.
+    CPU input encodes on the host (as the reference); CUDA input encodes on
+    its device (split + slab encode kernels) and the first five outputs stay
+    there.  Bytes are identical either way.
     """
     assert fp8_bytes.dim() == 2 and fp8_bytes.dtype == torch.uint8
     K, N = fp8_bytes.shape
@@ -143,11 +146,17 @@ def encode(
     if tile > 0:
         n_pairs = N // 2
         assert n_pairs % tile == 0, f"n_pairs={n_pairs} not divisible by tile={tile}"
-    pair_syms, sm_packed, _ = split_fp8(fp8_bytes, tile)
     pair_freqs = pair_freqs_from_exponents(exp_freqs)
     spread = build_spread(pair_freqs)
     pair_freqs_t = torch.from_numpy(pair_freqs)
     spread_t = torch.from_numpy(spread)
+    if fp8_bytes.is_cuda:
+        # device encoder: split and slab encode on the GPU, outputs stay there
+        from ._lib import ENC_INPUT_FP8
+        compressed, states, offsets, partial_cnts, sm_packed = _C.encode_device(
+            fp8_bytes.contiguous(), ENC_INPUT_FP8, pair_freqs_t, spread_t, tile)
+        return (compressed, states, offsets, partial_cnts, sm_packed, pair_freqs_t, spread_t)
+    pair_syms, sm_packed, _ = split_fp8(fp8_bytes, tile)
     compressed, states, offsets, partial_cnts = _C.tans_encode_interleaved(
         pair_syms, pair_freqs_t, spread_t)
     return (compressed, states, offsets, partial_cnts, sm_packed, pair_freqs_t, spread_t)

@@ -14,7 +14,8 @@ each stream:
   straight into a fragment register.
 
 `encode_weight` builds that stream matrix and encodes it with
-`tans_codec.encode(..., tile=8)`; `gemv` runs the sm_100a kernel.
+`tans_codec.encode(..., tile=8)` (on the GPU when W is a CUDA tensor);
+`gemv` runs the sm_100a kernel.
 """
 from __future__ import annotations
 
@@ -87,21 +88,22 @@ def default_col_splits(rows: int, cols: int, sms: int = 148, warps_per_sm: int =
 
 def encode_weight(w8: torch.Tensor, scale: torch.Tensor, exp_freqs=None,
                   col_splits: int | None = None) -> EncodedWeight:
-    """tANS-encode e4m3 weight bytes for `gemv` (host).  `col_splits`
-    defaults to default_col_splits(rows, cols)."""
-    w8 = w8.detach().to("cpu").contiguous()
+    """tANS-encode e4m3 weight bytes for `gemv`: on the host for a CPU w8,
+    with the device encoder (outputs on w8's device) for a CUDA w8; the bytes
+    are the same.  `col_splits` defaults to default_col_splits(rows, cols)."""
+    w8 = w8.detach().contiguous()
     if col_splits is None:
         col_splits = default_col_splits(*w8.shape)
     if exp_freqs is None:
         # empty exponent bins get weight 1 so every pair keeps a slot (no
         # zero-probability symbols for the frequency quantiser to misplace)
         exp_freqs = torch.bincount(((w8.reshape(-1) >> 3) & 15).long(),
-                                   minlength=16).clamp_min(1).double()
+                                   minlength=16).clamp_min(1).double().cpu()
     streams = stream_matrix(w8, col_splits)
     comp, st, off, part, sm, pf, sp = tans_codec.encode(streams, exp_freqs, tile=8)
-    table = tans_codec.build_decode_table(sp.numpy(), pf.numpy())
+    table = tans_codec.build_decode_table(sp.numpy(), pf.numpy()).to(w8.device)
     return EncodedWeight(comp, off, st, part, sm, table,
-                         scale.detach().float().to("cpu").contiguous(), w8.shape[0],
+                         scale.detach().float().to(w8.device).contiguous(), w8.shape[0],
                          w8.shape[1], col_splits, pf, sp)
 
 

@@ -92,3 +92,16 @@ def test_gemv_rejects_bad_shapes():
                               16, 96, 1, 1, None, None) == 1
     assert LIB.tans_b200_gemv(None, 0, None, None, None, None, None, None, None, None, None,
                               16, 64, 9, 1, None, None) == 1
+
+
+@pytest.mark.gpu
+def test_gemv_device_encoded_weight_matches_host(cuda):
+    """encode_weight on a CUDA W (device encoder) gives the host encoder's bytes."""
+    w8, s = make(1024, 4352, 9)
+    host = tans_gemv.encode_weight(w8, s, col_splits=4)
+    dev = tans_gemv.encode_weight(w8.to(cuda), s.to(cuda), col_splits=4)
+    for name in ("compressed", "offsets", "states", "partial", "sm", "table", "scale"):
+        a, b = getattr(host, name), getattr(dev, name)
+        assert b.is_cuda and torch.equal(a, b.cpu()), name
+    x = torch.randn(8, 4352, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16)
+    assert torch.equal(tans_gemv.gemv(dev, x.to(cuda)), tans_gemv.gemv(host.to(cuda), x.to(cuda)))
