@@ -149,6 +149,52 @@ int tans_b200_fp8_vecadd_fused(
     const int32_t *decode_table, uint8_t *out, int64_t n_streams,
     int64_t n_fp8_per_stream, int32_t *status, void *stream);
 
+/* The same on the streams [stream_begin, stream_end) of the K-stream layout
+ * only (stream_begin a multiple of 128: whole encoder blocks).  All pointers
+ * and K are those of the full tensors; only the range is read and written.
+ * No reference counterpart: it lets callers split one call across CUDA
+ * streams or pipeline it with host transfers. */
+int tans_b200_fp8_vecadd_fused_range(
+    const uint8_t *a_compressed, int64_t a_compressed_bytes,
+    const int32_t *a_offsets, const uint16_t *a_states,
+    const uint8_t *a_partial, const uint8_t *a_sm,
+    const uint8_t *b_compressed, int64_t b_compressed_bytes,
+    const int32_t *b_offsets, const uint16_t *b_states,
+    const uint8_t *b_partial, const uint8_t *b_sm,
+    const int32_t *decode_table, uint8_t *out, int64_t n_streams,
+    int64_t n_fp8_per_stream, int64_t stream_begin, int64_t stream_end,
+    int32_t *status, void *stream);
+
+/* Fused decode + FP8 add from and to HOST memory (no reference counterpart;
+ * the reference's op takes device tensors).  All a_* / b_* inputs,
+ * decode_table and out are host pointers, in the layouts of
+ * tans_b200_fp8_vecadd_fused; page-locked memory lets the copies overlap.
+ * The streams are split into chunks of whole encoder blocks
+ * (chunk_streams, rounded up to 128; <= 0 picks K/8) and pipelined over
+ * three internal CUDA streams: chunk c's host->device copies, its kernel and
+ * its device->host copy of the output run while neighbouring chunks copy in
+ * the other direction.  The work is ordered after `stream`'s prior work and
+ * `stream` waits for all of it, so the call is asynchronous like a
+ * cudaMemcpyAsync: host buffers must stay valid until `stream` reaches that
+ * point.  `workspace` is a caller-owned device buffer of
+ * tans_b200_fp8_vecadd_fused_host_workspace_bytes() bytes (256-byte
+ * aligned) that holds the device copies.  Calls on one device enqueue under
+ * a library lock; calls whose work overlaps must not share a workspace. */
+int tans_b200_fp8_vecadd_fused_host_workspace_bytes(
+    int64_t n_streams, int64_t n_fp8_per_stream, int64_t a_compressed_bytes,
+    int64_t b_compressed_bytes, int64_t *bytes);
+
+int tans_b200_fp8_vecadd_fused_host(
+    const uint8_t *a_compressed, int64_t a_compressed_bytes,
+    const int32_t *a_offsets, const uint16_t *a_states,
+    const uint8_t *a_partial, const uint8_t *a_sm,
+    const uint8_t *b_compressed, int64_t b_compressed_bytes,
+    const int32_t *b_offsets, const uint16_t *b_states,
+    const uint8_t *b_partial, const uint8_t *b_sm,
+    const int32_t *decode_table, uint8_t *out, int64_t n_streams,
+    int64_t n_fp8_per_stream, int64_t chunk_streams, void *workspace,
+    int64_t workspace_bytes, int32_t *status, void *stream);
+
 /* Fused tANS-decode GEMV (no counterpart in the reference; the BASELINE
  * configuration cfg3/cfg4):
  *   y[b][r] = bf16(scale[r] * sum_c e4m3(W[r][c]) * x[b][c]), fp32 accumulate,

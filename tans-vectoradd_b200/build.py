@@ -3,8 +3,9 @@
     python tans-vectoradd_b200/build.py [--force] [--verbose]
 
 Sources: csrc/kernels.cu (decode/add/GEMV kernels + their entry points),
-csrc/encode.cu (device slab encoder) and csrc/host.cpp (CPU encoder, host
-table builders, FP8 splitter, errors).
+csrc/encode.cu (device slab encoder), csrc/pipeline.cu (host-memory
+pipelined fused add) and csrc/host.cpp (CPU encoder, host table builders,
+FP8 splitter, errors).
 Output: rans_vectoradd/libtans_b200.so next to the Python package that loads
 it, so the built file travels with the source tree.  No torch headers are
 involved; the library depends only on the CUDA runtime and OpenMP.
@@ -22,7 +23,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 OUT = os.path.join(HERE, "rans_vectoradd", "libtans_b200.so")
-CU_SOURCES = [os.path.join(CSRC, "kernels.cu"), os.path.join(CSRC, "encode.cu")]
+CU_SOURCES = [os.path.join(CSRC, "kernels.cu"), os.path.join(CSRC, "encode.cu"),
+              os.path.join(CSRC, "pipeline.cu")]
 HOST_SOURCE = os.path.join(CSRC, "host.cpp")
 SOURCES = CU_SOURCES + [HOST_SOURCE, os.path.join(INCLUDE, "tans_b200.h"),
                         os.path.join(CSRC, "internal.h")]

@@ -421,6 +421,8 @@ __device__ __forceinline__ void cp_async_wait() {
 // tile refills from global memory, which is always exact.
 constexpr int kRingLag = 2;
 constexpr int32_t kNoRow = -(1 << 30);  // row reported by lanes without a stream
+constexpr int kDecodeLag = 1;   // fill-group age read by the decode kernel
+constexpr int kGemvLag = 2;     // and by the GEMV kernel
 constexpr int kRingBurst = 12;  // rows filled when a group starts
 constexpr int kRingPerTile = 2; // rows filled per tile after that
 
@@ -600,9 +602,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
             if (t + 4 < full_tiles) prefetch_l2(smw + 3 * srow + (qa & 1) * 4 * K);
             const int32_t need = ring_fill<R>(rg, ch, live);
             cp_async_commit();
-            cp_async_wait<kRingLag>();
+            cp_async_wait<kDecodeLag>();
             uint32_t e[kTablePairs];
-            if (need >= rg.done[kRingLag]) {
+            if (need >= rg.done[kDecodeLag]) {
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j++)
                     e[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
@@ -632,9 +634,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
         for (int64_t i = (int64_t)full_tiles * kTablePairs; i < P; i += kTablePairs) {
             const int32_t need = ring_fill<R>(rg, ch, live);
             cp_async_commit();
-            cp_async_wait<kRingLag>();
+            cp_async_wait<kDecodeLag>();
             uint32_t s8[kTablePairs];
-            if (need >= rg.done[kRingLag]) {
+            if (need >= rg.done[kDecodeLag]) {
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j++)
                     s8[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
@@ -670,7 +672,8 @@ struct FusedArgs {
     const uint8_t *a_sm, *b_sm;  // [N/16][K][8]
     const int32_t *table;
     uint8_t *out;                // [N/16][K][16]
-    int64_t K, N;
+    int64_t K, N;                // K: streams decoded (pointers start at the first one)
+    int64_t stride;              // streams of the layout: row stride of the sm/out tiles
     int32_t *status;
     Opq q;
 };
@@ -706,25 +709,73 @@ __device__ __forceinline__ void ring_copy2(uint32_t dst0, uint32_t dst1, const u
         : "memory");
 }
 
-// Per-tile ring upkeep for a warp with one chain: up to two rows filled
-// (never over a slot the slowest lane still needs), and a warp vote on
-// whether every row any lane can reach this tile is already complete.
-template <int R>
+// Four predicated 4-byte copies (rows r .. r-3 of this lane's column).
+__device__ __forceinline__ void ring_copy4(uint32_t base, uint32_t f, uint32_t wrap,
+                                           const uint32_t *src0, int32_t n, bool live) {
+    asm volatile(
+        "{\n\t.reg .pred p0, p1, p2, p3, lv;\n\t.reg .u32 d;\n\t"
+        "setp.ne.u32 lv, %4, 0;\n\t"
+        "setp.gt.and.s32 p0, %3, 0, lv;\n\t"
+        "setp.gt.and.s32 p1, %3, 1, lv;\n\t"
+        "setp.gt.and.s32 p2, %3, 2, lv;\n\t"
+        "setp.gt.and.s32 p3, %3, 3, lv;\n\t"
+        "and.b32 d, %1, %2;\n\t"
+        "shl.b32 d, d, 7;\n\t"
+        "add.u32 d, d, %0;\n\t"
+        "@p0 cp.async.ca.shared.global [d], [%5], 4;\n\t"
+        "sub.u32 d, %1, 1;\n\t"
+        "and.b32 d, d, %2;\n\t"
+        "shl.b32 d, d, 7;\n\t"
+        "add.u32 d, d, %0;\n\t"
+        "@p1 cp.async.ca.shared.global [d], [%6], 4;\n\t"
+        "sub.u32 d, %1, 2;\n\t"
+        "and.b32 d, d, %2;\n\t"
+        "shl.b32 d, d, 7;\n\t"
+        "add.u32 d, d, %0;\n\t"
+        "@p2 cp.async.ca.shared.global [d], [%7], 4;\n\t"
+        "sub.u32 d, %1, 3;\n\t"
+        "and.b32 d, d, %2;\n\t"
+        "shl.b32 d, d, 7;\n\t"
+        "add.u32 d, d, %0;\n\t"
+        "@p3 cp.async.ca.shared.global [d], [%8], 4;\n\t}" ::"r"(base),
+        "r"(f), "r"(wrap), "r"(n), "r"((uint32_t)live), "l"(src0), "l"(src0 - kBlk),
+        "l"(src0 - 2 * kBlk), "l"(src0 - 3 * kBlk)
+        : "memory");
+}
+
+// Ring upkeep for a warp with one chain, once per kTiles tiles: up to
+// 2 * kTiles rows filled (never over a slot the slowest lane still needs),
+// and a warp vote on whether every row any lane can reach in the next
+// kTiles tiles (at most 3 * kTiles refills: rows row .. row - (3 kTiles - 1))
+// is already complete.
+template <int R, int kTiles, int kLag>
 __device__ __forceinline__ bool ring_tile(Ring &rg, const Chain &ch, bool live) {
+    static_assert(kTiles == 1 || kTiles == 2, "ring upkeep covers one or two tiles");
+    static_assert(kLag >= 1 && kLag <= kRingLag, "lag beyond the recorded fill frontiers");
     const int32_t row = ch.v >> 7;
     const int32_t r_slow = __reduce_max_sync(0xffffffffu, live ? row : kNoRow);
-    const bool fast = __all_sync(0xffffffffu, !live || max(row - 2, 0) >= rg.done[kRingLag]);
+    const bool fast =
+        __all_sync(0xffffffffu, !live || max(row - (3 * kTiles - 1), 0) >= rg.done[kLag]);
     int32_t n = min(rg.fill + 1, rg.fill - (r_slow - R));
-    n = max(min(n, kRingPerTile), 0);
+    n = max(min(n, kRingPerTile * kTiles), 0);
     const uint32_t f = (uint32_t)rg.fill;
-    ring_copy2(rg.lane_base + ((f & (R - 1)) << 7), rg.lane_base + (((f - 1) & (R - 1)) << 7),
-               ch.src + (int64_t)rg.fill * kBlk, n, live);
+    static_assert(kRingPerTile * kTiles <= 4, "at most four row copies per upkeep");
+    if (kRingPerTile * kTiles <= 2)
+        ring_copy2(rg.lane_base + ((f & (R - 1)) << 7), rg.lane_base + (((f - 1) & (R - 1)) << 7),
+                   ch.src + (int64_t)rg.fill * kBlk, n, live);
+    else
+        ring_copy4(rg.lane_base, f, R - 1, ch.src + (int64_t)rg.fill * kBlk, n, live);
     rg.fill -= n;
 #pragma unroll
     for (int i = kRingLag; i > 0; i--) rg.done[i] = rg.done[i - 1];
     rg.done[0] = rg.fill + 1;
     return fast;
 }
+
+// Tiles between ring upkeeps in the fused kernel, and how many upkeeps old a
+// fill group must be before its rows are read (cp.async.wait_group depth).
+constexpr int kFusedUpkeepTiles = 1;
+constexpr int kFusedLag = 1;
 
 template <int R>
 __global__ void __launch_bounds__(kSplitMaxPairs * 64, 1) fused_split_kernel(const FusedArgs p) {
@@ -754,7 +805,7 @@ __global__ void __launch_bounds__(kSplitMaxPairs * 64, 1) fused_split_kernel(con
     const uint8_t *smv = side ? p.b_sm : p.a_sm;
     const int64_t n_groups = (p.K + 31) / 32;
     const int32_t n_tiles = (int32_t)(p.N / 16);
-    const int64_t K = p.K, tstep = K * 8, ostep = K * 16;
+    const int64_t K = p.K, tstep = p.stride * 8, ostep = p.stride * 16;
     uint2 *my_slot = xch + side * 32 + lane, *their_slot = xch + (side ^ 1) * 32 + lane;
     for (int64_t g = (int64_t)blockIdx.x * pairs + pair; g < n_groups;
          g += (int64_t)gridDim.x * pairs) {
@@ -779,14 +830,17 @@ __global__ void __launch_bounds__(kSplitMaxPairs * 64, 1) fused_split_kernel(con
         uint8_t *op = p.out + sid * 16 + 8 * side;
         uint2 m_n = make_uint2(0, 0);
         if (live && n_tiles > 0) m_n = ld_stream_v2(sp);
+        bool fast = false;
         for (int32_t t = 0; t < n_tiles; t++) {
             const uint2 m = m_n;
             sp += tstep;
             if (live && t + 1 < n_tiles) m_n = ld_stream_v2(sp);
             if (live && t + 4 < n_tiles) prefetch_l2(sp + 3 * tstep);
-            const bool fast = ring_tile<R>(rg, ch, live);
-            cp_async_commit();
-            cp_async_wait<kRingLag>();
+            if (t % kFusedUpkeepTiles == 0) {
+                fast = ring_tile<R, kFusedUpkeepTiles, kFusedLag>(rg, ch, live);
+                cp_async_commit();
+                cp_async_wait<kFusedLag>();
+            }
             uint32_t e[kTablePairs];
             if (fast) {
 #pragma unroll
@@ -959,9 +1013,9 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
             const int32_t need_a = ring_fill<R>(ra, ca, live);
             const int32_t need_b = ring_fill<R>(rb, cb, live);
             cp_async_commit();
-            cp_async_wait<kRingLag>();
+            cp_async_wait<kGemvLag>();
             uint32_t ea[kTablePairs], eb[kTablePairs];
-            if (need_a >= ra.done[kRingLag] && need_b >= rb.done[kRingLag]) {
+            if (need_a >= ra.done[kGemvLag] && need_b >= rb.done[kGemvLag]) {
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j++) {
                     ea[j] = chain_step_ring(ca, tb, ra.lane_base, mask, p.q);
@@ -1227,6 +1281,19 @@ extern "C" int tans_b200_fp8_vecadd_fused(
     const uint16_t *b_states, const uint8_t *b_partial, const uint8_t *b_sm,
     const int32_t *decode_table, uint8_t *out, int64_t n_streams, int64_t n_fp8_per_stream,
     int32_t *status, void *stream) {
+    return tans_b200_fp8_vecadd_fused_range(
+        a_compressed, a_compressed_bytes, a_offsets, a_states, a_partial, a_sm, b_compressed,
+        b_compressed_bytes, b_offsets, b_states, b_partial, b_sm, decode_table, out, n_streams,
+        n_fp8_per_stream, 0, n_streams, status, stream);
+}
+
+extern "C" int tans_b200_fp8_vecadd_fused_range(
+    const uint8_t *a_compressed, int64_t a_compressed_bytes, const int32_t *a_offsets,
+    const uint16_t *a_states, const uint8_t *a_partial, const uint8_t *a_sm,
+    const uint8_t *b_compressed, int64_t b_compressed_bytes, const int32_t *b_offsets,
+    const uint16_t *b_states, const uint8_t *b_partial, const uint8_t *b_sm,
+    const int32_t *decode_table, uint8_t *out, int64_t n_streams, int64_t n_fp8_per_stream,
+    int64_t stream_begin, int64_t stream_end, int32_t *status, void *stream) {
     tans_b200::clear_error();
     if (n_fp8_per_stream < 0 || n_fp8_per_stream % 16 != 0)
         return fail(TANS_B200_ERR_INVALID, "n_fp8_per_stream must be divisible by 16");
@@ -1235,7 +1302,13 @@ extern "C" int tans_b200_fp8_vecadd_fused(
         return fail(TANS_B200_ERR_INVALID,
                     "compressed tensors must have byte lengths divisible by 4");
     if (n_streams < 0) return fail(TANS_B200_ERR_INVALID, "n_streams must be >= 0");
-    if (n_streams == 0 || n_fp8_per_stream == 0) return TANS_B200_OK;
+    if (stream_begin < 0 || stream_begin % kBlk != 0 || stream_end < stream_begin ||
+        stream_end > n_streams)
+        return fail(TANS_B200_ERR_INVALID,
+                    "fp8_vecadd_fused: stream range [%lld, %lld) must start on a 128-stream "
+                    "block and lie in [0, %lld]",
+                    (long long)stream_begin, (long long)stream_end, (long long)n_streams);
+    if (n_streams == 0 || n_fp8_per_stream == 0 || stream_end == stream_begin) return TANS_B200_OK;
     if (!a_compressed || !a_offsets || !a_states || !a_partial || !a_sm || !b_compressed ||
         !b_offsets || !b_states || !b_partial || !b_sm || !decode_table || !out)
         return fail(TANS_B200_ERR_INVALID, "fp8_vecadd_fused: null pointer");
@@ -1247,17 +1320,22 @@ extern "C" int tans_b200_fp8_vecadd_fused(
     int sms;
     int rc = device_setup(&sms);
     if (rc) return rc;
+    // a range is the full layout seen from its first stream: per-stream and
+    // per-block arrays start there, tiles keep the full row stride
+    const int64_t s0 = stream_begin, b0 = stream_begin / kBlk;
     FusedArgs args{reinterpret_cast<const uint32_t *>(a_compressed),
                    reinterpret_cast<const uint32_t *>(b_compressed),
-                   a_compressed_bytes, b_compressed_bytes, a_offsets, b_offsets, a_states,
-                   b_states, a_partial, b_partial, a_sm, b_sm, decode_table, out, n_streams,
-                   n_fp8_per_stream, status, make_opq()};
+                   a_compressed_bytes, b_compressed_bytes, a_offsets + b0, b_offsets + b0,
+                   a_states + s0, b_states + s0, a_partial + s0, b_partial + s0, a_sm + 8 * s0,
+                   b_sm + 8 * s0, decode_table, out + 16 * s0, stream_end - stream_begin,
+                   n_fp8_per_stream, n_streams, status, make_opq()};
     cudaStream_t st = (cudaStream_t)stream;
+    const int64_t n_range = stream_end - stream_begin;
     switch (ring_rows(n_fp8_per_stream / 2)) {
-        case 16: return launch_fused_split<16>(args, n_streams, sms, st);
-        case 32: return launch_fused_split<32>(args, n_streams, sms, st);
-        case 64: return launch_fused_split<64>(args, n_streams, sms, st);
-        default: return launch_fused_split<128>(args, n_streams, sms, st);
+        case 16: return launch_fused_split<16>(args, n_range, sms, st);
+        case 32: return launch_fused_split<32>(args, n_range, sms, st);
+        case 64: return launch_fused_split<64>(args, n_range, sms, st);
+        default: return launch_fused_split<128>(args, n_range, sms, st);
     }
 }
 

@@ -333,5 +333,68 @@ def fp8_vecadd_fused_tans(a_comp: torch.Tensor, a_offsets: torch.Tensor,
     return out
 
 
+_host_ws: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def fp8_vecadd_fused_tans_host(a_comp: torch.Tensor, a_offsets: torch.Tensor,
+                               a_states: torch.Tensor, a_partial: torch.Tensor,
+                               a_sm: torch.Tensor, b_comp: torch.Tensor,
+                               b_offsets: torch.Tensor, b_states: torch.Tensor,
+                               b_partial: torch.Tensor, b_sm: torch.Tensor,
+                               decode_tbl: torch.Tensor, n_fp8_per_stream: int,
+                               out: torch.Tensor | None = None,
+                               device: torch.device | int | None = None,
+                               chunk_streams: int = 0) -> torch.Tensor:
+    """fp8_vecadd_fused_tans on HOST tensors (no reference counterpart): the
+    inputs are copied to `device` in chunks of encoder blocks and the tiled
+    output [N/16 * K * 16] is copied back into `out` (a host tensor; pinned
+    if allocated here), with copies and kernels pipelined over three CUDA
+    streams.  Asynchronous with respect to the host, like a non-blocking
+    copy: synchronise the device's current stream before reading `out`.
+    Page-locked inputs are needed for the copies to overlap."""
+    ts = (a_comp, a_offsets, a_states, a_partial, a_sm, b_comp, b_offsets, b_states, b_partial,
+          b_sm, decode_tbl)
+    for t in ts:
+        _req(not t.is_cuda and t.is_contiguous(), "host inputs must be contiguous CPU tensors")
+    _req(a_states.dtype == torch.uint16 and b_states.dtype == torch.uint16, "states must be uint16")
+    _req(a_offsets.dtype == torch.int32 and b_offsets.dtype == torch.int32, "offsets must be int32")
+    _req(decode_tbl.dtype == torch.int32 and decode_tbl.numel() == _L,
+         f"decode_tbl must be {_L} int32 entries")
+    N = int(n_fp8_per_stream)
+    _req(N % (2 * _TILE_PAIRS) == 0, f"n_fp8_per_stream must be divisible by {2 * _TILE_PAIRS}")
+    K = a_states.numel()
+    _req(b_states.numel() == K, "A/B stream counts must match")
+    nb = (K + _BLOCK - 1) // _BLOCK
+    _req(a_offsets.numel() == nb + 1 and b_offsets.numel() == nb + 1,
+         "offset tensors must have n_encoder_blocks + 1 entries")
+    _req(a_partial.numel() == K and b_partial.numel() == K, "partial-count tensors must match")
+    _req(a_sm.numel() == K * N // 2 and b_sm.numel() == K * N // 2,
+         "sign/mantissa tensors have the wrong tiled size")
+    dev = torch.device("cuda", torch.cuda.current_device() if device is None else
+                       (device if isinstance(device, int) else device.index or 0))
+    if out is None:
+        out = torch.empty(K * N, dtype=torch.uint8, pin_memory=True)
+    _req(not out.is_cuda and out.is_contiguous() and out.numel() == K * N and
+         out.dtype == torch.uint8, "out must be a contiguous CPU uint8 tensor of K*N bytes")
+    with torch.cuda.device(dev):
+        need = ctypes.c_int64()
+        check(LIB.tans_b200_fp8_vecadd_fused_host_workspace_bytes(
+            K, N, a_comp.numel(), b_comp.numel(), ctypes.byref(need)))
+        key = (dev.index, need.value)
+        ws = _host_ws.get(key)
+        if ws is None:
+            _host_ws.clear()
+            ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
+            _host_ws[key] = ws
+        check(LIB.tans_b200_fp8_vecadd_fused_host(
+            a_comp.data_ptr(), a_comp.numel(), a_offsets.data_ptr(), a_states.data_ptr(),
+            a_partial.data_ptr(), a_sm.data_ptr(),
+            b_comp.data_ptr(), b_comp.numel(), b_offsets.data_ptr(), b_states.data_ptr(),
+            b_partial.data_ptr(), b_sm.data_ptr(), decode_tbl.data_ptr(), out.data_ptr(), K, N,
+            int(chunk_streams), ws.data_ptr(), ws.numel(), _status(dev).data_ptr(), _stream(dev)))
+    return out
+
+
 __all__ = ["tans_encode_interleaved", "gpu_tans_decode", "fp8_memcpy", "fp8_vecadd_raw",
-           "fp8_vecadd_fused_tans", "build_decode_table_device", "data_status"]
+           "fp8_vecadd_fused_tans", "fp8_vecadd_fused_tans_host", "build_decode_table_device",
+           "data_status", "encode_device"]

@@ -46,6 +46,12 @@ def _load() -> ctypes.CDLL:
                                              i64, i64, p, p]),
         "tans_b200_decode_noalloc": (i32, [p, i64, p, p, p, p, p, p, i64, p, i64, i64, p, p]),
         "tans_b200_gemv": (i32, [p, i64, p, p, p, p, p, p, p, p, p, i64, i64, i64, i64, p, p]),
+        "tans_b200_fp8_vecadd_fused_range": (i32, [p, i64, p, p, p, p, p, i64, p, p, p, p, p, p,
+                                                   i64, i64, i64, i64, p, p]),
+        "tans_b200_fp8_vecadd_fused_host_workspace_bytes": (i32, [i64, i64, i64, i64,
+                                                                  ctypes.POINTER(i64)]),
+        "tans_b200_fp8_vecadd_fused_host": (i32, [p, i64, p, p, p, p, p, i64, p, p, p, p, p, p,
+                                                  i64, i64, i64, p, i64, p, p]),
         "tans_b200_encode_device_workspace_bytes": (i32, [i64, ctypes.POINTER(i64)]),
         "tans_b200_encode_device_plan": (i32, [p, i32, i64, i64, i64, p, i64, p, p, p, p, p, p]),
         "tans_b200_encode_device_emit": (i32, [p, i32, i64, i64, p, p, p, p, p]),
