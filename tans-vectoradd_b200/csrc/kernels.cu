@@ -743,24 +743,29 @@ __device__ __forceinline__ void ring_copy4(uint32_t base, uint32_t f, uint32_t w
         : "memory");
 }
 
-// Ring upkeep for a warp with one chain, once per kTiles tiles: up to
-// 2 * kTiles rows filled (never over a slot the slowest lane still needs),
-// and a warp vote on whether every row any lane can reach in the next
-// kTiles tiles (at most 3 * kTiles refills: rows row .. row - (3 kTiles - 1))
-// is already complete.
-template <int R, int kTiles, int kLag>
-__device__ __forceinline__ bool ring_tile(Ring &rg, const Chain &ch, bool live) {
-    static_assert(kTiles == 1 || kTiles == 2, "ring upkeep covers one or two tiles");
+// Warp vote: may every lane refill from the ring for the next tile?  Each
+// row a lane can reach in one tile (at most 3 refills: rows row .. row - 2)
+// must belong to a fill group that cp.async.wait_group has completed
+// (frontier done[kLag]).
+template <int kLag>
+__device__ __forceinline__ bool ring_vote(const Ring &rg, const Chain &ch, bool live) {
     static_assert(kLag >= 1 && kLag <= kRingLag, "lag beyond the recorded fill frontiers");
     const int32_t row = ch.v >> 7;
+    return __all_sync(0xffffffffu, !live || max(row - 2, 0) >= rg.done[kLag]);
+}
+
+// Ring fill for a warp with one chain: up to kMaxRows rows (never over a
+// slot the slowest lane still needs); shifts the frontier history.  The
+// caller commits the group.
+template <int R, int kMaxRows>
+__device__ __forceinline__ void ring_refill(Ring &rg, const Chain &ch, bool live) {
+    static_assert(kMaxRows == 2 || kMaxRows == 4, "two or four row copies per fill");
+    const int32_t row = ch.v >> 7;
     const int32_t r_slow = __reduce_max_sync(0xffffffffu, live ? row : kNoRow);
-    const bool fast =
-        __all_sync(0xffffffffu, !live || max(row - (3 * kTiles - 1), 0) >= rg.done[kLag]);
     int32_t n = min(rg.fill + 1, rg.fill - (r_slow - R));
-    n = max(min(n, kRingPerTile * kTiles), 0);
+    n = max(min(n, kMaxRows), 0);
     const uint32_t f = (uint32_t)rg.fill;
-    static_assert(kRingPerTile * kTiles <= 4, "at most four row copies per upkeep");
-    if (kRingPerTile * kTiles <= 2)
+    if (kMaxRows == 2)
         ring_copy2(rg.lane_base + ((f & (R - 1)) << 7), rg.lane_base + (((f - 1) & (R - 1)) << 7),
                    ch.src + (int64_t)rg.fill * kBlk, n, live);
     else
@@ -769,12 +774,12 @@ __device__ __forceinline__ bool ring_tile(Ring &rg, const Chain &ch, bool live) 
 #pragma unroll
     for (int i = kRingLag; i > 0; i--) rg.done[i] = rg.done[i - 1];
     rg.done[0] = rg.fill + 1;
-    return fast;
 }
 
-// Tiles between ring upkeeps in the fused kernel, and how many upkeeps old a
-// fill group must be before its rows are read (cp.async.wait_group depth).
-constexpr int kFusedUpkeepTiles = 1;
+// Fused kernel ring schedule: a fill of up to kRingPerTile rows per tile
+// every kFusedFillTiles tiles, and the fast/slow vote every tile against
+// the frontier of the fill kFusedLag fills back (cp.async.wait_group depth).
+constexpr int kFusedFillTiles = 2;
 constexpr int kFusedLag = 1;
 
 template <int R>
@@ -830,17 +835,17 @@ __global__ void __launch_bounds__(kSplitMaxPairs * 64, 1) fused_split_kernel(con
         uint8_t *op = p.out + sid * 16 + 8 * side;
         uint2 m_n = make_uint2(0, 0);
         if (live && n_tiles > 0) m_n = ld_stream_v2(sp);
-        bool fast = false;
         for (int32_t t = 0; t < n_tiles; t++) {
             const uint2 m = m_n;
             sp += tstep;
             if (live && t + 1 < n_tiles) m_n = ld_stream_v2(sp);
             if (live && t + 4 < n_tiles) prefetch_l2(sp + 3 * tstep);
-            if (t % kFusedUpkeepTiles == 0) {
-                fast = ring_tile<R, kFusedUpkeepTiles, kFusedLag>(rg, ch, live);
+            if (t % kFusedFillTiles == 0) {
+                ring_refill<R, kRingPerTile * kFusedFillTiles>(rg, ch, live);
                 cp_async_commit();
                 cp_async_wait<kFusedLag>();
             }
+            const bool fast = ring_vote<kFusedLag>(rg, ch, live);
             uint32_t e[kTablePairs];
             if (fast) {
 #pragma unroll
