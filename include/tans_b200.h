@@ -254,20 +254,24 @@ int tans_b200_decode_noalloc(const uint8_t *compressed, int64_t compressed_bytes
  *   TANS_B200_ENC_INPUT_SYMBOLS  in = pair symbols [K][n] (sm_out unused).
  *
  * Sequence (the caller allocates between the calls):
- *   1. tans_b200_encode_device_workspace_bytes(K, &bytes); allocate a device
- *      workspace of that size (256-byte aligned);
+ *   1. tans_b200_encode_device_workspace_bytes(K, n, kind, &bytes); allocate
+ *      a device workspace of that size (256-byte aligned): tables, per-stream
+ *      slab counts and a staging area of ceil(13 P / 32) slab rows per
+ *      encoder block (P = symbols per stream), about 0.8 bytes per FP8 byte;
  *   2. tans_b200_encode_device_plan(...): validates freqs/spread on the host
- *      (same checks and messages as tans_b200_encode), then enqueues pass 1:
- *      sm_out, states_out[K] and offsets_out[B+1] are written and the
- *      workspace header (tans_b200_enc_header at workspace offset 0) gets
- *      total_bytes and error bits;
+ *      (same checks and messages as tans_b200_encode), then enqueues the
+ *      encode: sm_out, states_out[K], partial_out[K] and offsets_out[B+1]
+ *      are written, the slabs are staged in the workspace, and the workspace
+ *      header (tans_b200_enc_header at workspace offset 0) gets total_bytes
+ *      and error bits;
  *   3. the caller reads the header (16 bytes, device -> host); error_bits
  *      TANS_B200_ENC_BAD_SYMBOL: a symbol with zero frequency occurs (the
  *      smallest one is bad_symbol); TANS_B200_ENC_TOO_LARGE: the compressed
  *      size exceeds the format's int32 offsets;
  *   4. with no error bits, allocate compressed[total_bytes] and call
- *      tans_b200_encode_device_emit(...), which writes compressed and
- *      partial_out[K].  (With error bits set the emit kernel writes nothing.)
+ *      tans_b200_encode_device_emit(...), which places the staged slabs
+ *      (every byte of compressed is written).  With error bits set it writes
+ *      nothing.
  * freqs[n_syms] and spread[4096] are HOST pointers.  Streams are limited to
  * 357,913,941 symbols (32-bit per-stream bit counts). */
 #define TANS_B200_ENC_INPUT_FP8 0
@@ -281,20 +285,21 @@ typedef struct tans_b200_enc_header {
     int64_t total_bytes; /* compressed bytes = offsets[B] */
 } tans_b200_enc_header;
 
-int tans_b200_encode_device_workspace_bytes(int64_t n_streams, int64_t *bytes);
+int tans_b200_encode_device_workspace_bytes(int64_t n_streams,
+                                            int64_t n_per_stream,
+                                            int input_kind, int64_t *bytes);
 
 int tans_b200_encode_device_plan(const uint8_t *in, int input_kind,
                                  int64_t n_streams, int64_t n_per_stream,
                                  int64_t tile, const int32_t *freqs,
                                  int64_t n_syms, const int32_t *spread,
                                  uint8_t *sm_out, uint16_t *states_out,
-                                 int32_t *offsets_out, void *workspace,
-                                 void *stream);
+                                 uint8_t *partial_out, int32_t *offsets_out,
+                                 void *workspace, void *stream);
 
-int tans_b200_encode_device_emit(const uint8_t *in, int input_kind,
-                                 int64_t n_streams, int64_t n_per_stream,
-                                 const int32_t *offsets, const void *workspace,
-                                 uint8_t *compressed, uint8_t *partial_out,
+int tans_b200_encode_device_emit(int input_kind, int64_t n_streams,
+                                 int64_t n_per_stream, const int32_t *offsets,
+                                 const void *workspace, uint8_t *compressed,
                                  void *stream);
 
 #ifdef __cplusplus

@@ -8,27 +8,36 @@
 // Work split.  The format is serial inside a stream (each step's state
 // depends on the previous one) and independent across streams, so one
 // thread encodes one stream and a CTA of 128 threads is one encoder block.
-// The block layout (slab count G_b of every block, top-aligned streams) must
-// be known before any slab can be placed, so the encoder runs the state
-// machine twice:
+// Slabs are top-aligned in their block, so a stream's first slab index
+// depends on its block's longest stream, which is only known once every
+// stream of the block is encoded.  The encoder therefore runs the state
+// machine once, into a staging area, and places the slabs afterwards:
 //   enc_setup_kernel  copies the alphabet tables into the workspace;
-//   enc_count_kernel  pass 1: reads the input back to front, writes the
-//                     sign/mantissa bytes (FP8 input), the final state and
-//                     the slab count of every stream and G_b of its block;
+//   enc_stage_kernel  reads the input back to front, writes the
+//                     sign/mantissa bytes (FP8 input), the final state, the
+//                     partial-slab bit count, and every completed slab into
+//                     the stream's staging column bottom-up; records each
+//                     stream's slab count and its block's G_b;
 //   enc_scan_kernel   exclusive scan of G_b * 512 into the int32 offsets;
-//   enc_emit_kernel   pass 2: re-runs the state machine and stores every
-//                     completed slab straight into its final slot (zero slabs
-//                     below a short stream are written too, so the output
-//                     needs no memset).
-// The host reads the 16-byte workspace header between the two calls to size
-// the compressed buffer.
+//   enc_place_kernel  copies each block's staging rows to their top-aligned
+//                     rows of the output, destination row by destination row
+//                     (coalesced 512-byte stores), zeroing the rows below
+//                     short streams and the unused columns of a partial last
+//                     block, so the output needs no memset.
+// The host reads the 16-byte workspace header between the scan and the
+// placement to size the compressed buffer.  Staging holds ceil(13 P / 32)
+// rows per block (13 bits bound every step, the error marker included).
 //
 // Step (pair symbol s, state x in [4096, 8192), tables in shared memory):
-//     k  = (x + delta[s]) >> 16          bits to emit
+//     k  = (x + delta[s]) >> 13          bits to emit
 //     emit x & (2^k - 1), LSB-first
 //     x  = next[base[s] + (x >> k)]
-// delta/base depend only on s, so their lookup is off the x dependency
-// chain; the chain is add, shift, shift, address, one 16-bit shared load.
+// delta and base of a symbol share one 32-bit word (delta << 14 | base as a
+// 14-bit two's-complement field), kept in 4 copies interleaved by word so
+// that lane l reads copy l % 4: one 4-byte random lookup per step instead
+// of an 8-byte one, with fewer bank conflicts.  The word depends only on s,
+// so its lookup is off the x dependency chain; the chain is add, shift,
+// shift, address, one 16-bit shared load.
 
 #include "../../include/tans_b200.h"
 #include "internal.h"
@@ -48,12 +57,24 @@ constexpr int kBlk = TANS_B200_BLOCK_STREAMS;
 constexpr int kScanThreads = 1024;
 
 // Workspace layout (bytes).  The header is the public tans_b200_enc_header.
-constexpr size_t kWsInfo = 16;                    // int2[256] {delta, base}
-constexpr size_t kWsNext = kWsInfo + 256 * 8;     // uint16[4096]
-constexpr size_t kWsSlabs = 10496;                // uint32[K]: slabs per stream
+constexpr int kInfoCopies = 4;
+constexpr size_t kWsInfo = 16;                                 // uint32[256][4] packed delta/base
+constexpr size_t kWsNext = kWsInfo + 256 * 4 * kInfoCopies;    // uint16[4096]
+constexpr size_t kWsSlabs = 12544;                             // uint32[K]: slabs per stream
 static_assert(kWsNext + kL * 2 <= kWsSlabs, "workspace tables overlap");
 
-__host__ __device__ __forceinline__ size_t ws_blocks_offset(int64_t K) { return (kWsSlabs + 4 * (size_t)K + 255) & ~(size_t)255; }
+__host__ __device__ __forceinline__ size_t ws_blocks_offset(int64_t K) {
+    return (kWsSlabs + 4 * (size_t)K + 255) & ~(size_t)255;
+}
+__host__ __device__ __forceinline__ size_t ws_stage_offset(int64_t K) {
+    const int64_t B = (K + kBlk - 1) / kBlk;
+    return (ws_blocks_offset(K) + 4 * (size_t)B + 4 + 255) & ~(size_t)255;
+}
+// Staging rows per block: every step emits at most 13 bits.
+__host__ __device__ __forceinline__ int64_t stage_rows(int64_t P) {
+    const int64_t g = (13 * P + 31) / 32;
+    return g > 0 ? g : 1;
+}
 
 struct EncArgs {
     const uint8_t *in;    // FP8 bytes [K][2P] or pair symbols [K][P]
@@ -68,6 +89,7 @@ struct EncArgs {
     uint8_t *compressed;
     uint8_t *partial;
     uint8_t *ws;
+    int64_t gmax;         // staging rows per block
 };
 
 __device__ __forceinline__ tans_b200_enc_header *header(uint8_t *ws) {
@@ -107,42 +129,38 @@ __device__ __forceinline__ uint32_t sm_pairs_of(uint32_t w) {
 __device__ __forceinline__ uint32_t byte_of(uint32_t w, int j) { return (w >> (8 * j)) & 0xFFu; }
 
 struct EncTables {
-    const int2 *info;
+    const uint32_t *info;  // this lane's copy: entry s at info[4 * s]
     const uint16_t *next;
 };
 
-// Pass-1 state: state, bit count and the largest k seen (13 marks a symbol
-// that cannot be coded).
-struct Counter {
-    uint32_t x, bits, kmax;
-    __device__ __forceinline__ void step(const EncTables &t, uint32_t s) {
-        const int2 inf = t.info[s];
-        const uint32_t k = (x + (uint32_t)inf.x) >> 16;
-        bits += k;
-        kmax = max(kmax, k);
-        x = t.next[inf.y + (int32_t)(x >> k)];
-    }
-};
+__device__ __forceinline__ int32_t info_delta(uint32_t w) { return (int32_t)w >> 14; }
+__device__ __forceinline__ int32_t info_base(uint32_t w) {
+    int32_t b;
+    asm("bfe.s32 %0, %1, 0, 14;" : "=r"(b) : "r"(w));
+    return b;
+}
 
-// Pass-2 state: state plus the pending slab lo (fill bits) and a running
-// pointer to the next slab slot of this stream (stride 512 bytes).
+// Encoder state: state x, the pending slab lo (fill bits), the largest k
+// seen (13 marks a symbol that cannot be coded) and a running pointer to the
+// next slab slot of this stream's staging column (stride 512 bytes).
 struct Emitter {
-    uint32_t x, lo, fill;
+    uint32_t x, lo, fill, kmax;
     uint32_t *out;
     __device__ __forceinline__ void step(const EncTables &t, uint32_t s) {
-        const int2 inf = t.info[s];
-        const uint32_t k = (x + (uint32_t)inf.x) >> 16;
+        const uint32_t w = t.info[kInfoCopies * s];
+        const uint32_t k = (uint32_t)((int32_t)x + info_delta(w)) >> 13;
         const uint32_t v = x & ((1u << k) - 1u);
         const uint32_t hi = __funnelshift_l(v, 0u, fill);  // bits that spill past 32
         lo |= v << fill;
         fill += k;
+        kmax = max(kmax, k);
         if (fill >= 32) {
             *out = lo;
             out += kBlk;
             lo = hi;
             fill -= 32;
         }
-        x = t.next[inf.y + (int32_t)(x >> k)];
+        x = t.next[info_base(w) + (int32_t)(x >> k)];
     }
 };
 
@@ -219,13 +237,13 @@ __device__ __forceinline__ void run_stream(const EncArgs &a, const EncTables &t,
 }
 
 __device__ __forceinline__ EncTables load_tables(uint8_t *smem, const uint8_t *ws) {
-    // 2 KB of {delta, base} and 8 KB of next states, copied as 16-byte words
+    // 4 KB of packed delta/base words and 8 KB of next states, 16-byte copies
     const uint4 *src = reinterpret_cast<const uint4 *>(ws + kWsInfo);
     uint4 *dst = reinterpret_cast<uint4 *>(smem);
     for (int i = threadIdx.x; i < (int)((kWsNext - kWsInfo + kL * 2) / 16); i += blockDim.x)
         dst[i] = src[i];
     __syncthreads();
-    return EncTables{reinterpret_cast<const int2 *>(smem),
+    return EncTables{reinterpret_cast<const uint32_t *>(smem) + (threadIdx.x % kInfoCopies),
                      reinterpret_cast<const uint16_t *>(smem + (kWsNext - kWsInfo))};
 }
 
@@ -239,26 +257,36 @@ __global__ void enc_setup_kernel(const __grid_constant__ EncoderTables t, uint8_
         h->bad_symbol = INT_MAX;
         h->total_bytes = 0;
     }
-    int2 *info = reinterpret_cast<int2 *>(ws + kWsInfo);
-    for (int s = i; s < 256; s += blockDim.x) info[s] = make_int2(t.delta[s], t.base[s]);
+    uint32_t *info = reinterpret_cast<uint32_t *>(ws + kWsInfo);
+    for (int s = i; s < 256; s += blockDim.x) {
+        const uint32_t w = ((uint32_t)t.delta[s] << 14) | ((uint32_t)t.base[s] & 0x3FFFu);
+        for (int c = 0; c < kInfoCopies; c++) info[kInfoCopies * s + c] = w;
+    }
     uint16_t *next = reinterpret_cast<uint16_t *>(ws + kWsNext);
     for (int j = i; j < kL; j += blockDim.x) next[j] = t.next[j];
 }
 
 template <bool kFp8>
-__global__ void __launch_bounds__(kBlk) enc_count_kernel(const EncArgs a) {
+__global__ void __launch_bounds__(kBlk, 8) enc_stage_kernel(const EncArgs a) {
     __shared__ __align__(16) uint8_t smem[kTableSmem];
     __shared__ uint32_t warp_max[kBlk / 32];
     const EncTables t = load_tables(smem, a.ws);
     const int64_t k = (int64_t)blockIdx.x * kBlk + threadIdx.x;
     uint32_t slabs = 0;
     if (k < a.K) {
-        Counter c{(uint32_t)kL, 0u, 0u};
-        run_stream<kFp8, true>(a, t, k, c);
-        a.states[k] = (uint16_t)c.x;
-        slabs = (c.bits + 31) >> 5;
+        uint32_t *col = reinterpret_cast<uint32_t *>(a.ws + ws_stage_offset(a.K)) +
+                        (int64_t)blockIdx.x * a.gmax * kBlk + threadIdx.x;
+        Emitter e{(uint32_t)kL, 0u, 0u, 0u, col};
+        run_stream<kFp8, true>(a, t, k, e);
+        if (e.fill > 0) {
+            *e.out = e.lo;
+            e.out += kBlk;
+        }
+        a.states[k] = (uint16_t)e.x;
+        a.partial[k] = (uint8_t)e.fill;
+        slabs = (uint32_t)((e.out - col) / kBlk);
         slabs_of(a.ws)[k] = slabs;
-        if (c.kmax >= (uint32_t)tans_b200::kEncoderBadBits) {
+        if (e.kmax >= (uint32_t)tans_b200::kEncoderBadBits) {
             // error path: find the symbols that have no slot and report the smallest
             tans_b200_enc_header *h = header(a.ws);
             atomicOr(&h->error_bits, TANS_B200_ENC_BAD_SYMBOL);
@@ -269,7 +297,8 @@ __global__ void __launch_bounds__(kBlk) enc_count_kernel(const EncArgs a) {
                     s = (((row[2 * i] >> 3) & 15u) << 4) | ((row[2 * i + 1] >> 3) & 15u);
                 else
                     s = row[i];
-                if (t.info[s].x == (tans_b200::kEncoderBadBits << 16)) atomicMin(&h->bad_symbol, (int)s);
+                if (info_delta(t.info[kInfoCopies * s]) == (tans_b200::kEncoderBadBits << 13))
+                    atomicMin(&h->bad_symbol, (int)s);
             }
         }
     }
@@ -329,24 +358,23 @@ __global__ void __launch_bounds__(kScanThreads) enc_scan_kernel(const EncArgs a,
     }
 }
 
-template <bool kFp8>
-__global__ void __launch_bounds__(kBlk) enc_emit_kernel(const EncArgs a) {
-    __shared__ __align__(16) uint8_t smem[kTableSmem];
-    const EncTables t = load_tables(smem, a.ws);
+// Destination row r of stream t's column holds staging row r - (G_b - G_s)
+// (zero below it): stores walk the output row by row, 512 contiguous bytes
+// per row and block; the staging reads of a warp fall in a few rows.
+__global__ void __launch_bounds__(kBlk) enc_place_kernel(const EncArgs a) {
     if (header(a.ws)->error_bits != 0) return;  // layout not valid: write nothing
     const int64_t k = (int64_t)blockIdx.x * kBlk + threadIdx.x;
     const int64_t off = a.offsets[blockIdx.x];
-    const uint32_t g_b = (uint32_t)((a.offsets[blockIdx.x + 1] - off) / (kBlk * 4));
-    // columns past the last stream of a partial block are zero, like the slabs
-    // below a short stream
-    const uint32_t g_s = k < a.K ? slabs_of(a.ws)[k] : 0u;
-    uint32_t *out = reinterpret_cast<uint32_t *>(a.compressed + off) + threadIdx.x;
-    for (uint32_t g = g_s; g < g_b; g++, out += kBlk) *out = 0u;  // slabs below a short stream
-    if (k >= a.K) return;
-    Emitter e{(uint32_t)kL, 0u, 0u, out};
-    run_stream<kFp8, false>(a, t, k, e);
-    if (e.fill > 0) *e.out = e.lo;
-    a.partial[k] = (uint8_t)e.fill;
+    const int32_t g_b = (int32_t)((a.offsets[blockIdx.x + 1] - off) / (kBlk * 4));
+    const int32_t g_s = k < a.K ? (int32_t)slabs_of(a.ws)[k] : 0;
+    const int32_t shift = g_b - g_s;
+    const uint32_t *src = reinterpret_cast<const uint32_t *>(a.ws + ws_stage_offset(a.K)) +
+                          (int64_t)blockIdx.x * a.gmax * kBlk + threadIdx.x;
+    uint32_t *dst = reinterpret_cast<uint32_t *>(a.compressed + off) + threadIdx.x;
+    for (int32_t r = 0; r < g_b; r++) {
+        const int32_t g = r - shift;
+        dst[(int64_t)r * kBlk] = g >= 0 ? src[(int64_t)g * kBlk] : 0u;
+    }
 }
 
 int launch_status(const char *what) {
@@ -375,11 +403,15 @@ int check_shape(int input_kind, int64_t K, int64_t n, int64_t *P) {
 
 }  // namespace
 
-extern "C" int tans_b200_encode_device_workspace_bytes(int64_t K, int64_t *bytes) {
+extern "C" int tans_b200_encode_device_workspace_bytes(int64_t K, int64_t n, int input_kind,
+                                                       int64_t *bytes) {
     tans_b200::clear_error();
-    if (K < 0 || !bytes) return fail(TANS_B200_ERR_INVALID, "encode_device_workspace_bytes: bad arguments");
+    if (!bytes) return fail(TANS_B200_ERR_INVALID, "encode_device_workspace_bytes: bytes is null");
+    int64_t P;
+    int rc = check_shape(input_kind, K, n, &P);
+    if (rc) return rc;
     const int64_t B = (K + kBlk - 1) / kBlk;
-    *bytes = (int64_t)ws_blocks_offset(K) + 4 * B + 4;
+    *bytes = (int64_t)ws_stage_offset(K) + B * stage_rows(P) * kBlk * 4;
     return TANS_B200_OK;
 }
 
@@ -387,7 +419,8 @@ extern "C" int tans_b200_encode_device_plan(const uint8_t *in, int input_kind, i
                                             int64_t n, int64_t tile, const int32_t *freqs,
                                             int64_t n_syms, const int32_t *spread,
                                             uint8_t *sm_out, uint16_t *states_out,
-                                            int32_t *offsets_out, void *workspace, void *stream) {
+                                            uint8_t *partial_out, int32_t *offsets_out,
+                                            void *workspace, void *stream) {
     tans_b200::clear_error();
     int64_t P;
     int rc = check_shape(input_kind, K, n, &P);
@@ -397,7 +430,7 @@ extern "C" int tans_b200_encode_device_plan(const uint8_t *in, int input_kind, i
     if (fp8 && tile > 0 && P % tile != 0)
         return fail(TANS_B200_ERR_INVALID, "n_pairs=%lld not divisible by tile=%lld", (long long)P,
                     (long long)tile);
-    if (!workspace || !offsets_out || (K > 0 && !states_out) ||
+    if (!workspace || !offsets_out || (K > 0 && (!states_out || !partial_out)) ||
         (K > 0 && P > 0 && (!in || (fp8 && !sm_out))))
         return fail(TANS_B200_ERR_INVALID, "encode_device: null pointer");
     if (!aligned(workspace, 256) || !aligned(offsets_out, 4) || !aligned(states_out, 2))
@@ -405,11 +438,12 @@ extern "C" int tans_b200_encode_device_plan(const uint8_t *in, int input_kind, i
     EncoderTables tables;
     rc = tans_b200::encoder_tables(freqs, n_syms, spread, &tables);
     if (rc) return rc;
+    const int64_t B = (K + kBlk - 1) / kBlk;
+    if (B > INT_MAX) return fail(TANS_B200_ERR_INVALID, "encode_device: too many streams");
     cudaStream_t st = (cudaStream_t)stream;
     uint8_t *ws = static_cast<uint8_t *>(workspace);
     enc_setup_kernel<<<1, 256, 0, st>>>(tables, ws);
     if ((rc = launch_status("enc_setup_kernel"))) return rc;
-    const int64_t B = (K + kBlk - 1) / kBlk;
     EncArgs a{};
     a.in = in;
     a.K = K;
@@ -419,49 +453,42 @@ extern "C" int tans_b200_encode_device_plan(const uint8_t *in, int input_kind, i
     a.sm = sm_out;
     a.sm_vec = fp8 && tile == 8 && aligned(sm_out, 8);
     a.states = states_out;
+    a.partial = partial_out;
     a.offsets_out = offsets_out;
     a.ws = ws;
+    a.gmax = stage_rows(P);
     if (B > 0) {
-        if (B > INT_MAX) return fail(TANS_B200_ERR_INVALID, "encode_device: too many streams");
         if (fp8)
-            enc_count_kernel<true><<<(unsigned)B, kBlk, 0, st>>>(a);
+            enc_stage_kernel<true><<<(unsigned)B, kBlk, 0, st>>>(a);
         else
-            enc_count_kernel<false><<<(unsigned)B, kBlk, 0, st>>>(a);
-        if ((rc = launch_status("enc_count_kernel"))) return rc;
+            enc_stage_kernel<false><<<(unsigned)B, kBlk, 0, st>>>(a);
+        if ((rc = launch_status("enc_stage_kernel"))) return rc;
     }
     enc_scan_kernel<<<1, kScanThreads, 0, st>>>(a, B);
     return launch_status("enc_scan_kernel");
 }
 
-extern "C" int tans_b200_encode_device_emit(const uint8_t *in, int input_kind, int64_t K,
-                                            int64_t n, const int32_t *offsets,
-                                            const void *workspace, uint8_t *compressed,
-                                            uint8_t *partial_out, void *stream) {
+extern "C" int tans_b200_encode_device_emit(int input_kind, int64_t K, int64_t n,
+                                            const int32_t *offsets, const void *workspace,
+                                            uint8_t *compressed, void *stream) {
     tans_b200::clear_error();
     int64_t P;
     int rc = check_shape(input_kind, K, n, &P);
     if (rc) return rc;
     if (K == 0) return TANS_B200_OK;
-    if (!workspace || !offsets || !compressed || !partial_out || (P > 0 && !in))
+    if (!workspace || !offsets || !compressed)
         return fail(TANS_B200_ERR_INVALID, "encode_device: null pointer");
     if (!aligned(workspace, 256) || !aligned(offsets, 4) || !aligned(compressed, 4))
         return fail(TANS_B200_ERR_INVALID, "encode_device: misaligned compressed or workspace");
-    const bool fp8 = input_kind == TANS_B200_ENC_INPUT_FP8;
     const int64_t B = (K + kBlk - 1) / kBlk;
     if (B > INT_MAX) return fail(TANS_B200_ERR_INVALID, "encode_device: too many streams");
     EncArgs a{};
-    a.in = in;
     a.K = K;
     a.P = P;
-    a.vec = fp8 ? (aligned(in, 16) && (2 * P) % 16 == 0) : (aligned(in, 8) && P % 8 == 0);
     a.offsets = offsets;
     a.compressed = compressed;
-    a.partial = partial_out;
     a.ws = static_cast<uint8_t *>(const_cast<void *>(workspace));
-    cudaStream_t st = (cudaStream_t)stream;
-    if (fp8)
-        enc_emit_kernel<true><<<(unsigned)B, kBlk, 0, st>>>(a);
-    else
-        enc_emit_kernel<false><<<(unsigned)B, kBlk, 0, st>>>(a);
-    return launch_status("enc_emit_kernel");
+    a.gmax = stage_rows(P);
+    enc_place_kernel<<<(unsigned)B, kBlk, 0, (cudaStream_t)stream>>>(a);
+    return launch_status("enc_place_kernel");
 }

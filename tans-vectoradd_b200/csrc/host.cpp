@@ -335,12 +335,12 @@ int tans_b200::encoder_tables(const int32_t *freqs, int64_t n_syms, const int32_
     for (int s = 0; s < 256; s++) {
         const uint32_t f = s < n_syms ? static_cast<uint32_t>(freqs[s]) : 0u;
         if (f == 0) {
-            t->delta[s] = kEncoderBadBits << 16;
+            t->delta[s] = kEncoderBadBits << 13;
             t->base[s] = 0;
             continue;
         }
         const uint32_t k1 = 12u - std::min(31u - static_cast<uint32_t>(__builtin_clz(f)), 12u);
-        t->delta[s] = static_cast<int32_t>((k1 << 16) - (f << k1));
+        t->delta[s] = static_cast<int32_t>(k1 << 13) - static_cast<int32_t>(f << k1);
         t->base[s] = static_cast<int32_t>(cum[s]) - static_cast<int32_t>(f);
     }
     return TANS_B200_OK;

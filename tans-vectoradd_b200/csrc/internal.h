@@ -12,16 +12,16 @@ void clear_error();
 
 // Per-alphabet tables of the slab encoder in the form the device encoder
 // uses.  For a symbol s with frequency f = freqs[s] > 0, k1 = 12 - floor(log2 f):
-//   delta[s] = (k1 << 16) - (f << k1)   so that (x + delta) >> 16 is the
+//   delta[s] = (k1 << 13) - (f << k1)  so that (x + delta) >> 13 is the
 //            number of bits x emits before s (k1 - 1 below f << k1, else k1;
 //            the threshold rule of csrc/tans_codec.cpp:38-47 in one add and
-//            one shift);
+//            one shift: x and f << k1 both lie in [4096, 8192));
 //   base[s]  = cum[s] - f              so that next[base + (x >> k)] is the
 //            successor state (x >> k lies in [f, 2f));
 //   next[cum[s] + r] = 4096 + (slot of the r-th occurrence of s in spread).
-// A symbol outside the alphabet or with f = 0 gets delta = 13 << 16 and base 0:
-// the encoder then reads 13 bits (more than any codable symbol, which is how
-// it notices) and next[0], which stays in bounds.
+// A symbol outside the alphabet or with f = 0 gets delta = 13 << 13 and base
+// 0: the encoder then reads 13 bits (more than any codable symbol, which is
+// how it notices) and next[0], which stays in bounds.
 struct EncoderTables {
     int32_t delta[256];
     int32_t base[256];

@@ -121,9 +121,10 @@ def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: tor
     nblocks = (K + _BLOCK - 1) // _BLOCK
     with torch.cuda.device(dev):
         wsb = ctypes.c_int64()
-        check(LIB.tans_b200_encode_device_workspace_bytes(K, ctypes.byref(wsb)))
+        check(LIB.tans_b200_encode_device_workspace_bytes(K, n, kind, ctypes.byref(wsb)))
         ws = torch.empty(wsb.value, dtype=torch.uint8, device=dev)
         states = torch.empty(K, dtype=torch.uint16, device=dev)
+        partial = torch.empty(K, dtype=torch.uint8, device=dev)
         offsets = torch.empty(nblocks + 1, dtype=torch.int32, device=dev)
         sm = None
         if fp8:
@@ -132,8 +133,8 @@ def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: tor
         st = _stream(dev)
         check(LIB.tans_b200_encode_device_plan(
             inp.data_ptr(), kind, K, n, tile, fr.data_ptr(), fr.numel(), sp.data_ptr(),
-            sm.data_ptr() if sm is not None else None, states.data_ptr(), offsets.data_ptr(),
-            ws.data_ptr(), st))
+            sm.data_ptr() if sm is not None else None, states.data_ptr(), partial.data_ptr(),
+            offsets.data_ptr(), ws.data_ptr(), st))
         hdr = ws[:16].cpu()
         err, bad = (int(v) for v in hdr[:8].view(torch.int32))
         total = int(hdr[8:].view(torch.int64)[0])
@@ -142,10 +143,8 @@ def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: tor
         if err & _lib.ENC_TOO_LARGE:
             raise RuntimeError("encode: compressed size exceeds the int32 offsets of the format")
         comp = torch.empty(total, dtype=torch.uint8, device=dev)
-        partial = torch.empty(K, dtype=torch.uint8, device=dev)
-        check(LIB.tans_b200_encode_device_emit(inp.data_ptr(), kind, K, n, offsets.data_ptr(),
-                                               ws.data_ptr(), comp.data_ptr(),
-                                               partial.data_ptr(), st))
+        check(LIB.tans_b200_encode_device_emit(kind, K, n, offsets.data_ptr(), ws.data_ptr(),
+                                               comp.data_ptr(), st))
     return comp, states, offsets, partial, sm
 
 
