@@ -46,16 +46,21 @@ def parse():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--n-fp8", type=int, default=8192, help="fp8 bytes per stream")
     ap.add_argument("--elems-log2", type=int, default=29, help="log2 elements per input")
+    ap.add_argument("--working-set-gib", type=float, default=0.0,
+                    help="vecadd: size the inputs to this working set per GPU (e.g. 8) instead")
     ap.add_argument("--sweep", action="store_true", help="extra lines over stream lengths")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-chunk", type=int, default=0,
                     help="streams per pipelined chunk of the e2e call (0: K/8)")
     ap.add_argument("--out", default=None, help="also append the JSON line(s) to this file")
-    ap.add_argument("--workload", choices=["vecadd", "decode", "encode", "gemv", "stack"],
+    ap.add_argument("--workload", choices=["vecadd", "decode", "encode", "gemv", "stack", "container"],
                     default="vecadd", help="vecadd (cfg1, headline), decode (cfg2), "
                     "encode (device encoder on the cfg2 input), gemv (cfg3), "
-                    "stack (cfg4: 40-layer row-sharded GEMV + all-gather)")
+                    "stack (cfg4: 40-layer row-sharded GEMV + all-gather), "
+                    "container (save/load of encoded tensors)")
+    ap.add_argument("--container-log2", type=int, default=30,
+                    help="log2 e4m3 bytes saved and loaded by --workload container")
     ap.add_argument("--decode-log2", type=int, default=32,
                     help="log2 fp8 elements (decode, encode)")
     ap.add_argument("--layers", type=int, default=40, help="layers of the GEMV stack")
@@ -112,6 +117,35 @@ def make_workload(n: int, N: int, seed: int):
     ey = tans_codec.encode(y.view(K, N), hist, tile=8)
     tbl = tans_codec.build_decode_table(ex[6].numpy(), ex[5].numpy())
     # kernel argument order: comp, offsets, states, partial, sm
+    a = [ex[0], ex[2], ex[1], ex[3], ex[4]]
+    b = [ey[0], ey[2], ey[1], ey[3], ey[4]]
+    return x, y, a, b, tbl, K
+
+
+def make_workload_device(n: int, N: int, seed: int, dev):
+    """Large working sets: the same N(0,1)*448/absmax e4m3 inputs drawn on the
+    GPU (seeded CUDA generator, chunks of 2^28 each scaled by its own absmax),
+    exponent histogram over both, encoded with the device encoder.  Returns
+    device tensors in make_workload's order."""
+    from rans_vectoradd import tans_codec
+    g = torch.Generator(device=dev).manual_seed(seed)
+    chunk = 1 << 28
+    xy = []
+    for _ in range(2):
+        v8 = torch.empty(n, dtype=torch.uint8, device=dev)
+        for off in range(0, n, chunk):
+            m = min(chunk, n - off)
+            v = torch.randn(m, device=dev, generator=g)
+            v8[off:off + m] = (v * (448.0 / v.abs().max())).to(torch.float8_e4m3fn).view(torch.uint8)
+            del v
+        xy.append(v8)
+    x, y = xy
+    hist = (torch.bincount(((x >> 3) & 15).long(), minlength=16) +
+            torch.bincount(((y >> 3) & 15).long(), minlength=16)).cpu().double()
+    K = n // N
+    ex = tans_codec.encode(x.view(K, N), hist, tile=8)
+    ey = tans_codec.encode(y.view(K, N), hist, tile=8)
+    tbl = tans_codec.build_decode_table(ex[6].numpy(), ex[5].numpy())
     a = [ex[0], ex[2], ex[1], ex[3], ex[4]]
     b = [ey[0], ey[2], ey[1], ey[3], ey[4]]
     return x, y, a, b, tbl, K
@@ -234,7 +268,7 @@ def cpu_decode_add(a, b, tbl, N, n_total, budget_s=10.0):
         comp, off, st, part, sm = t
         end = int(off[nb])
         sm_s = sm.view(N // 16, K, 8)[:, :k_s].contiguous()
-        return (comp[:end], off[:nb + 1], st[:k_s], part[:k_s], sm_s)
+        return tuple(v.cpu() for v in (comp[:end], off[:nb + 1], st[:k_s], part[:k_s], sm_s))
 
     sa, sb = shard(a), shard(b)
     elems = k_s * N
@@ -305,10 +339,23 @@ def run_reference_arm(args, ws, rank):
     emit(line, args)
 
 
+def vecadd_elements(args) -> int:
+    """Elements per input per GPU: 2^elems_log2, or with --working-set-gib W
+    the largest multiple of 128 streams x n_fp8 with 3 x n <= W GiB (two
+    inputs and the output)."""
+    if args.working_set_gib > 0:
+        unit = 128 * args.n_fp8
+        return int(args.working_set_gib * (1 << 30) / 3) // unit * unit
+    return 1 << args.elems_log2
+
+
 def workload_config(args, K):
-    return {"workload": (f"fused tANS-decode + e4m3 add, 2 x 2^{args.elems_log2} e4m3 inputs per "
+    n = vecadd_elements(args)
+    size = (f"2^{args.elems_log2}" if args.working_set_gib <= 0 else
+            f"{n} ({args.working_set_gib:g} GiB working set, generated on the GPU)")
+    return {"workload": (f"fused tANS-decode + e4m3 add, 2 x {size} e4m3 inputs per "
                          f"GPU, N(0,1)*448/absmax, {args.n_fp8 // 2} pair-symbols per stream"),
-            "elements_per_input_per_gpu": 1 << args.elems_log2,
+            "elements_per_input_per_gpu": n,
             "n_fp8_per_stream": args.n_fp8, "pair_symbols_per_stream": args.n_fp8 // 2,
             "streams_per_input": K, "table_log": 12, "l2": "inputs > L2 (no flush)",
             "parallelism": f"dp{args.gpus} (independent stream shards)"}
@@ -419,6 +466,57 @@ def run_decode(args, dev, barrier):
           "hbm_frac_algorithmic": round(alg / (ms / 1e3) / 1e9 / peak, 4),
           "algorithmic_bytes": alg, "bits_per_fp8": round((alg - n) * 8 / n, 4),
           "bit_exact_round_trip": ok, "peak_source": kind}, args)
+
+
+def run_container(args, dev, barrier):
+    """On-disk container: the cfg2 generator at 2^container_log2 e4m3 bytes,
+    encoded on the device, saved in the safetensors layout, then loaded back
+    to the GPU (whole file, and rank 0's eighth) from the page cache; GB/s of
+    file bytes reaching HBM (wall clock around load + synchronize), checked
+    by a device decode round trip."""
+    import shutil
+    import tempfile
+    from rans_vectoradd import container, gpu_tans_decode, tans_codec
+    n = 1 << args.container_log2
+    N = args.n_fp8
+    K = n // N
+    raw, hist = cfg2_input(n, N, 0, dev)
+    enc = tans_codec.encode(raw.view(K, N), hist, tile=0)
+    d = tempfile.mkdtemp(prefix="tans_container_")
+    try:
+        path = os.path.join(d, "cfg2.safetensors")
+        t0 = time.perf_counter()
+        container.save_encoded(path, enc, N, tile=0)
+        save_s = time.perf_counter() - t0
+        size = os.path.getsize(path)
+        del enc
+        container.load_encoded(path, dev)  # the file is in the page cache now
+        torch.cuda.synchronize()
+        reps = max(3, args.steps)
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            got, _meta = container.load_encoded(path, dev)
+        torch.cuda.synchronize()
+        load_s = (time.perf_counter() - t0) / reps
+        c, st_, off_, part_, sm_, pf, sp = got
+        out = gpu_tans_decode(c, off_, st_, part_, sm_, sp.to(dev), pf.to(dev), N)
+        ok = bool(torch.equal(out.t(), raw.view(K, N)))
+        del out, got
+        t0 = time.perf_counter()
+        for _ in range(reps):
+            part8, _meta8 = container.load_encoded(path, dev, rank=0, world=8)
+        torch.cuda.synchronize()
+        shard_s = (time.perf_counter() - t0) / reps
+        shard_bytes = sum(t.numel() * t.element_size() for t in part8[:5])
+        emit({"workload": "container load (cfg2 generator)", "elements": n, "file_bytes": size,
+              "save_s": round(save_s, 3), "load_ms": round(load_s * 1e3, 2),
+              "load_gbs_file_to_hbm": round(size / load_s / 1e9, 2),
+              "shard_1_of_8_ms": round(shard_s * 1e3, 2),
+              "shard_1_of_8_gbs": round(shard_bytes / shard_s / 1e9, 2),
+              "bit_exact_round_trip": ok, "source": "page cache (file written just before)"},
+             args)
+    finally:
+        shutil.rmtree(d, ignore_errors=True)
 
 
 def make_gemv_weight(R, C, seed, dev, col_splits):
@@ -556,18 +654,21 @@ def main():
         if args.workload == "stack":
             run_stack(args, ws, rank, dev, barrier)
         elif rank == 0 and ws == 1:
-            {"decode": run_decode, "encode": run_encode,
-             "gemv": run_gemv}[args.workload](args, dev, barrier)
+            {"decode": run_decode, "encode": run_encode, "gemv": run_gemv,
+             "container": run_container}[args.workload](args, dev, barrier)
         if ws > 1:
             import torch.distributed as dist
             dist.barrier(device_ids=[local])
             dist.destroy_process_group()
         return
 
-    n = 1 << args.elems_log2
     N = args.n_fp8
+    n = vecadd_elements(args)
     t_setup = time.perf_counter()
-    x, y, a, b, tbl, K = make_workload(n, N, rank)
+    if args.working_set_gib > 0:
+        x, y, a, b, tbl, K = make_workload_device(n, N, rank, dev)
+    else:
+        x, y, a, b, tbl, K = make_workload(n, N, rank)
     setup_s = time.perf_counter() - t_setup
     total_alg, stream_bytes = alg_bytes(a, b, n)
     bits_per_fp8 = stream_bytes * 8 / (2 * n)
@@ -627,11 +728,12 @@ def main():
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        gbs, threads, desc = cpu_decode_add(a, b, tbl, N, n)
+        gbs, threads, desc = cpu_decode_add(a, b, tbl.cpu(), N, n)
         cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "sample": desc}
         from rans_vectoradd.data import exponent_histogram
-        cpu["encode"] = cpu_encode_rates(x, N, exponent_histogram(x, y).double())
+        xs, ys = x[:1 << 24].cpu(), y[:1 << 24].cpu()
+        cpu["encode"] = cpu_encode_rates(xs, N, exponent_histogram(xs, ys).double())
 
     same_all = sum_over_ranks(1.0 if same else 0.0, ws, dev) == ws
     if rank == 0:
