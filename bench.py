@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--working-set-gib", type=float, default=0.0,
                     help="vecadd: size the inputs to this working set per GPU (e.g. 8) instead")
     ap.add_argument("--sweep", action="store_true", help="extra lines over stream lengths")
+    ap.add_argument("--segment-pairs", type=int, default=4096,
+                    help="--sweep: split-stream segment length for streams longer than it")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--e2e-chunk", type=int, default=0,
@@ -765,15 +767,23 @@ def main():
         emit(line, args)
 
     if args.sweep and ws == 1:
+        sweep_hist = (torch.bincount(((xd >> 3) & 15).long(), minlength=16) +
+                      torch.bincount(((yd >> 3) & 15).long(), minlength=16)).cpu().double()
         for n_fp8 in (2048, 8192, 32768, 131072, 1024, 4096, 16384, 65536):
             if n_fp8 == N:
                 continue
             del da, db
             torch.cuda.empty_cache()
-            _, _, a2, b2, tbl2, K2 = make_workload(n, n_fp8, rank)
-            da = [t.to(dev) for t in a2]
-            db = [t.to(dev) for t in b2]
-            dt2 = tbl2.to(dev)
+            # the same inputs re-encoded on the device at this stream length
+            # (the device encoder's bytes equal the host encoder's)
+            from rans_vectoradd import tans_codec
+            K2 = n // n_fp8
+            ex = tans_codec.encode(xd.view(K2, n_fp8), sweep_hist, tile=8)
+            ey = tans_codec.encode(yd.view(K2, n_fp8), sweep_hist, tile=8)
+            a2 = [ex[0], ex[2], ex[1], ex[3], ex[4]]
+            b2 = [ey[0], ey[2], ey[1], ey[3], ey[4]]
+            da, db = a2, b2
+            dt2 = tans_codec.build_decode_table(ex[6].numpy(), ex[5].numpy()).to(dev)
             ms = timed(lambda: rv.fp8_vecadd_fused_tans(*da, *db, dt2, n_fp8), args.steps,
                        args.warmup, stream, barrier)
             tot2, sb2 = alg_bytes(a2, b2, n)
@@ -783,6 +793,32 @@ def main():
                   "gbs_uncompressed_equiv": round(3.0 * n / (ps / 1e3) / 1e9, 2),
                   "x_raw": round(raw_step / ps, 4), "bits_per_fp8": round(sb2 * 8 / (2 * n), 4),
                   "hbm_frac_compressed": round(tot2 / (ps / 1e3) / 1e9 / peak, 4)}, args)
+            S = args.segment_pairs
+            if n_fp8 // 2 > S and (n_fp8 // 2) % S == 0 and K2 % 32 == 0:
+                # split-stream format: the same streams as n_fp8/2/S sub-streams each
+                del da, db, a2, b2
+                torch.cuda.empty_cache()
+                ex = tans_codec.encode(xd.view(K2, n_fp8), sweep_hist, tile=8, segment_pairs=S)
+                ey = tans_codec.encode(yd.view(K2, n_fp8), sweep_hist, tile=8, segment_pairs=S)
+                a2 = [ex[0], ex[2], ex[1], ex[3], ex[4]]
+                b2 = [ey[0], ey[2], ey[1], ey[3], ey[4]]
+                da, db = a2, b2
+                o = rv.fp8_vecadd_fused_tans(*da, *db, dt2, n_fp8, segment_pairs=S)
+                ok = torch.equal(o.view(n_fp8 // 16, K2, 16).permute(1, 0, 2).reshape(-1),
+                                 rv.fp8_vecadd_raw(xd, yd))
+                del o
+                ms = timed(lambda: rv.fp8_vecadd_fused_tans(*da, *db, dt2, n_fp8, segment_pairs=S),
+                           args.steps, args.warmup, stream, barrier)
+                tot2, sb2 = alg_bytes(a2, b2, n)
+                ps = ms / args.steps
+                emit({"sweep": True, "split_stream_segment_pairs": S, "n_fp8_per_stream": n_fp8,
+                      "pair_symbols": n_fp8 // 2, "streams": K2,
+                      "chains": K2 * (n_fp8 // 2 // S), "ms": round(ps, 4),
+                      "gbs_uncompressed_equiv": round(3.0 * n / (ps / 1e3) / 1e9, 2),
+                      "x_raw": round(raw_step / ps, 4),
+                      "bits_per_fp8": round(sb2 * 8 / (2 * n), 4),
+                      "hbm_frac_compressed": round(tot2 / (ps / 1e3) / 1e9 / peak, 4),
+                      "bit_exact_vs_raw": bool(ok)}, args)
 
     if ws > 1:
         import torch.distributed as dist

@@ -134,6 +134,18 @@ int tans_b200_decode(const uint8_t *compressed, int64_t compressed_bytes,
                      int64_t n_streams, int64_t n_fp8_per_stream,
                      int32_t *status, void *stream);
 
+/* Standalone decode of split streams (format of
+ * tans_b200_fp8_vecadd_fused_split: K*P/S sub-streams of S pair symbols,
+ * segment-major; sign_mantissa [N/2][K] and out [N][K] unchanged).
+ * segment_pairs divides N/2; more than one segment needs K % 32 == 0. */
+int tans_b200_decode_split(const uint8_t *compressed, int64_t compressed_bytes,
+                           const int32_t *offsets, const uint16_t *states,
+                           const uint8_t *partial, const uint8_t *sign_mantissa,
+                           const int32_t *decode_table, uint8_t *out,
+                           int64_t n_streams, int64_t n_fp8_per_stream,
+                           int64_t segment_pairs, int32_t *status,
+                           void *stream);
+
 /* Fused decode + FP8 add: replaces `fp8_vecadd_fused_tans`
  * (csrc/vecadd.cu:290-393).  Both inputs share decode_table and the stream
  * count K; sm tensors are tiled [N/16][K][8]; out is tiled [N/16][K][16]
@@ -164,6 +176,28 @@ int tans_b200_fp8_vecadd_fused_range(
     const int32_t *decode_table, uint8_t *out, int64_t n_streams,
     int64_t n_fp8_per_stream, int64_t stream_begin, int64_t stream_end,
     int32_t *status, void *stream);
+
+/* Fused decode + FP8 add on split streams (a format extension; no
+ * reference counterpart).  Each stream of P = N/2 pair symbols is encoded as
+ * P/S independent sub-streams of S = segment_pairs pair symbols, sub-stream
+ * (segment j, stream k) at index j*K + k of the compressed/offsets/states/
+ * partial arrays (K*P/S entries, ceil(K*P/S / 128) + 1 offsets) — exactly
+ * what tans_b200_encode produces from the pair-symbol matrix rearranged to
+ * [P/S * K][S].  The sign/mantissa tensors and the output keep the
+ * unsplit layouts ([N/16][K][8], [N/16][K][16]).  Long streams then decode
+ * as P/S times as many chains.  segment_pairs: a multiple of 8 dividing
+ * N/2 (segment_pairs == N/2 is the unsplit format); with more than one
+ * segment K must be a multiple of 32. */
+int tans_b200_fp8_vecadd_fused_split(
+    const uint8_t *a_compressed, int64_t a_compressed_bytes,
+    const int32_t *a_offsets, const uint16_t *a_states,
+    const uint8_t *a_partial, const uint8_t *a_sm,
+    const uint8_t *b_compressed, int64_t b_compressed_bytes,
+    const int32_t *b_offsets, const uint16_t *b_states,
+    const uint8_t *b_partial, const uint8_t *b_sm,
+    const int32_t *decode_table, uint8_t *out, int64_t n_streams,
+    int64_t n_fp8_per_stream, int64_t segment_pairs, int32_t *status,
+    void *stream);
 
 /* Fused decode + FP8 add from and to HOST memory (no reference counterpart;
  * the reference's op takes device tensors).  All a_* / b_* inputs,
@@ -273,7 +307,11 @@ int tans_b200_decode_noalloc(const uint8_t *compressed, int64_t compressed_bytes
  *      (every byte of compressed is written).  With error bits set it writes
  *      nothing.
  * freqs[n_syms] and spread[4096] are HOST pointers.  Streams are limited to
- * 357,913,941 symbols (32-bit per-stream bit counts). */
+ * 357,913,941 symbols (32-bit per-stream bit counts).
+ * segment_pairs > 0 (dividing the symbols per stream) writes the split-stream
+ * format of tans_b200_fp8_vecadd_fused_split: K * segments sub-streams,
+ * segment-major (states_out, partial_out and offsets sized for them), with
+ * sm_out in the unsplit layout; 0 writes the plain format. */
 #define TANS_B200_ENC_INPUT_FP8 0
 #define TANS_B200_ENC_INPUT_SYMBOLS 1
 #define TANS_B200_ENC_TOO_LARGE 1
@@ -287,20 +325,23 @@ typedef struct tans_b200_enc_header {
 
 int tans_b200_encode_device_workspace_bytes(int64_t n_streams,
                                             int64_t n_per_stream,
-                                            int input_kind, int64_t *bytes);
+                                            int input_kind,
+                                            int64_t segment_pairs,
+                                            int64_t *bytes);
 
 int tans_b200_encode_device_plan(const uint8_t *in, int input_kind,
                                  int64_t n_streams, int64_t n_per_stream,
-                                 int64_t tile, const int32_t *freqs,
-                                 int64_t n_syms, const int32_t *spread,
-                                 uint8_t *sm_out, uint16_t *states_out,
-                                 uint8_t *partial_out, int32_t *offsets_out,
-                                 void *workspace, void *stream);
+                                 int64_t tile, int64_t segment_pairs,
+                                 const int32_t *freqs, int64_t n_syms,
+                                 const int32_t *spread, uint8_t *sm_out,
+                                 uint16_t *states_out, uint8_t *partial_out,
+                                 int32_t *offsets_out, void *workspace,
+                                 void *stream);
 
 int tans_b200_encode_device_emit(int input_kind, int64_t n_streams,
-                                 int64_t n_per_stream, const int32_t *offsets,
-                                 const void *workspace, uint8_t *compressed,
-                                 void *stream);
+                                 int64_t n_per_stream, int64_t segment_pairs,
+                                 const int32_t *offsets, const void *workspace,
+                                 uint8_t *compressed, void *stream);
 
 #ifdef __cplusplus
 }

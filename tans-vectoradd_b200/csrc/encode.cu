@@ -77,8 +77,10 @@ __host__ __device__ __forceinline__ int64_t stage_rows(int64_t P) {
 }
 
 struct EncArgs {
-    const uint8_t *in;    // FP8 bytes [K][2P] or pair symbols [K][P]
-    int64_t K, P;         // streams, pair symbols per stream
+    const uint8_t *in;    // FP8 bytes [stride][2 row_pairs] or pair symbols [stride][row_pairs]
+    int64_t K, P;         // chains (encoded streams), pair symbols per chain
+    int64_t stride;       // streams of the input rows and of the sm layout
+    int64_t row_pairs;    // pair symbols per input row (P * segments for split streams)
     int64_t tile;         // sm layout: 0 -> [P][K], t -> [P/t][K][t]
     int32_t vec;          // 16-byte (FP8) / 8-byte (symbols) chunk loads allowed
     int32_t sm_vec;       // tile 8 and sm 8-byte aligned: one 8-byte store per chunk
@@ -164,35 +166,49 @@ struct Emitter {
     }
 };
 
-__device__ __forceinline__ void store_sm_byte(const EncArgs &a, int64_t k, int64_t i, uint32_t v) {
+// Sign/mantissa byte of pair i (index within the whole input row) of column col.
+__device__ __forceinline__ void store_sm_byte(const EncArgs &a, int64_t col, int64_t i, uint32_t v) {
     if (a.tile == 0)
-        a.sm[i * a.K + k] = (uint8_t)v;
+        a.sm[i * a.stride + col] = (uint8_t)v;
     else
-        a.sm[((i / a.tile) * a.K + k) * a.tile + (i % a.tile)] = (uint8_t)v;
+        a.sm[((i / a.tile) * a.stride + col) * a.tile + (i % a.tile)] = (uint8_t)v;
 }
 
-// Symbol i of stream k read without chunking (ragged tail, unaligned rows);
-// writes the sign/mantissa byte in pass 1.
+// Symbol i of a chain read without chunking (ragged tail, unaligned rows);
+// writes the sign/mantissa byte (row pair pbase + i of column col) in pass 1.
 template <bool kFp8, bool kPass1>
-__device__ __forceinline__ uint32_t scalar_symbol(const EncArgs &a, const uint8_t *row, int64_t k,
-                                                  int64_t i) {
+__device__ __forceinline__ uint32_t scalar_symbol(const EncArgs &a, const uint8_t *row, int64_t col,
+                                                  int64_t pbase, int64_t i) {
     if (!kFp8) return row[i];
     const uint32_t b0 = row[2 * i], b1 = row[2 * i + 1];
     if (kPass1) {
         const uint32_t m0 = ((b0 >> 4) & 8u) | (b0 & 7u), m1 = ((b1 >> 4) & 8u) | (b1 & 7u);
-        store_sm_byte(a, k, i, m0 | (m1 << 4));
+        store_sm_byte(a, col, pbase + i, m0 | (m1 << 4));
     }
     return (((b0 >> 3) & 15u) << 4) | ((b1 >> 3) & 15u);
 }
 
-// Run `m` over stream k from its last pair symbol to its first.
+// First input byte of chain k: split streams are segment-major (chain
+// k = seg * stride + col covers pairs [seg P, (seg + 1) P) of row col).
+template <bool kFp8>
+__device__ __forceinline__ const uint8_t *chain_row(const EncArgs &a, int64_t k, int64_t *col,
+                                                   int64_t *pbase) {
+    const int64_t seg = k / a.stride;
+    *col = k - seg * a.stride;
+    *pbase = seg * a.P;
+    return a.in + (*col * a.row_pairs + *pbase) * (kFp8 ? 2 : 1);
+}
+
+// Run `m` over chain k from its last pair symbol to its first.
 template <bool kFp8, bool kPass1, typename Machine>
 __device__ __forceinline__ void run_stream(const EncArgs &a, const EncTables &t, int64_t k,
                                            Machine &m) {
     const int64_t P = a.P;
-    const uint8_t *row = a.in + k * P * (kFp8 ? 2 : 1);
+    int64_t col, pbase;
+    const uint8_t *row = chain_row<kFp8>(a, k, &col, &pbase);
     const int64_t chunks = a.vec ? P / 8 : 0;
-    for (int64_t i = P - 1; i >= chunks * 8; i--) m.step(t, scalar_symbol<kFp8, kPass1>(a, row, k, i));
+    for (int64_t i = P - 1; i >= chunks * 8; i--)
+        m.step(t, scalar_symbol<kFp8, kPass1>(a, row, col, pbase, i));
     if (chunks == 0) return;
     if (kFp8) {
         const uint8_t *cp = row + (chunks - 1) * 16;
@@ -207,11 +223,12 @@ __device__ __forceinline__ void run_stream(const EncArgs &a, const EncTables &t,
                 const uint32_t lo = __byte_perm(sm_pairs_of(cur.x), sm_pairs_of(cur.y), 0x6420);
                 const uint32_t hi = __byte_perm(sm_pairs_of(cur.z), sm_pairs_of(cur.w), 0x6420);
                 if (a.sm_vec) {
-                    *reinterpret_cast<uint2 *>(a.sm + (c * a.K + k) * 8) = make_uint2(lo, hi);
+                    *reinterpret_cast<uint2 *>(a.sm + ((pbase / 8 + c) * a.stride + col) * 8) =
+                        make_uint2(lo, hi);
                 } else {
 #pragma unroll
                     for (int j = 0; j < 8; j++)
-                        store_sm_byte(a, k, c * 8 + j, byte_of(j < 4 ? lo : hi, j & 3));
+                        store_sm_byte(a, col, pbase + c * 8 + j, byte_of(j < 4 ? lo : hi, j & 3));
                 }
             }
             m.step(t, s3 >> 16);
@@ -290,7 +307,8 @@ __global__ void __launch_bounds__(kBlk, 8) enc_stage_kernel(const EncArgs a) {
             // error path: find the symbols that have no slot and report the smallest
             tans_b200_enc_header *h = header(a.ws);
             atomicOr(&h->error_bits, TANS_B200_ENC_BAD_SYMBOL);
-            const uint8_t *row = a.in + k * a.P * (kFp8 ? 2 : 1);
+            int64_t col, pbase;
+            const uint8_t *row = chain_row<kFp8>(a, k, &col, &pbase);
             for (int64_t i = 0; i < a.P; i++) {
                 uint32_t s;
                 if (kFp8)
@@ -388,13 +406,20 @@ bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p
 // 12 bits per pair symbol at most: the per-stream bit count stays in 32 bits.
 constexpr int64_t kMaxPairsPerStream = (int64_t)(UINT32_MAX / 12);
 
-int check_shape(int input_kind, int64_t K, int64_t n, int64_t *P) {
+int check_shape(int input_kind, int64_t K, int64_t n, int64_t segment_pairs, int64_t *P,
+                int64_t *segs) {
     if (input_kind != TANS_B200_ENC_INPUT_FP8 && input_kind != TANS_B200_ENC_INPUT_SYMBOLS)
         return fail(TANS_B200_ERR_INVALID, "encode_device: unknown input kind %d", input_kind);
     if (K < 0 || n < 0) return fail(TANS_B200_ERR_INVALID, "encode: bad arguments");
     if (input_kind == TANS_B200_ENC_INPUT_FP8 && n % 2 != 0)
         return fail(TANS_B200_ERR_INVALID, "encode_device: FP8 bytes per stream must be even");
-    *P = input_kind == TANS_B200_ENC_INPUT_FP8 ? n / 2 : n;
+    const int64_t row = input_kind == TANS_B200_ENC_INPUT_FP8 ? n / 2 : n;
+    if (segment_pairs < 0 || (segment_pairs > 0 && row % segment_pairs != 0))
+        return fail(TANS_B200_ERR_INVALID,
+                    "encode_device: segment_pairs must divide the %lld symbols per stream",
+                    (long long)row);
+    *P = segment_pairs > 0 ? segment_pairs : row;
+    *segs = segment_pairs > 0 ? row / segment_pairs : 1;
     if (*P > kMaxPairsPerStream)
         return fail(TANS_B200_ERR_INVALID, "encode_device: more than %lld symbols per stream",
                     (long long)kMaxPairsPerStream);
@@ -404,28 +429,29 @@ int check_shape(int input_kind, int64_t K, int64_t n, int64_t *P) {
 }  // namespace
 
 extern "C" int tans_b200_encode_device_workspace_bytes(int64_t K, int64_t n, int input_kind,
-                                                       int64_t *bytes) {
+                                                       int64_t segment_pairs, int64_t *bytes) {
     tans_b200::clear_error();
     if (!bytes) return fail(TANS_B200_ERR_INVALID, "encode_device_workspace_bytes: bytes is null");
-    int64_t P;
-    int rc = check_shape(input_kind, K, n, &P);
+    int64_t P, segs;
+    int rc = check_shape(input_kind, K, n, segment_pairs, &P, &segs);
     if (rc) return rc;
-    const int64_t B = (K + kBlk - 1) / kBlk;
-    *bytes = (int64_t)ws_stage_offset(K) + B * stage_rows(P) * kBlk * 4;
+    const int64_t chains = K * segs, B = (chains + kBlk - 1) / kBlk;
+    *bytes = (int64_t)ws_stage_offset(chains) + B * stage_rows(P) * kBlk * 4;
     return TANS_B200_OK;
 }
 
 extern "C" int tans_b200_encode_device_plan(const uint8_t *in, int input_kind, int64_t K,
-                                            int64_t n, int64_t tile, const int32_t *freqs,
-                                            int64_t n_syms, const int32_t *spread,
-                                            uint8_t *sm_out, uint16_t *states_out,
-                                            uint8_t *partial_out, int32_t *offsets_out,
-                                            void *workspace, void *stream) {
+                                            int64_t n, int64_t tile, int64_t segment_pairs,
+                                            const int32_t *freqs, int64_t n_syms,
+                                            const int32_t *spread, uint8_t *sm_out,
+                                            uint16_t *states_out, uint8_t *partial_out,
+                                            int32_t *offsets_out, void *workspace, void *stream) {
     tans_b200::clear_error();
-    int64_t P;
-    int rc = check_shape(input_kind, K, n, &P);
+    int64_t P, segs;
+    int rc = check_shape(input_kind, K, n, segment_pairs, &P, &segs);
     if (rc) return rc;
     const bool fp8 = input_kind == TANS_B200_ENC_INPUT_FP8;
+    const int64_t row_pairs = P * segs, chains = K * segs;
     if (fp8 && tile < 0) return fail(TANS_B200_ERR_INVALID, "encode_device: tile must be >= 0");
     if (fp8 && tile > 0 && P % tile != 0)
         return fail(TANS_B200_ERR_INVALID, "n_pairs=%lld not divisible by tile=%lld", (long long)P,
@@ -438,7 +464,7 @@ extern "C" int tans_b200_encode_device_plan(const uint8_t *in, int input_kind, i
     EncoderTables tables;
     rc = tans_b200::encoder_tables(freqs, n_syms, spread, &tables);
     if (rc) return rc;
-    const int64_t B = (K + kBlk - 1) / kBlk;
+    const int64_t B = (chains + kBlk - 1) / kBlk;
     if (B > INT_MAX) return fail(TANS_B200_ERR_INVALID, "encode_device: too many streams");
     cudaStream_t st = (cudaStream_t)stream;
     uint8_t *ws = static_cast<uint8_t *>(workspace);
@@ -446,10 +472,13 @@ extern "C" int tans_b200_encode_device_plan(const uint8_t *in, int input_kind, i
     if ((rc = launch_status("enc_setup_kernel"))) return rc;
     EncArgs a{};
     a.in = in;
-    a.K = K;
+    a.K = chains;
     a.P = P;
+    a.stride = K;
+    a.row_pairs = row_pairs;
     a.tile = fp8 ? tile : 0;
-    a.vec = fp8 ? (aligned(in, 16) && (2 * P) % 16 == 0) : (aligned(in, 8) && P % 8 == 0);
+    a.vec = fp8 ? (aligned(in, 16) && (2 * row_pairs) % 16 == 0 && (2 * P) % 16 == 0)
+                : (aligned(in, 8) && row_pairs % 8 == 0 && P % 8 == 0);
     a.sm = sm_out;
     a.sm_vec = fp8 && tile == 8 && aligned(sm_out, 8);
     a.states = states_out;
@@ -469,22 +498,25 @@ extern "C" int tans_b200_encode_device_plan(const uint8_t *in, int input_kind, i
 }
 
 extern "C" int tans_b200_encode_device_emit(int input_kind, int64_t K, int64_t n,
-                                            const int32_t *offsets, const void *workspace,
-                                            uint8_t *compressed, void *stream) {
+                                            int64_t segment_pairs, const int32_t *offsets,
+                                            const void *workspace, uint8_t *compressed,
+                                            void *stream) {
     tans_b200::clear_error();
-    int64_t P;
-    int rc = check_shape(input_kind, K, n, &P);
+    int64_t P, segs;
+    int rc = check_shape(input_kind, K, n, segment_pairs, &P, &segs);
     if (rc) return rc;
     if (K == 0) return TANS_B200_OK;
     if (!workspace || !offsets || !compressed)
         return fail(TANS_B200_ERR_INVALID, "encode_device: null pointer");
     if (!aligned(workspace, 256) || !aligned(offsets, 4) || !aligned(compressed, 4))
         return fail(TANS_B200_ERR_INVALID, "encode_device: misaligned compressed or workspace");
-    const int64_t B = (K + kBlk - 1) / kBlk;
+    const int64_t chains = K * segs, B = (chains + kBlk - 1) / kBlk;
     if (B > INT_MAX) return fail(TANS_B200_ERR_INVALID, "encode_device: too many streams");
     EncArgs a{};
-    a.K = K;
+    a.K = chains;
     a.P = P;
+    a.stride = K;
+    a.row_pairs = P * segs;
     a.offsets = offsets;
     a.compressed = compressed;
     a.ws = static_cast<uint8_t *>(const_cast<void *>(workspace));

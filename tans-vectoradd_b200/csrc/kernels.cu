@@ -530,10 +530,12 @@ struct DecodeArgs {
     const uint8_t *sm;  // [N/2][K]
     const int32_t *table;
     uint8_t *out;       // [N][K]
-    int64_t K, N;
+    int64_t K, N;       // K: chains decoded
+    int64_t stride;     // streams of the layout: row stride of sm and out
+    int64_t seg_pairs;  // pair symbols per chain: N/2, or S for split streams
     int32_t *status;
     Opq q;
-    int32_t word_rows;  // K % 4 == 0 and sm/out 4-byte aligned: word path allowed
+    int32_t word_rows;  // stride % 4 == 0 and sm/out 4-byte aligned: word path allowed
 };
 
 // 4x4 byte transpose across the four lanes of a quad (lane = 4a + b):
@@ -563,10 +565,15 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
     rg.lane_base = ring_area<R>(smem, warp, 1) + 4u * lane;
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int64_t n_groups = (p.K + 31) / 32;
-    const int64_t P = p.N / 2, K = p.K;
+    const int64_t P = p.seg_pairs, K = p.stride;
     for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; g < n_groups; g += warps) {
         const int64_t sid = g * 32 + lane;
-        const bool active = sid < K;
+        const bool active = sid < p.K;
+        // chain sid is segment seg of output stream col (split streams: chains
+        // are segment-major, 32 | stride; otherwise seg = 0 and col = sid)
+        const int64_t seg = (g * 32) / K, col0 = g * 32 - seg * K, col = col0 + lane;
+        const uint8_t *sm_seg = p.sm + seg * P * K;
+        uint8_t *out_seg = p.out + 2 * seg * P * K;
         Chain ch;
         chain_idle(ch, p.comp);
         int32_t G = 0;
@@ -582,10 +589,10 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
         // transposed across the lane quad; the composed even/odd output words
         // are transposed back and stored 4 bytes (4 streams) at a time, each
         // warp store covering four full 32-byte row segments.
-        const bool words = p.word_rows && g * 32 + 32 <= K;
+        const bool words = p.word_rows && g * 32 + 32 <= p.K;
         const int32_t full_tiles = words ? (int32_t)(P / kTablePairs) : 0;
-        const uint8_t *smw = p.sm + qb * K + g * 32 + 4 * qa;
-        uint8_t *ow = p.out + 2 * qb * K + g * 32 + 4 * qa;
+        const uint8_t *smw = sm_seg + qb * K + col0 + 4 * qa;
+        uint8_t *ow = out_seg + 2 * qb * K + col0 + 4 * qa;
         const int64_t srow = kTablePairs * K, orow = 2 * kTablePairs * K;
         uint32_t w0n = 0, w1n = 0;
         if (full_tiles > 0) {
@@ -648,12 +655,12 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j++) {
                     if (i + j >= P) break;
-                    const uint32_t m = live ? __ldg(p.sm + (i + j) * K + sid) : 0u;
+                    const uint32_t m = live ? __ldg(sm_seg + (i + j) * K + col) : 0u;
                     const uint32_t sy = (s8[j] >> 8) & 0xFFu;
                     const uint32_t v0 = ((m & 8u) << 4) | ((sy >> 4) << 3) | (m & 7u);
                     const uint32_t v1 = (((m >> 4) & 8u) << 4) | ((sy & 15u) << 3) | ((m >> 4) & 7u);
-                    p.out[(2 * (i + j)) * K + sid] = live ? (uint8_t)v0 : 0;
-                    p.out[(2 * (i + j) + 1) * K + sid] = live ? (uint8_t)v1 : 0;
+                    out_seg[(2 * (i + j)) * K + col] = live ? (uint8_t)v0 : 0;
+                    out_seg[(2 * (i + j) + 1) * K + col] = live ? (uint8_t)v1 : 0;
                 }
             }
         }
@@ -672,8 +679,9 @@ struct FusedArgs {
     const uint8_t *a_sm, *b_sm;  // [N/16][K][8]
     const int32_t *table;
     uint8_t *out;                // [N/16][K][16]
-    int64_t K, N;                // K: streams decoded (pointers start at the first one)
+    int64_t K, N;                // K: chains decoded (pointers start at the first one)
     int64_t stride;              // streams of the layout: row stride of the sm/out tiles
+    int64_t seg_tiles;           // tiles per chain: N/16, or S/8 for split streams
     int32_t *status;
     Opq q;
 };
@@ -809,7 +817,7 @@ __global__ void __launch_bounds__(kSplitMaxPairs * 64, 1) fused_split_kernel(con
     const uint8_t *part = side ? p.b_part : p.a_part;
     const uint8_t *smv = side ? p.b_sm : p.a_sm;
     const int64_t n_groups = (p.K + 31) / 32;
-    const int32_t n_tiles = (int32_t)(p.N / 16);
+    const int32_t n_tiles = (int32_t)p.seg_tiles;
     const int64_t K = p.K, tstep = p.stride * 8, ostep = p.stride * 16;
     uint2 *my_slot = xch + side * 32 + lane, *their_slot = xch + (side ^ 1) * 32 + lane;
     for (int64_t g = (int64_t)blockIdx.x * pairs + pair; g < n_groups;
@@ -831,8 +839,12 @@ __global__ void __launch_bounds__(kSplitMaxPairs * 64, 1) fused_split_kernel(con
         cp_async_wait<0>();
         // this warp's input: 8 sign/mantissa bytes per tile, loaded a tile
         // ahead; this side prefetches its own input four tiles ahead
-        const uint8_t *sp = smv + sid * 8;
-        uint8_t *op = p.out + sid * 16 + 8 * side;
+        // chain sid is segment j of output stream col (split streams: chains
+        // are segment-major, 32 | stride; otherwise j = 0 and col = sid)
+        const int64_t j = (g * 32) / p.stride;
+        const int64_t col = sid - j * p.stride, tile0 = j * p.seg_tiles * p.stride;
+        const uint8_t *sp = smv + (tile0 + col) * 8;
+        uint8_t *op = p.out + (tile0 + col) * 16 + 8 * side;
         uint2 m_n = make_uint2(0, 0);
         if (live && n_tiles > 0) m_n = ld_stream_v2(sp);
         for (int32_t t = 0; t < n_tiles; t++) {
@@ -1192,6 +1204,16 @@ int launch_fused_split(const FusedArgs &args, int64_t n_streams, int sms, cudaSt
     return launch_status("fused_split_kernel");
 }
 
+static int launch_fused(const FusedArgs &args, int64_t chains, int64_t pairs_per_chain, int sms,
+                 cudaStream_t st) {
+    switch (ring_rows(pairs_per_chain)) {
+        case 16: return launch_fused_split<16>(args, chains, sms, st);
+        case 32: return launch_fused_split<32>(args, chains, sms, st);
+        case 64: return launch_fused_split<64>(args, chains, sms, st);
+        default: return launch_fused_split<128>(args, chains, sms, st);
+    }
+}
+
 extern "C" int tans_b200_sm_count(int *sm_count) {
     if (!sm_count) return fail(TANS_B200_ERR_INVALID, "sm_count: null");
     return device_setup(sm_count);
@@ -1246,18 +1268,20 @@ extern "C" int tans_b200_build_decode_table(const int32_t *spread, const int32_t
     return launch_status("build_table_kernel");
 }
 
-extern "C" int tans_b200_decode(const uint8_t *compressed, int64_t compressed_bytes,
-                                const int32_t *offsets, const uint16_t *states,
-                                const uint8_t *partial, const uint8_t *sign_mantissa,
-                                const int32_t *decode_table, uint8_t *out, int64_t n_streams,
-                                int64_t n_fp8_per_stream, int32_t *status, void *stream) {
-    tans_b200::clear_error();
+static int decode_launch(const uint8_t *compressed, int64_t compressed_bytes,
+                         const int32_t *offsets, const uint16_t *states, const uint8_t *partial,
+                         const uint8_t *sign_mantissa, const int32_t *decode_table, uint8_t *out,
+                         int64_t n_streams, int64_t n_fp8_per_stream, int64_t segment_pairs,
+                         int32_t *status, void *stream) {
     if (n_fp8_per_stream < 0 || n_fp8_per_stream % 2 != 0)
         return fail(TANS_B200_ERR_INVALID, "n_fp8_per_stream must be even");
     if (compressed_bytes < 0 || compressed_bytes % 4 != 0)
         return fail(TANS_B200_ERR_INVALID, "compressed length must be divisible by 4 bytes");
     if (n_streams < 0) return fail(TANS_B200_ERR_INVALID, "n_streams must be >= 0");
     if (n_streams == 0 || n_fp8_per_stream == 0) return TANS_B200_OK;
+    const int64_t segs = (n_fp8_per_stream / 2) / segment_pairs;
+    if (segs > 1 && n_streams % 32 != 0)
+        return fail(TANS_B200_ERR_INVALID, "split streams need n_streams divisible by 32");
     if (!compressed || !offsets || !states || !partial || !sign_mantissa || !decode_table || !out)
         return fail(TANS_B200_ERR_INVALID, "decode: null pointer");
     if (!aligned(compressed, 4) || !aligned(offsets, 4) || !aligned(states, 2) ||
@@ -1266,17 +1290,44 @@ extern "C" int tans_b200_decode(const uint8_t *compressed, int64_t compressed_by
     int sms;
     int rc = device_setup(&sms);
     if (rc) return rc;
+    const int64_t chains = n_streams * segs;
     DecodeArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets,
-                    states, partial, sign_mantissa, decode_table, out, n_streams,
-                    n_fp8_per_stream, status, make_opq(),
+                    states, partial, sign_mantissa, decode_table, out, chains,
+                    n_fp8_per_stream, n_streams, segment_pairs, status, make_opq(),
                     (int32_t)(n_streams % 4 == 0 && aligned(sign_mantissa, 4) && aligned(out, 4))};
     cudaStream_t st = (cudaStream_t)stream;
-    switch (ring_rows(n_fp8_per_stream / 2)) {
-        case 16: return launch_ring_kernel<16>(decode_kernel<16>, args, 1, n_streams, sms, st, "decode_kernel");
-        case 32: return launch_ring_kernel<32>(decode_kernel<32>, args, 1, n_streams, sms, st, "decode_kernel");
-        case 64: return launch_ring_kernel<64>(decode_kernel<64>, args, 1, n_streams, sms, st, "decode_kernel");
-        default: return launch_ring_kernel<128>(decode_kernel<128>, args, 1, n_streams, sms, st, "decode_kernel");
+    switch (ring_rows(segment_pairs)) {
+        case 16: return launch_ring_kernel<16>(decode_kernel<16>, args, 1, chains, sms, st, "decode_kernel");
+        case 32: return launch_ring_kernel<32>(decode_kernel<32>, args, 1, chains, sms, st, "decode_kernel");
+        case 64: return launch_ring_kernel<64>(decode_kernel<64>, args, 1, chains, sms, st, "decode_kernel");
+        default: return launch_ring_kernel<128>(decode_kernel<128>, args, 1, chains, sms, st, "decode_kernel");
     }
+}
+
+extern "C" int tans_b200_decode(const uint8_t *compressed, int64_t compressed_bytes,
+                                const int32_t *offsets, const uint16_t *states,
+                                const uint8_t *partial, const uint8_t *sign_mantissa,
+                                const int32_t *decode_table, uint8_t *out, int64_t n_streams,
+                                int64_t n_fp8_per_stream, int32_t *status, void *stream) {
+    tans_b200::clear_error();
+    return decode_launch(compressed, compressed_bytes, offsets, states, partial, sign_mantissa,
+                         decode_table, out, n_streams, n_fp8_per_stream,
+                         n_fp8_per_stream > 0 ? n_fp8_per_stream / 2 : 1, status, stream);
+}
+
+extern "C" int tans_b200_decode_split(const uint8_t *compressed, int64_t compressed_bytes,
+                                      const int32_t *offsets, const uint16_t *states,
+                                      const uint8_t *partial, const uint8_t *sign_mantissa,
+                                      const int32_t *decode_table, uint8_t *out,
+                                      int64_t n_streams, int64_t n_fp8_per_stream,
+                                      int64_t segment_pairs, int32_t *status, void *stream) {
+    tans_b200::clear_error();
+    if (segment_pairs <= 0 || n_fp8_per_stream < 0 || (n_fp8_per_stream / 2) % segment_pairs != 0)
+        return fail(TANS_B200_ERR_INVALID,
+                    "segment_pairs must be a positive divisor of n_fp8_per_stream/2");
+    return decode_launch(compressed, compressed_bytes, offsets, states, partial, sign_mantissa,
+                         decode_table, out, n_streams, n_fp8_per_stream, segment_pairs, status,
+                         stream);
 }
 
 extern "C" int tans_b200_fp8_vecadd_fused(
@@ -1333,15 +1384,52 @@ extern "C" int tans_b200_fp8_vecadd_fused_range(
                    a_compressed_bytes, b_compressed_bytes, a_offsets + b0, b_offsets + b0,
                    a_states + s0, b_states + s0, a_partial + s0, b_partial + s0, a_sm + 8 * s0,
                    b_sm + 8 * s0, decode_table, out + 16 * s0, stream_end - stream_begin,
-                   n_fp8_per_stream, n_streams, status, make_opq()};
-    cudaStream_t st = (cudaStream_t)stream;
-    const int64_t n_range = stream_end - stream_begin;
-    switch (ring_rows(n_fp8_per_stream / 2)) {
-        case 16: return launch_fused_split<16>(args, n_range, sms, st);
-        case 32: return launch_fused_split<32>(args, n_range, sms, st);
-        case 64: return launch_fused_split<64>(args, n_range, sms, st);
-        default: return launch_fused_split<128>(args, n_range, sms, st);
-    }
+                   n_fp8_per_stream, n_streams, n_fp8_per_stream / 16, status, make_opq()};
+    return launch_fused(args, stream_end - stream_begin, n_fp8_per_stream / 2, sms,
+                        (cudaStream_t)stream);
+}
+
+extern "C" int tans_b200_fp8_vecadd_fused_split(
+    const uint8_t *a_compressed, int64_t a_compressed_bytes, const int32_t *a_offsets,
+    const uint16_t *a_states, const uint8_t *a_partial, const uint8_t *a_sm,
+    const uint8_t *b_compressed, int64_t b_compressed_bytes, const int32_t *b_offsets,
+    const uint16_t *b_states, const uint8_t *b_partial, const uint8_t *b_sm,
+    const int32_t *decode_table, uint8_t *out, int64_t n_streams, int64_t n_fp8_per_stream,
+    int64_t segment_pairs, int32_t *status, void *stream) {
+    tans_b200::clear_error();
+    if (n_fp8_per_stream < 0 || n_fp8_per_stream % 16 != 0)
+        return fail(TANS_B200_ERR_INVALID, "n_fp8_per_stream must be divisible by 16");
+    if (segment_pairs <= 0 || segment_pairs % kTablePairs != 0 ||
+        (n_fp8_per_stream / 2) % segment_pairs != 0)
+        return fail(TANS_B200_ERR_INVALID,
+                    "segment_pairs must be a positive multiple of 8 dividing n_fp8_per_stream/2");
+    if (a_compressed_bytes < 0 || b_compressed_bytes < 0 || a_compressed_bytes % 4 != 0 ||
+        b_compressed_bytes % 4 != 0)
+        return fail(TANS_B200_ERR_INVALID,
+                    "compressed tensors must have byte lengths divisible by 4");
+    if (n_streams < 0) return fail(TANS_B200_ERR_INVALID, "n_streams must be >= 0");
+    const int64_t segs = (n_fp8_per_stream / 2) / segment_pairs;
+    if (segs > 1 && n_streams % 32 != 0)
+        return fail(TANS_B200_ERR_INVALID, "split streams need n_streams divisible by 32");
+    if (n_streams == 0 || n_fp8_per_stream == 0) return TANS_B200_OK;
+    if (!a_compressed || !a_offsets || !a_states || !a_partial || !a_sm || !b_compressed ||
+        !b_offsets || !b_states || !b_partial || !b_sm || !decode_table || !out)
+        return fail(TANS_B200_ERR_INVALID, "fp8_vecadd_fused: null pointer");
+    if (!aligned(a_compressed, 4) || !aligned(b_compressed, 4) || !aligned(a_offsets, 4) ||
+        !aligned(b_offsets, 4) || !aligned(a_states, 2) || !aligned(b_states, 2) ||
+        !aligned(a_sm, 8) || !aligned(b_sm, 8) || !aligned(decode_table, 4) || !aligned(out, 16))
+        return fail(TANS_B200_ERR_INVALID,
+                    "fp8_vecadd_fused: sm tensors need 8-byte and the output 16-byte alignment");
+    int sms;
+    int rc = device_setup(&sms);
+    if (rc) return rc;
+    FusedArgs args{reinterpret_cast<const uint32_t *>(a_compressed),
+                   reinterpret_cast<const uint32_t *>(b_compressed),
+                   a_compressed_bytes, b_compressed_bytes, a_offsets, b_offsets, a_states,
+                   b_states, a_partial, b_partial, a_sm, b_sm, decode_table, out,
+                   n_streams * segs, n_fp8_per_stream, n_streams, segment_pairs / kTablePairs,
+                   status, make_opq()};
+    return launch_fused(args, n_streams * segs, segment_pairs, sms, (cudaStream_t)stream);
 }
 
 extern "C" int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_bytes,
@@ -1484,7 +1572,7 @@ extern "C" int tans_b200_decode_noalloc(const uint8_t *compressed, int64_t compr
     if (rc) return rc;
     DecodeArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets,
                     states, partial, sign_mantissa, table, out, n_streams,
-                    n_fp8_per_stream, status, make_opq(),
+                    n_fp8_per_stream, n_streams, n_fp8_per_stream / 2, status, make_opq(),
                     (int32_t)(n_streams % 4 == 0 && aligned(sign_mantissa, 4) && aligned(out, 4))};
     switch (ring_rows(n_fp8_per_stream / 2)) {
         case 16: return launch_ring_kernel<16>(decode_kernel<16>, args, 1, n_streams, sms, st, "decode_kernel");

@@ -84,6 +84,16 @@ def _same_device(dev: torch.device, *ts: torch.Tensor) -> None:
         _req(t.device == dev, f"all tensors must be on {dev}; got one on {t.device}")
 
 
+def _segments(n_fp8_per_stream: int, segment_pairs: int) -> int:
+    """Sub-streams per stream of the split-stream format (1 when unsplit)."""
+    if not segment_pairs:
+        return 1
+    P = n_fp8_per_stream // 2
+    _req(segment_pairs > 0 and P % segment_pairs == 0,
+         "segment_pairs must be a positive divisor of n_fp8_per_stream / 2")
+    return P // segment_pairs
+
+
 def _streams_per_block_from_env() -> int:
     value = os.environ.get("TANS_STREAMS_PER_BLOCK")
     if not value:
@@ -99,13 +109,15 @@ def _streams_per_block_from_env() -> int:
 # ------------------------------------------------------------------ encoder
 
 def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: torch.Tensor,
-                  tile: int = 0):
+                  tile: int = 0, segment_pairs: int = 0):
     """Device slab encoder (csrc/encode.cu) on a contiguous CUDA uint8 input
     [K, n]: kind ENC_INPUT_FP8 (e4m3 bytes, n even; also returns the
     sign/mantissa pairs in the `tile` layout) or ENC_INPUT_SYMBOLS (pair
     symbols).  freqs/spread may live on any device.  Returns (compressed u8,
     states u16[K], offsets i32[B+1], partial u8[K], sm u8 or None), all on
-    inp's device; bytes identical to the CPU encoder's."""
+    inp's device; bytes identical to the CPU encoder's.  segment_pairs > 0:
+    split-stream format (K * segments sub-streams, segment-major; sm keeps
+    the unsplit layout)."""
     from . import _lib
     _req(inp.is_cuda and inp.dtype == torch.uint8 and inp.dim() == 2 and inp.is_contiguous(),
          "input must be a contiguous CUDA uint8 [K, n] tensor")
@@ -118,13 +130,16 @@ def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: tor
     dev = inp.device
     fp8 = kind == _lib.ENC_INPUT_FP8
     P = n // 2 if fp8 else n
-    nblocks = (K + _BLOCK - 1) // _BLOCK
+    S = int(segment_pairs)
+    _req(S == 0 or (S > 0 and P % S == 0), "segment_pairs must divide the symbols per stream")
+    chains = K * (P // S if S else 1)
+    nblocks = (chains + _BLOCK - 1) // _BLOCK
     with torch.cuda.device(dev):
         wsb = ctypes.c_int64()
-        check(LIB.tans_b200_encode_device_workspace_bytes(K, n, kind, ctypes.byref(wsb)))
+        check(LIB.tans_b200_encode_device_workspace_bytes(K, n, kind, S, ctypes.byref(wsb)))
         ws = torch.empty(wsb.value, dtype=torch.uint8, device=dev)
-        states = torch.empty(K, dtype=torch.uint16, device=dev)
-        partial = torch.empty(K, dtype=torch.uint8, device=dev)
+        states = torch.empty(chains, dtype=torch.uint16, device=dev)
+        partial = torch.empty(chains, dtype=torch.uint8, device=dev)
         offsets = torch.empty(nblocks + 1, dtype=torch.int32, device=dev)
         sm = None
         if fp8:
@@ -132,7 +147,7 @@ def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: tor
             sm = torch.empty(shape, dtype=torch.uint8, device=dev)
         st = _stream(dev)
         check(LIB.tans_b200_encode_device_plan(
-            inp.data_ptr(), kind, K, n, tile, fr.data_ptr(), fr.numel(), sp.data_ptr(),
+            inp.data_ptr(), kind, K, n, tile, S, fr.data_ptr(), fr.numel(), sp.data_ptr(),
             sm.data_ptr() if sm is not None else None, states.data_ptr(), partial.data_ptr(),
             offsets.data_ptr(), ws.data_ptr(), st))
         hdr = ws[:16].cpu()
@@ -143,8 +158,8 @@ def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: tor
         if err & _lib.ENC_TOO_LARGE:
             raise RuntimeError("encode: compressed size exceeds the int32 offsets of the format")
         comp = torch.empty(total, dtype=torch.uint8, device=dev)
-        check(LIB.tans_b200_encode_device_emit(kind, K, n, offsets.data_ptr(), ws.data_ptr(),
-                                               comp.data_ptr(), st))
+        check(LIB.tans_b200_encode_device_emit(kind, K, n, S, offsets.data_ptr(),
+                                               ws.data_ptr(), comp.data_ptr(), st))
     return comp, states, offsets, partial, sm
 
 
@@ -217,9 +232,10 @@ def build_decode_table_device(spread: torch.Tensor, freqs: torch.Tensor,
 def gpu_tans_decode(compressed: torch.Tensor, offsets: torch.Tensor, states: torch.Tensor,
                     partial_cnts: torch.Tensor, sign_mantissa: torch.Tensor,
                     spread: torch.Tensor, freqs: torch.Tensor,
-                    n_fp8_per_stream: int) -> torch.Tensor:
+                    n_fp8_per_stream: int, segment_pairs: int = 0) -> torch.Tensor:
     """GPU tANS pair decoder.  Returns [n_fp8_per_stream, n_streams] uint8
-    (csrc/tans_decode.cu:159-210)."""
+    (csrc/tans_decode.cu:159-210).  segment_pairs > 0: the inputs are in the
+    split-stream format (`tans_codec.encode(..., segment_pairs=S)`)."""
     _req(compressed.is_cuda and compressed.dtype == torch.uint8 and compressed.is_contiguous(),
          "compressed must be contiguous CUDA uint8")
     _req(offsets.is_cuda and offsets.dtype == torch.int32 and offsets.is_contiguous(),
@@ -233,20 +249,27 @@ def gpu_tans_decode(compressed: torch.Tensor, offsets: torch.Tensor, states: tor
     N = int(n_fp8_per_stream)
     _req(N % 2 == 0, "n_fp8_per_stream must be even")
     _req(compressed.numel() % 4 == 0, "compressed length must be divisible by 4 bytes")
-    K = states.numel()
-    n_blocks = (K + _BLOCK - 1) // _BLOCK
+    S = int(segment_pairs)
+    segs = _segments(N, S)
+    chains = states.numel()
+    _req(chains % segs == 0, "split-stream states must hold streams x segments entries")
+    K = chains // segs
+    n_blocks = (chains + _BLOCK - 1) // _BLOCK
     _req(offsets.numel() == n_blocks + 1, "offsets must have n_blocks + 1 entries")
-    _req(partial_cnts.numel() == K, "partial_cnts must match states")
+    _req(partial_cnts.numel() == chains, "partial_cnts must match states")
     _req(sign_mantissa.numel() == (N // 2) * K, "sign_mantissa has the wrong shape")
     dev = compressed.device
     _same_device(dev, offsets, states, partial_cnts, sign_mantissa)
     with torch.cuda.device(dev):
         table = build_decode_table_device(spread, freqs, dev)
         out = torch.empty((N, K), dtype=torch.uint8, device=dev)
-        check(LIB.tans_b200_decode(compressed.data_ptr(), compressed.numel(), offsets.data_ptr(),
-                                   states.data_ptr(), partial_cnts.data_ptr(),
-                                   sign_mantissa.data_ptr(), table.data_ptr(), out.data_ptr(),
-                                   K, N, _status(dev).data_ptr(), _stream(dev)))
+        args = (compressed.data_ptr(), compressed.numel(), offsets.data_ptr(), states.data_ptr(),
+                partial_cnts.data_ptr(), sign_mantissa.data_ptr(), table.data_ptr(),
+                out.data_ptr(), K, N)
+        if S:
+            check(LIB.tans_b200_decode_split(*args, S, _status(dev).data_ptr(), _stream(dev)))
+        else:
+            check(LIB.tans_b200_decode(*args, _status(dev).data_ptr(), _stream(dev)))
     _post_check(dev)
     return out
 
@@ -287,9 +310,12 @@ def fp8_vecadd_fused_tans(a_comp: torch.Tensor, a_offsets: torch.Tensor,
                           a_states: torch.Tensor, a_partial: torch.Tensor, a_sm: torch.Tensor,
                           b_comp: torch.Tensor, b_offsets: torch.Tensor,
                           b_states: torch.Tensor, b_partial: torch.Tensor, b_sm: torch.Tensor,
-                          decode_tbl: torch.Tensor, n_fp8_per_stream: int) -> torch.Tensor:
+                          decode_tbl: torch.Tensor, n_fp8_per_stream: int,
+                          segment_pairs: int = 0) -> torch.Tensor:
     """Fused tANS decompress + FP8 vector add (csrc/vecadd.cu:290-393).
-    Returns the tiled output [N/16 * K * 16] uint8."""
+    Returns the tiled output [N/16 * K * 16] uint8.  segment_pairs > 0: both
+    inputs are in the split-stream format (`tans_codec.encode(...,
+    segment_pairs=S)`); the output layout is unchanged."""
     for name, t in (("a_comp", a_comp), ("a_partial", a_partial), ("a_sm", a_sm),
                     ("b_comp", b_comp), ("b_partial", b_partial), ("b_sm", b_sm)):
         _check_u8_cuda_contiguous(name, t)
@@ -308,8 +334,11 @@ def fp8_vecadd_fused_tans(a_comp: torch.Tensor, a_offsets: torch.Tensor,
     _req(decode_tbl.numel() == _L, f"decode_tbl must have {_L} entries")
     N = int(n_fp8_per_stream)
     _req(N % (2 * _TILE_PAIRS) == 0, f"n_fp8_per_stream must be divisible by {2 * _TILE_PAIRS}")
-    K = a_states.numel()
-    n_enc_blocks = (K + _BLOCK - 1) // _BLOCK
+    S = int(segment_pairs)
+    segs = _segments(N, S)
+    _req(a_states.numel() % segs == 0, "split-stream states must hold streams x segments entries")
+    K = a_states.numel() // segs
+    n_enc_blocks = (K * segs + _BLOCK - 1) // _BLOCK
     _req(a_offsets.numel() == n_enc_blocks + 1 and b_offsets.numel() == n_enc_blocks + 1,
          "offset tensors must have n_encoder_blocks + 1 entries")
     n_tiles = (N // 2) // _TILE_PAIRS
@@ -322,12 +351,15 @@ def fp8_vecadd_fused_tans(a_comp: torch.Tensor, a_offsets: torch.Tensor,
     _streams_per_block_from_env()
     with torch.cuda.device(dev):
         out = torch.empty(n_tiles * K * _TILE_PAIRS * 2, dtype=torch.uint8, device=dev)
-        check(LIB.tans_b200_fp8_vecadd_fused(
-            a_comp.data_ptr(), a_comp.numel(), a_offsets.data_ptr(), a_states.data_ptr(),
-            a_partial.data_ptr(), a_sm.data_ptr(),
-            b_comp.data_ptr(), b_comp.numel(), b_offsets.data_ptr(), b_states.data_ptr(),
-            b_partial.data_ptr(), b_sm.data_ptr(),
-            decode_tbl.data_ptr(), out.data_ptr(), K, N, _status(dev).data_ptr(), _stream(dev)))
+        args = (a_comp.data_ptr(), a_comp.numel(), a_offsets.data_ptr(), a_states.data_ptr(),
+                a_partial.data_ptr(), a_sm.data_ptr(),
+                b_comp.data_ptr(), b_comp.numel(), b_offsets.data_ptr(), b_states.data_ptr(),
+                b_partial.data_ptr(), b_sm.data_ptr(), decode_tbl.data_ptr(), out.data_ptr(), K, N)
+        if S:
+            check(LIB.tans_b200_fp8_vecadd_fused_split(*args, S, _status(dev).data_ptr(),
+                                                        _stream(dev)))
+        else:
+            check(LIB.tans_b200_fp8_vecadd_fused(*args, _status(dev).data_ptr(), _stream(dev)))
     _post_check(dev)
     return out
 

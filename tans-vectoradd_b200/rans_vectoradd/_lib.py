@@ -52,10 +52,14 @@ def _load() -> ctypes.CDLL:
                                                                   ctypes.POINTER(i64)]),
         "tans_b200_fp8_vecadd_fused_host": (i32, [p, i64, p, p, p, p, p, i64, p, p, p, p, p, p,
                                                   i64, i64, i64, p, i64, p, p]),
-        "tans_b200_encode_device_workspace_bytes": (i32, [i64, i64, i32, ctypes.POINTER(i64)]),
-        "tans_b200_encode_device_plan": (i32, [p, i32, i64, i64, i64, p, i64, p, p, p, p, p, p,
-                                               p]),
-        "tans_b200_encode_device_emit": (i32, [i32, i64, i64, p, p, p, p]),
+        "tans_b200_encode_device_workspace_bytes": (i32, [i64, i64, i32, i64,
+                                                          ctypes.POINTER(i64)]),
+        "tans_b200_encode_device_plan": (i32, [p, i32, i64, i64, i64, i64, p, i64, p, p, p, p,
+                                               p, p, p]),
+        "tans_b200_encode_device_emit": (i32, [i32, i64, i64, i64, p, p, p, p]),
+        "tans_b200_fp8_vecadd_fused_split": (i32, [p, i64, p, p, p, p, p, i64, p, p, p, p, p, p,
+                                                   i64, i64, i64, p, p]),
+        "tans_b200_decode_split": (i32, [p, i64, p, p, p, p, p, p, i64, i64, i64, p, p]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)

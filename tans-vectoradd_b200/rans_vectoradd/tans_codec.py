@@ -127,6 +127,7 @@ def encode(
     fp8_bytes: torch.Tensor,
     exp_freqs: torch.Tensor,
     tile: int = 0,
+    segment_pairs: int = 0,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
            torch.Tensor, torch.Tensor, torch.Tensor]:
     """tANS encode FP8 bytes [K, N] (pair alphabet).
@@ -139,6 +140,14 @@ def encode(
     CPU input encodes on the host (as the reference); CUDA input encodes on
     its device (split + slab encode kernels) and the first five outputs stay
     there.  Bytes are identical either way.
+
+    segment_pairs = S > 0 (a format extension, not in the reference): every
+    stream is cut into N/2/S sub-streams of S pair symbols, encoded as
+    independent streams in segment-major order (sub-stream j*K + k is pairs
+    [jS, (j+1)S) of stream k) — the reference encoder's bytes for the
+    pair-symbol matrix rearranged that way; sm_packed keeps the unsplit
+    layout.  Long streams then decode as N/2/S times as many chains
+    (gpu_tans_decode / fp8_vecadd_fused_tans with segment_pairs=S).
     """
     assert fp8_bytes.dim() == 2 and fp8_bytes.dtype == torch.uint8
     K, N = fp8_bytes.shape
@@ -146,6 +155,9 @@ def encode(
     if tile > 0:
         n_pairs = N // 2
         assert n_pairs % tile == 0, f"n_pairs={n_pairs} not divisible by tile={tile}"
+    if segment_pairs:
+        assert segment_pairs > 0 and (N // 2) % segment_pairs == 0, \
+            f"segment_pairs={segment_pairs} must divide n_pairs={N // 2}"
     pair_freqs = pair_freqs_from_exponents(exp_freqs)
     spread = build_spread(pair_freqs)
     pair_freqs_t = torch.from_numpy(pair_freqs)
@@ -154,9 +166,12 @@ def encode(
         # device encoder: split and slab encode on the GPU, outputs stay there
         from ._lib import ENC_INPUT_FP8
         compressed, states, offsets, partial_cnts, sm_packed = _C.encode_device(
-            fp8_bytes.contiguous(), ENC_INPUT_FP8, pair_freqs_t, spread_t, tile)
+            fp8_bytes.contiguous(), ENC_INPUT_FP8, pair_freqs_t, spread_t, tile, segment_pairs)
         return (compressed, states, offsets, partial_cnts, sm_packed, pair_freqs_t, spread_t)
     pair_syms, sm_packed, _ = split_fp8(fp8_bytes, tile)
+    if segment_pairs and segment_pairs != N // 2:
+        S = segment_pairs
+        pair_syms = pair_syms.view(K, N // 2 // S, S).transpose(0, 1).reshape(-1, S).contiguous()
     compressed, states, offsets, partial_cnts = _C.tans_encode_interleaved(
         pair_syms, pair_freqs_t, spread_t)
     return (compressed, states, offsets, partial_cnts, sm_packed, pair_freqs_t, spread_t)
