@@ -56,9 +56,10 @@ def parse():
     ap.add_argument("--e2e-chunk", type=int, default=0,
                     help="streams per pipelined chunk of the e2e call (0: K/8)")
     ap.add_argument("--out", default=None, help="also append the JSON line(s) to this file")
-    ap.add_argument("--workload", choices=["vecadd", "decode", "encode", "gemv", "stack", "container"],
+    ap.add_argument("--workload", choices=["vecadd", "decode", "encode", "gemv", "gemm", "stack", "container"],
                     default="vecadd", help="vecadd (cfg1, headline), decode (cfg2), "
-                    "encode (device encoder on the cfg2 input), gemv (cfg3), "
+                    "encode (device encoder on the cfg2 input), gemv (cfg3), gemm (cfg3 "
+                    "weight at prefill batches), "
                     "stack (cfg4: 40-layer row-sharded GEMV + all-gather), "
                     "container (save/load of encoded tensors)")
     ap.add_argument("--container-log2", type=int, default=30,
@@ -556,6 +557,42 @@ def run_gemv(args, dev, barrier):
                   "peak_source": kind}, args)
 
 
+def run_gemm(args, dev, barrier):
+    """Prefill-size batches on the cfg3 weight [17408 x 5120]: the dense
+    bf16 decode of the encoded weight (GB/s of e4m3 output) and
+    tans_gemv.gemm (decode + library bf16 GEMM with fp32 output + per-row
+    scale) against the GEMM alone on a pre-decoded weight; rel err vs the
+    decode-then-dense fp32 reference."""
+    from rans_vectoradd import tans_gemv
+    stream = torch.cuda.current_stream(dev)
+    R, C = 17408, 5120
+    enc, w8, s = make_gemv_weight(R, C, 0, dev, None)
+    w = tans_gemv.dense_weight(enc)
+    exact = bool(torch.equal(w, w8.view(torch.float8_e4m3fn).to(torch.bfloat16)))
+    ms_dec = timed(lambda: tans_gemv.dense_weight(enc, w), args.steps * 4, args.warmup, stream,
+                   barrier) / (args.steps * 4)
+    line = {"workload": "gemm (cfg3 weight, prefill batches)", "rows": R, "cols": C,
+            "dense_decode_us": round(ms_dec * 1e3, 2),
+            "dense_decode_gbs_e4m3": round(R * C / (ms_dec / 1e3) / 1e9, 1),
+            "dense_exact": exact, "batches": []}
+    for B in (64, 512, 2048):
+        g = torch.Generator(device=dev).manual_seed(B)
+        x = torch.randn(B, C, device=dev, generator=g).to(torch.bfloat16)
+        y = tans_gemv.gemm(enc, x)
+        err = tans_gemv.rel_err(y, tans_gemv.reference_gemv(w8, s, x))
+        ms = timed(lambda: tans_gemv.gemm(enc, x), args.steps, args.warmup, stream,
+                   barrier) / args.steps
+        ms_mm = timed(lambda: torch.mm(x, w.t(), out_dtype=torch.float32), args.steps,
+                      args.warmup, stream, barrier) / args.steps
+        fl = 2.0 * B * R * C
+        line["batches"].append({"batch": B, "us": round(ms * 1e3, 1),
+                                "tflops": round(fl / (ms / 1e3) / 1e12, 1),
+                                "gemm_only_us": round(ms_mm * 1e3, 1),
+                                "gemm_only_tflops": round(fl / (ms_mm / 1e3) / 1e12, 1),
+                                "rel_err": err})
+    emit(line, args)
+
+
 def run_stack(args, ws, rank, dev, barrier):
     """cfg4: `layers` x (up [17408 x 5120] + down [5120 x 17408]) e4m3 GEMVs,
     rows sharded over the ranks, NCCL all-gather of each y; one step = one
@@ -657,7 +694,7 @@ def main():
             run_stack(args, ws, rank, dev, barrier)
         elif rank == 0 and ws == 1:
             {"decode": run_decode, "encode": run_encode, "gemv": run_gemv,
-             "container": run_container}[args.workload](args, dev, barrier)
+             "gemm": run_gemm, "container": run_container}[args.workload](args, dev, barrier)
         if ws > 1:
             import torch.distributed as dist
             dist.barrier(device_ids=[local])

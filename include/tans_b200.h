@@ -247,6 +247,18 @@ int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_bytes,
                    int64_t cols, int64_t batch, int64_t col_splits,
                    int32_t *status, void *stream);
 
+/* Decode a GEMV-layout weight (tans_b200_gemv's stream format) to a dense
+ * row-major bf16 [rows][cols] matrix of its e4m3 values (unscaled; exact).
+ * For batches above 8, where the contraction belongs to a library bf16 GEMM
+ * (y = (x @ w^T) * scale); no reference counterpart. */
+int tans_b200_gemv_weight_dense(const uint8_t *compressed,
+                                int64_t compressed_bytes,
+                                const int32_t *offsets, const uint16_t *states,
+                                const uint8_t *partial, const uint8_t *sm,
+                                const int32_t *decode_table, uint16_t *w_bf16,
+                                int64_t rows, int64_t cols, int64_t col_splits,
+                                int32_t *status, void *stream);
+
 /* Allocation-free standalone decode.  No counterpart in the reference: it
  * exists for callers that cannot allocate device memory (a runtime that
  * hands the library only buffers carved from a pre-sized pool, or a

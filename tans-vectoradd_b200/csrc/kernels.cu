@@ -1101,6 +1101,106 @@ __global__ void gemv_reduce_kernel(const float *__restrict__ part, const float *
     }
 }
 
+// --------------------------------------------------- GEMV weight -> dense
+//
+// Decode a GEMV-layout weight (streams as in gemv_kernel) to a dense
+// row-major bf16 matrix of the e4m3 values (exact: e4m3 -> f16 -> f32 ->
+// bf16 loses nothing), for batches beyond the GEMV kernel's 8, where the
+// contraction is done by a library bf16 GEMM.  One chain per lane; lane
+// (g, t) of a warp holds row 16w + g (+8 for the second chain set) and, per
+// 16-column chunk, columns 2t, 2t+1, 8+2t, 9+2t: each composed pair becomes
+// one bf16x2 store, and a warp's stores cover 8 rows x 16 contiguous bytes.
+
+struct DenseArgs {
+    const uint32_t *comp;
+    int64_t comp_bytes;
+    const int32_t *offsets;
+    const uint16_t *states;
+    const uint8_t *partial;
+    const uint8_t *sm;  // [N/16][K][8]
+    const int32_t *table;
+    uint16_t *w;        // bf16 [R][C]
+    int64_t R, C, KS;
+    int32_t *status;
+    Opq q;
+};
+
+__device__ __forceinline__ uint32_t cvt_bf16x2_e4m3x2(uint32_t v16) {
+    uint32_t r;
+    asm("{\n\t.reg .b16 h, l, u;\n\t.reg .b32 f;\n\t.reg .f32 fl, fu;\n\t"
+        "cvt.u16.u32 h, %1;\n\t"
+        "cvt.rn.f16x2.e4m3x2 f, h;\n\t"
+        "mov.b32 {l, u}, f;\n\t"
+        "cvt.f32.f16 fl, l;\n\t"
+        "cvt.f32.f16 fu, u;\n\t"
+        "cvt.rn.bf16x2.f32 %0, fu, fl;\n\t}"
+        : "=r"(r)
+        : "r"(v16));
+    return r;
+}
+
+template <int R>
+__global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_dense_kernel(const DenseArgs p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
+    __syncthreads();
+    const uint8_t *tb = smem;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const uint32_t lane_off = 4u * (lane % kCopies);
+    const uint32_t mask = (uint32_t)(R - 1) << 7;
+    Ring rg;
+    rg.lane_base = ring_area<R>(smem, warp, 1) + 4u * lane;
+    const int64_t CS = p.C / p.KS, K = p.R * 4 * p.KS;
+    const int32_t n_tiles = (int32_t)(CS / 64);
+    const int64_t n_groups = K / 32;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    for (int64_t g = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; g < n_groups; g += warps) {
+        const int64_t sid = g * 32 + lane;
+        Chain ch;
+        const int32_t G = chain_init(ch, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
+                                     sid, lane_off, p.status);
+        const bool live = G > 0;
+        if (!live) chain_idle(ch, p.comp);
+        ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, live ? G : 0), live);
+        cp_async_commit();
+        cp_async_wait<0>();
+        // stream group g = (w * KS + k) * 2 + chain
+        const int64_t chain = g & 1, wk = g >> 1, k = wk % p.KS, w = wk / p.KS;
+        const int64_t row = 16 * w + (lane >> 2) + 8 * chain;
+        uint32_t *dst = reinterpret_cast<uint32_t *>(p.w + row * p.C + k * CS + 2 * (lane & 3));
+        const uint8_t *sp = p.sm + sid * 8;
+        uint2 m_n = live ? ld_stream_v2(sp) : make_uint2(0, 0);
+        for (int32_t t = 0; t < n_tiles; t++) {
+            const uint2 m = m_n;
+            sp += K * 8;
+            if (live && t + 1 < n_tiles) m_n = ld_stream_v2(sp);
+            if (live && t + 4 < n_tiles) prefetch_l2(sp + 3 * K * 8);
+            const int32_t need = ring_fill<R>(rg, ch, live);
+            cp_async_commit();
+            cp_async_wait<kDecodeLag>();
+            uint32_t e[kTablePairs];
+            if (need >= rg.done[kDecodeLag]) {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++)
+                    e[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
+            } else {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_global(ch, tb, p.q);
+            }
+            uint32_t wd[4];
+            compose_pairs(gather_syms(e[0], e[1], e[2], e[3]), m.x, p.q, wd[0], wd[1]);
+            compose_pairs(gather_syms(e[4], e[5], e[6], e[7]), m.y, p.q, wd[2], wd[3]);
+#pragma unroll
+            for (int c = 0; c < 4; c++) {  // 16-column chunk 4t + c
+                uint32_t *d = dst + (int64_t)(4 * t + c) * 8;
+                d[0] = live ? cvt_bf16x2_e4m3x2(wd[c] & 0xFFFFu) : 0u;  // columns 2t, 2t+1
+                d[4] = live ? cvt_bf16x2_e4m3x2(wd[c] >> 16) : 0u;      // columns 8+2t, 9+2t
+            }
+        }
+        cp_async_wait<0>();
+    }
+}
+
 // ------------------------------------------------------------- host glue
 
 constexpr int kMaxDevices = 64;
@@ -1494,6 +1594,40 @@ extern "C" int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_byte
     gemv_reduce_kernel<<<(unsigned)(blocks < 4 * sms ? blocks : 4 * sms), threads, 0, st>>>(
         partials, scale, y, rows, batch, col_splits);
     return launch_status("gemv_reduce_kernel");
+}
+
+extern "C" int tans_b200_gemv_weight_dense(const uint8_t *compressed, int64_t compressed_bytes,
+                                           const int32_t *offsets, const uint16_t *states,
+                                           const uint8_t *partial, const uint8_t *sm,
+                                           const int32_t *decode_table, uint16_t *w_bf16,
+                                           int64_t rows, int64_t cols, int64_t col_splits,
+                                           int32_t *status, void *stream) {
+    tans_b200::clear_error();
+    if (rows <= 0 || rows % 16 != 0)
+        return fail(TANS_B200_ERR_INVALID, "gemv: rows must be a positive multiple of 16");
+    if (col_splits < 1 || cols <= 0 || cols % (64 * col_splits) != 0)
+        return fail(TANS_B200_ERR_INVALID, "gemv: cols must be a positive multiple of 64 * col_splits");
+    if (!compressed || !offsets || !states || !partial || !sm || !decode_table || !w_bf16)
+        return fail(TANS_B200_ERR_INVALID, "gemv_weight_dense: null pointer");
+    if (!aligned(compressed, 4) || !aligned(offsets, 4) || !aligned(states, 2) ||
+        !aligned(sm, 8) || !aligned(decode_table, 4) || !aligned(w_bf16, 4))
+        return fail(TANS_B200_ERR_INVALID, "gemv_weight_dense: misaligned buffer");
+    if (compressed_bytes < 0 || compressed_bytes % 4 != 0)
+        return fail(TANS_B200_ERR_INVALID, "compressed length must be divisible by 4 bytes");
+    int sms;
+    int rc = device_setup(&sms);
+    if (rc) return rc;
+    DenseArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets,
+                   states, partial, sm, decode_table, w_bf16, rows, cols, col_splits, status,
+                   make_opq()};
+    const int64_t chains = rows * 4 * col_splits;
+    cudaStream_t st = (cudaStream_t)stream;
+    switch (ring_rows(cols / col_splits / 8)) {
+        case 16: return launch_ring_kernel<16>(gemv_dense_kernel<16>, args, 1, chains, sms, st, "gemv_dense_kernel");
+        case 32: return launch_ring_kernel<32>(gemv_dense_kernel<32>, args, 1, chains, sms, st, "gemv_dense_kernel");
+        case 64: return launch_ring_kernel<64>(gemv_dense_kernel<64>, args, 1, chains, sms, st, "gemv_dense_kernel");
+        default: return launch_ring_kernel<128>(gemv_dense_kernel<128>, args, 1, chains, sms, st, "gemv_dense_kernel");
+    }
 }
 
 // ------------------------------------------------------- allocation-free decode

@@ -134,6 +134,41 @@ def gemv(weight: EncodedWeight, x: torch.Tensor, out: torch.Tensor | None = None
     return out
 
 
+def dense_weight(weight: EncodedWeight, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Decode a CUDA EncodedWeight to a dense row-major bf16 [rows, cols]
+    matrix of its e4m3 values (unscaled; e4m3 -> bf16 is exact)."""
+    dev = weight.compressed.device
+    _req(weight.compressed.is_cuda, "weight must be on a CUDA device")
+    _same_device(dev, weight.offsets, weight.states, weight.partial, weight.sm, weight.table)
+    R, C = weight.rows, weight.cols
+    with torch.cuda.device(dev):
+        if out is None:
+            out = torch.empty((R, C), dtype=torch.bfloat16, device=dev)
+        _req(out.shape == (R, C) and out.dtype == torch.bfloat16 and out.is_contiguous()
+             and out.device == dev, "out must be a contiguous bf16 [rows, cols] tensor")
+        check(LIB.tans_b200_gemv_weight_dense(
+            weight.compressed.data_ptr(), weight.compressed.numel(), weight.offsets.data_ptr(),
+            weight.states.data_ptr(), weight.partial.data_ptr(), weight.sm.data_ptr(),
+            weight.table.data_ptr(), out.data_ptr(), R, C, weight.col_splits,
+            _status(dev).data_ptr(), _stream(dev)))
+    return out
+
+
+def gemm(weight: EncodedWeight, x: torch.Tensor, w_dense: torch.Tensor | None = None
+         ) -> torch.Tensor:
+    """y [batch, rows] bf16 = scale * W @ x^T for any batch: the fused GEMV
+    kernel up to batch 8; above it the weight is decoded to dense bf16
+    (`dense_weight`, reusable through `w_dense`) and contracted by a library
+    bf16 GEMM with fp32 output, scaled per row of W, then rounded once."""
+    _req(x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(),
+         "x must be a contiguous CUDA bfloat16 [batch, cols] tensor")
+    if x.shape[0] <= 8:
+        return gemv(weight, x)
+    w = dense_weight(weight) if w_dense is None else w_dense
+    y = torch.mm(x, w.t(), out_dtype=torch.float32)
+    return (y * weight.scale).to(torch.bfloat16)
+
+
 def reference_gemv(w8: torch.Tensor, scale: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """Decode-then-dense fp32 reference: bf16((W8.float() * s) @ x.float()^T)."""
     w = w8.view(torch.float8_e4m3fn).float() * scale.float()[:, None]
@@ -146,4 +181,4 @@ def rel_err(y: torch.Tensor, y_ref: torch.Tensor) -> float:
 
 
 __all__ = ["EncodedWeight", "quantize_rows", "stream_matrix", "encode_weight", "gemv",
-           "reference_gemv", "rel_err"]
+           "dense_weight", "gemm", "reference_gemv", "rel_err"]

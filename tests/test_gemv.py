@@ -105,3 +105,25 @@ def test_gemv_device_encoded_weight_matches_host(cuda):
         assert b.is_cuda and torch.equal(a, b.cpu()), name
     x = torch.randn(8, 4352, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16)
     assert torch.equal(tans_gemv.gemv(dev, x.to(cuda)), tans_gemv.gemv(host.to(cuda), x.to(cuda)))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("R,C,KS", [(64, 512, 1), (256, 4352, 4), (17408, 5120, 2)])
+def test_dense_weight_is_exact(cuda, R, C, KS):
+    """The dense decode returns the e4m3 values themselves (as bf16)."""
+    w8, s = make(R, C, R * 3 + C)
+    enc = tans_gemv.encode_weight(w8.to(cuda), s.to(cuda), col_splits=KS)
+    dense = tans_gemv.dense_weight(enc)
+    assert torch.equal(dense, w8.to(cuda).view(torch.float8_e4m3fn).to(torch.bfloat16))
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("B", [9, 64, 512])
+def test_gemm_large_batch_matches_reference(cuda, B):
+    R, C = 1024, 5120
+    w8, s = make(R, C, 11)
+    enc = tans_gemv.encode_weight(w8.to(cuda), s.to(cuda))
+    x = torch.randn(B, C, generator=torch.Generator().manual_seed(B)).to(torch.bfloat16).to(cuda)
+    y = tans_gemv.gemm(enc, x)
+    ref = tans_gemv.reference_gemv(w8.to(cuda), s.to(cuda), x)
+    assert y.shape == (B, R) and tans_gemv.rel_err(y, ref) <= TOL
