@@ -549,7 +549,16 @@ __device__ __forceinline__ uint32_t quad_transpose(uint32_t v, uint32_t sel1, ui
     return __byte_perm(t, u, sel2);
 }
 
-template <int R>
+// Output staging of the team form (kTeams): 4 warps = one 128-stream block
+// hand their decoded 16 x 32-byte tile pieces to shared memory, and each
+// warp then stores 4 whole 128-byte output rows, instead of each warp
+// storing 32-byte row segments (the [N][K] output puts every row K bytes
+// apart, and scattered 32-byte pieces cost ~20 % of the kernel on cfg2).
+constexpr int kTeamWarps = 4;
+constexpr int kStageRowWords = 36;  // 32 + 4 padding: conflict-free staging writes
+constexpr int kStageBytes = 2 * 16 * kStageRowWords * 4;  // double-buffered tile
+
+template <int R, bool kTeams>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeArgs p) {
     extern __shared__ __align__(16) uint8_t smem[];
     load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
@@ -593,6 +602,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
         const int32_t full_tiles = words ? (int32_t)(P / kTablePairs) : 0;
         const uint8_t *smw = sm_seg + qb * K + col0 + 4 * qa;
         uint8_t *ow = out_seg + 2 * qb * K + col0 + 4 * qa;
+        // team form: this warp stores rows 4 wi .. 4 wi + 3 of every tile,
+        // 128 bytes each (the team's 128 columns)
+        const int wi = warp & (kTeamWarps - 1);
+        uint32_t *stage = reinterpret_cast<uint32_t *>(
+            smem + (ring_area<R>(smem, blockDim.x >> 5, 1) - smem_addr(smem)) +
+            (warp / kTeamWarps) * kStageBytes);
+        uint8_t *otp = out_seg + (int64_t)(4 * wi) * K + (col0 - 32 * wi) + 4 * lane;
         const int64_t srow = kTablePairs * K, orow = 2 * kTablePairs * K;
         uint32_t w0n = 0, w1n = 0;
         if (full_tiles > 0) {
@@ -630,11 +646,26 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
             O0 = quad_transpose(O0, sel1, sel2);
             E1 = quad_transpose(E1, sel1, sel2);
             O1 = quad_transpose(O1, sel1, sel2);
-            st_stream_u32(ow, E0);          // element 2b
-            st_stream_u32(ow + K, O0);      // element 2b + 1
-            st_stream_u32(ow + 8 * K, E1);  // element 8 + 2b
-            st_stream_u32(ow + 9 * K, O1);  // element 9 + 2b
-            ow += orow;
+            if (kTeams) {
+                uint32_t *sb = stage + (t & 1) * (16 * kStageRowWords) + wi * 8 + qa;
+                sb[(2 * qb) * kStageRowWords] = E0;      // element 2b
+                sb[(2 * qb + 1) * kStageRowWords] = O0;  // element 2b + 1
+                sb[(8 + 2 * qb) * kStageRowWords] = E1;  // element 8 + 2b
+                sb[(9 + 2 * qb) * kStageRowWords] = O1;  // element 9 + 2b
+                asm volatile("bar.sync %0, %1;" ::"r"(1 + warp / kTeamWarps), "n"(kTeamWarps * 32)
+                             : "memory");
+                const uint32_t *rb = stage + (t & 1) * (16 * kStageRowWords) +
+                                     (4 * wi) * kStageRowWords + lane;
+#pragma unroll
+                for (int r = 0; r < 4; r++) st_stream_u32(otp + r * K, rb[r * kStageRowWords]);
+                otp += orow;
+            } else {
+                st_stream_u32(ow, E0);          // element 2b
+                st_stream_u32(ow + K, O0);      // element 2b + 1
+                st_stream_u32(ow + 8 * K, E1);  // element 8 + 2b
+                st_stream_u32(ow + 9 * K, O1);  // element 9 + 2b
+                ow += orow;
+            }
         }
         // Byte path: the rest of the stream (all of it for a partial warp or
         // unaligned rows), one pair at a time.
@@ -1368,6 +1399,25 @@ extern "C" int tans_b200_build_decode_table(const int32_t *spread, const int32_t
     return launch_status("build_table_kernel");
 }
 
+// Decode launch: the team form (output staged per 128-stream block) when
+// rows are word-aligned and the layout's stream count is a multiple of 128,
+// else the per-warp form.
+template <int R>
+int launch_decode(const DecodeArgs &args, int64_t chains, int sms, cudaStream_t st) {
+    if (!(args.word_rows && args.stride % (kTeamWarps * 32) == 0))
+        return launch_ring_kernel<R>(decode_kernel<R, false>, args, 1, chains, sms, st,
+                                     "decode_kernel");
+    const int per_team = kTeamWarps * R * 128 + kStageBytes;
+    int max_t = (kSmemMax - kTableBytes - R * 128) / per_team;
+    if (max_t > kMaxWarps / kTeamWarps) max_t = kMaxWarps / kTeamWarps;
+    const Geometry geo = balance(chains / (kTeamWarps * 32), sms, max_t);
+    const int smem = kTableBytes + R * 128 + geo.warps_per_cta * per_team;
+    int rc = set_smem(decode_kernel<R, true>, smem);
+    if (rc) return rc;
+    decode_kernel<R, true><<<geo.grid, geo.warps_per_cta * kTeamWarps * 32, smem, st>>>(args);
+    return launch_status("decode_kernel");
+}
+
 static int decode_launch(const uint8_t *compressed, int64_t compressed_bytes,
                          const int32_t *offsets, const uint16_t *states, const uint8_t *partial,
                          const uint8_t *sign_mantissa, const int32_t *decode_table, uint8_t *out,
@@ -1397,10 +1447,10 @@ static int decode_launch(const uint8_t *compressed, int64_t compressed_bytes,
                     (int32_t)(n_streams % 4 == 0 && aligned(sign_mantissa, 4) && aligned(out, 4))};
     cudaStream_t st = (cudaStream_t)stream;
     switch (ring_rows(segment_pairs)) {
-        case 16: return launch_ring_kernel<16>(decode_kernel<16>, args, 1, chains, sms, st, "decode_kernel");
-        case 32: return launch_ring_kernel<32>(decode_kernel<32>, args, 1, chains, sms, st, "decode_kernel");
-        case 64: return launch_ring_kernel<64>(decode_kernel<64>, args, 1, chains, sms, st, "decode_kernel");
-        default: return launch_ring_kernel<128>(decode_kernel<128>, args, 1, chains, sms, st, "decode_kernel");
+        case 16: return launch_decode<16>(args, chains, sms, st);
+        case 32: return launch_decode<32>(args, chains, sms, st);
+        case 64: return launch_decode<64>(args, chains, sms, st);
+        default: return launch_decode<128>(args, chains, sms, st);
     }
 }
 
@@ -1709,9 +1759,9 @@ extern "C" int tans_b200_decode_noalloc(const uint8_t *compressed, int64_t compr
                     n_fp8_per_stream, n_streams, n_fp8_per_stream / 2, status, make_opq(),
                     (int32_t)(n_streams % 4 == 0 && aligned(sign_mantissa, 4) && aligned(out, 4))};
     switch (ring_rows(n_fp8_per_stream / 2)) {
-        case 16: return launch_ring_kernel<16>(decode_kernel<16>, args, 1, n_streams, sms, st, "decode_kernel");
-        case 32: return launch_ring_kernel<32>(decode_kernel<32>, args, 1, n_streams, sms, st, "decode_kernel");
-        case 64: return launch_ring_kernel<64>(decode_kernel<64>, args, 1, n_streams, sms, st, "decode_kernel");
-        default: return launch_ring_kernel<128>(decode_kernel<128>, args, 1, n_streams, sms, st, "decode_kernel");
+        case 16: return launch_decode<16>(args, n_streams, sms, st);
+        case 32: return launch_decode<32>(args, n_streams, sms, st);
+        case 64: return launch_decode<64>(args, n_streams, sms, st);
+        default: return launch_decode<128>(args, n_streams, sms, st);
     }
 }
