@@ -6,11 +6,12 @@
 // tans_b200_fp8_vecadd_fused_range.
 //
 // Chunks are whole 128-stream encoder blocks, so each chunk's compressed
-// bytes are one contiguous range [offsets[b0], offsets[b1]) and its states /
-// partial counts are contiguous; its sign/mantissa tiles and output tiles
-// are column ranges of [N/16][K][8] / [N/16][K][16], copied with one 2D copy
-// each.  The device copies live at the same offsets in a caller-owned
-// workspace, so the kernel sees the full-size layout.
+// bytes are one contiguous range [offsets[b0], offsets[b1]); its
+// sign/mantissa tiles and output tiles are column ranges of [N/16][K][8] /
+// [N/16][K][16], copied with one 2D copy each.  The small metadata (offsets,
+// states, partial counts, table) is copied whole before the first chunk.
+// The device copies live at the same offsets in a caller-owned workspace,
+// so the kernel sees the full-size layout.
 
 #include "../../include/tans_b200.h"
 #include "internal.h"
@@ -175,10 +176,16 @@ extern "C" int tans_b200_fp8_vecadd_fused_host(
     // stream 0 brings the offsets and the table, the others wait for them
     PIPE_CHECK(cudaEventRecord(p->fork, user));
     for (int i = 0; i < kPipeStreams; i++) PIPE_CHECK(cudaStreamWaitEvent(p->s[i], p->fork, 0));
+    // the small per-stream and per-block metadata goes over in one piece
+    // each up front (a few hundred KB); the chunks carry only the bulk data
     PIPE_CHECK(cudaMemcpyAsync(d_a_off, a_off, 4 * (B + 1), cudaMemcpyHostToDevice, p->s[0]));
     PIPE_CHECK(cudaMemcpyAsync(d_b_off, b_off, 4 * (B + 1), cudaMemcpyHostToDevice, p->s[0]));
     PIPE_CHECK(cudaMemcpyAsync(d_table, table, 4 * TANS_B200_TABLE_SIZE, cudaMemcpyHostToDevice,
                                p->s[0]));
+    PIPE_CHECK(cudaMemcpyAsync(d_a_st, a_st, 2 * K, cudaMemcpyHostToDevice, p->s[0]));
+    PIPE_CHECK(cudaMemcpyAsync(d_b_st, b_st, 2 * K, cudaMemcpyHostToDevice, p->s[0]));
+    PIPE_CHECK(cudaMemcpyAsync(d_a_part, a_part, K, cudaMemcpyHostToDevice, p->s[0]));
+    PIPE_CHECK(cudaMemcpyAsync(d_b_part, b_part, K, cudaMemcpyHostToDevice, p->s[0]));
     PIPE_CHECK(cudaEventRecord(p->meta, p->s[0]));
     for (int i = 1; i < kPipeStreams; i++) PIPE_CHECK(cudaStreamWaitEvent(p->s[i], p->meta, 0));
 
@@ -192,10 +199,6 @@ extern "C" int tans_b200_fp8_vecadd_fused_host(
                                    cudaMemcpyHostToDevice, st));
         PIPE_CHECK(cudaMemcpyAsync(d_b_comp + b_off[b0], b_comp + b_off[b0], b_off[b1] - b_off[b0],
                                    cudaMemcpyHostToDevice, st));
-        PIPE_CHECK(cudaMemcpyAsync(d_a_st + s0, a_st + s0, 2 * ns, cudaMemcpyHostToDevice, st));
-        PIPE_CHECK(cudaMemcpyAsync(d_b_st + s0, b_st + s0, 2 * ns, cudaMemcpyHostToDevice, st));
-        PIPE_CHECK(cudaMemcpyAsync(d_a_part + s0, a_part + s0, ns, cudaMemcpyHostToDevice, st));
-        PIPE_CHECK(cudaMemcpyAsync(d_b_part + s0, b_part + s0, ns, cudaMemcpyHostToDevice, st));
         PIPE_CHECK(cudaMemcpy2DAsync(d_a_sm + 8 * s0, 8 * K, a_sm + 8 * s0, 8 * K, 8 * ns, tiles,
                                      cudaMemcpyHostToDevice, st));
         PIPE_CHECK(cudaMemcpy2DAsync(d_b_sm + 8 * s0, 8 * K, b_sm + 8 * s0, 8 * K, 8 * ns, tiles,
