@@ -259,6 +259,13 @@ int tans_b200_gemv_weight_dense(const uint8_t *compressed,
                                 int64_t rows, int64_t cols, int64_t col_splits,
                                 int32_t *status, void *stream);
 
+/* Prefill epilogue: y[m][r] = bf16(acc[m][r] * scale[r]) for an fp32 GEMM
+ * output acc [m][rows] (rows % 4 == 0; acc and scale 16-byte aligned, y
+ * 8-byte aligned); one rounding. */
+int tans_b200_scale_rows_bf16(const float *acc, const float *scale,
+                              uint16_t *y, int64_t m, int64_t rows,
+                              void *stream);
+
 /* Allocation-free standalone decode.  No counterpart in the reference: it
  * exists for callers that cannot allocate device memory (a runtime that
  * hands the library only buffers carved from a pre-sized pool, or a

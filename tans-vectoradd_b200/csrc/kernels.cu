@@ -1198,7 +1198,15 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_dense_kernel(const Den
         // stream group g = (w * KS + k) * 2 + chain
         const int64_t chain = g & 1, wk = g >> 1, k = wk % p.KS, w = wk / p.KS;
         const int64_t row = 16 * w + (lane >> 2) + 8 * chain;
-        uint32_t *dst = reinterpret_cast<uint32_t *>(p.w + row * p.C + k * CS + 2 * (lane & 3));
+        // warp-private staging of one tile: 8 rows x 64 bf16 (row stride 36
+        // words, conflict-free), written back as 16-byte stores that cover
+        // whole 128-byte row pieces
+        uint32_t *stage = reinterpret_cast<uint32_t *>(
+            smem + (ring_area<R>(smem, blockDim.x >> 5, 1) - smem_addr(smem)) + warp * 1152);
+        const int64_t row0 = 16 * w + 8 * chain;
+        uint8_t *dst = reinterpret_cast<uint8_t *>(p.w + (row0 + (lane >> 3)) * p.C + k * CS) +
+                       (lane & 7) * 16;
+        (void)row;
         const uint8_t *sp = p.sm + sid * 8;
         uint2 m_n = live ? ld_stream_v2(sp) : make_uint2(0, 0);
         for (int32_t t = 0; t < n_tiles; t++) {
@@ -1221,12 +1229,23 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_dense_kernel(const Den
             uint32_t wd[4];
             compose_pairs(gather_syms(e[0], e[1], e[2], e[3]), m.x, p.q, wd[0], wd[1]);
             compose_pairs(gather_syms(e[4], e[5], e[6], e[7]), m.y, p.q, wd[2], wd[3]);
+            uint32_t *sw = stage + (lane >> 2) * kStageRowWords + (lane & 3);
 #pragma unroll
             for (int c = 0; c < 4; c++) {  // 16-column chunk 4t + c
-                uint32_t *d = dst + (int64_t)(4 * t + c) * 8;
-                d[0] = live ? cvt_bf16x2_e4m3x2(wd[c] & 0xFFFFu) : 0u;  // columns 2t, 2t+1
-                d[4] = live ? cvt_bf16x2_e4m3x2(wd[c] >> 16) : 0u;      // columns 8+2t, 9+2t
+                sw[c * 8] = live ? cvt_bf16x2_e4m3x2(wd[c] & 0xFFFFu) : 0u;  // columns 2t, 2t+1
+                sw[c * 8 + 4] = live ? cvt_bf16x2_e4m3x2(wd[c] >> 16) : 0u;  // columns 8+2t, 9+2t
             }
+            __syncwarp();
+            const uint32_t *sr = stage + (lane >> 3) * kStageRowWords + (lane & 7) * 4;
+#pragma unroll
+            for (int h = 0; h < 2; h++) {  // rows (lane >> 3) + 4h
+                const uint4 v = *reinterpret_cast<const uint4 *>(sr + h * 4 * kStageRowWords);
+                asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(
+                                 dst + (int64_t)h * 4 * p.C * 2 + (int64_t)t * 128),
+                             "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                             : "memory");
+            }
+            __syncwarp();
         }
         cp_async_wait<0>();
     }
@@ -1646,6 +1665,35 @@ extern "C" int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_byte
     return launch_status("gemv_reduce_kernel");
 }
 
+// y[m][r] = bf16(acc[m][r] * scale[r]): the prefill epilogue after the
+// library GEMM (fp32 output), one rounding; 4 columns per thread.
+__global__ void scale_rows_bf16_kernel(const float4 *__restrict__ acc, const float *__restrict__ scale,
+                                       uint2 *__restrict__ y, int64_t n4, int64_t R4) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float4 a = acc[i];
+        const float4 sc = reinterpret_cast<const float4 *>(scale)[i % R4];
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(a.x * sc.x, a.y * sc.y);
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(a.z * sc.z, a.w * sc.w);
+        y[i] = make_uint2(*reinterpret_cast<const uint32_t *>(&lo),
+                          *reinterpret_cast<const uint32_t *>(&hi));
+    }
+}
+
+// Dense decode launch: per warp a slab ring and a 1152-byte staging tile.
+template <int R>
+int launch_dense(const DenseArgs &args, int64_t chains, int sms, cudaStream_t st) {
+    const int per_warp = R * 128 + 1152;
+    int max_w = (kSmemMax - kTableBytes - R * 128) / per_warp;
+    if (max_w > kMaxWarps) max_w = kMaxWarps;
+    const Geometry geo = balance((chains + 31) / 32, sms, max_w);
+    const int smem = kTableBytes + R * 128 + geo.warps_per_cta * per_warp;
+    int rc = set_smem(gemv_dense_kernel<R>, smem);
+    if (rc) return rc;
+    gemv_dense_kernel<R><<<geo.grid, geo.warps_per_cta * 32, smem, st>>>(args);
+    return launch_status("gemv_dense_kernel");
+}
+
 extern "C" int tans_b200_gemv_weight_dense(const uint8_t *compressed, int64_t compressed_bytes,
                                            const int32_t *offsets, const uint16_t *states,
                                            const uint8_t *partial, const uint8_t *sm,
@@ -1673,11 +1721,31 @@ extern "C" int tans_b200_gemv_weight_dense(const uint8_t *compressed, int64_t co
     const int64_t chains = rows * 4 * col_splits;
     cudaStream_t st = (cudaStream_t)stream;
     switch (ring_rows(cols / col_splits / 8)) {
-        case 16: return launch_ring_kernel<16>(gemv_dense_kernel<16>, args, 1, chains, sms, st, "gemv_dense_kernel");
-        case 32: return launch_ring_kernel<32>(gemv_dense_kernel<32>, args, 1, chains, sms, st, "gemv_dense_kernel");
-        case 64: return launch_ring_kernel<64>(gemv_dense_kernel<64>, args, 1, chains, sms, st, "gemv_dense_kernel");
-        default: return launch_ring_kernel<128>(gemv_dense_kernel<128>, args, 1, chains, sms, st, "gemv_dense_kernel");
+        case 16: return launch_dense<16>(args, chains, sms, st);
+        case 32: return launch_dense<32>(args, chains, sms, st);
+        case 64: return launch_dense<64>(args, chains, sms, st);
+        default: return launch_dense<128>(args, chains, sms, st);
     }
+}
+
+extern "C" int tans_b200_scale_rows_bf16(const float *acc, const float *scale, uint16_t *y,
+                                         int64_t m, int64_t rows, void *stream) {
+    tans_b200::clear_error();
+    if (m < 0 || rows <= 0 || rows % 4 != 0)
+        return fail(TANS_B200_ERR_INVALID, "scale_rows_bf16: rows must be a positive multiple of 4");
+    if (m == 0) return TANS_B200_OK;
+    if (!acc || !scale || !y) return fail(TANS_B200_ERR_INVALID, "scale_rows_bf16: null pointer");
+    if (!aligned(acc, 16) || !aligned(scale, 16) || !aligned(y, 8))
+        return fail(TANS_B200_ERR_INVALID, "scale_rows_bf16: misaligned buffer");
+    int sms;
+    int rc = device_setup(&sms);
+    if (rc) return rc;
+    const int64_t n4 = m * rows / 4;
+    const int64_t blocks = (n4 + 255) / 256;
+    scale_rows_bf16_kernel<<<(unsigned)(blocks < 8 * sms ? blocks : 8 * sms), 256, 0,
+                             (cudaStream_t)stream>>>(reinterpret_cast<const float4 *>(acc), scale,
+                                                     reinterpret_cast<uint2 *>(y), n4, rows / 4);
+    return launch_status("scale_rows_bf16_kernel");
 }
 
 // ------------------------------------------------------- allocation-free decode

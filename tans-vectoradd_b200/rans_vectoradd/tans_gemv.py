@@ -167,8 +167,14 @@ def gemm(weight: EncodedWeight, x: torch.Tensor, w_dense: torch.Tensor | None = 
     if x.shape[0] <= 8:
         return gemv(weight, x)
     w = dense_weight(weight) if w_dense is None else w_dense
-    y = torch.mm(x, w.t(), out_dtype=torch.float32)
-    return (y * weight.scale).to(torch.bfloat16)
+    acc = torch.mm(x, w.t(), out_dtype=torch.float32)
+    R = weight.rows
+    dev = x.device
+    with torch.cuda.device(dev):
+        y = torch.empty((x.shape[0], R), dtype=torch.bfloat16, device=dev)
+        check(LIB.tans_b200_scale_rows_bf16(acc.data_ptr(), weight.scale.data_ptr(), y.data_ptr(),
+                                            x.shape[0], R, _stream(dev)))
+    return y
 
 
 def reference_gemv(w8: torch.Tensor, scale: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
