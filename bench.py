@@ -680,7 +680,7 @@ def main():
     if ws > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=dev)
         barrier = lambda: dist.barrier(device_ids=[local])  # noqa: E731
     else:
