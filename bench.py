@@ -575,7 +575,7 @@ def run_gemm(args, dev, barrier):
             "dense_decode_us": round(ms_dec * 1e3, 2),
             "dense_decode_gbs_e4m3": round(R * C / (ms_dec / 1e3) / 1e9, 1),
             "dense_exact": exact, "batches": []}
-    for B in (64, 512, 2048):
+    for B in (16, 64, 256, 512, 2048):
         g = torch.Generator(device=dev).manual_seed(B)
         x = torch.randn(B, C, device=dev, generator=g).to(torch.bfloat16)
         y = tans_gemv.gemm(enc, x)
@@ -584,12 +584,19 @@ def run_gemm(args, dev, barrier):
                    barrier) / args.steps
         ms_mm = timed(lambda: torch.mm(x, w.t(), out_dtype=torch.float32), args.steps,
                       args.warmup, stream, barrier) / args.steps
+        y_tc = tans_gemv.gemm_tc(enc, x)
+        err_tc = tans_gemv.rel_err(y_tc, tans_gemv.reference_gemv(w8, s, x))
+        ms_tc = timed(lambda: tans_gemv.gemm_tc(enc, x, y_tc), args.steps, args.warmup, stream,
+                      barrier) / args.steps
         fl = 2.0 * B * R * C
         line["batches"].append({"batch": B, "us": round(ms * 1e3, 1),
                                 "tflops": round(fl / (ms / 1e3) / 1e12, 1),
                                 "gemm_only_us": round(ms_mm * 1e3, 1),
                                 "gemm_only_tflops": round(fl / (ms_mm / 1e3) / 1e12, 1),
-                                "rel_err": err})
+                                "rel_err": err,
+                                "tc_fused_us": round(ms_tc * 1e3, 1),
+                                "tc_fused_tflops": round(fl / (ms_tc / 1e3) / 1e12, 1),
+                                "tc_fused_rel_err": err_tc})
     emit(line, args)
 
 

@@ -259,6 +259,22 @@ int tans_b200_gemv_weight_dense(const uint8_t *compressed,
                                 int64_t rows, int64_t cols, int64_t col_splits,
                                 int32_t *status, void *stream);
 
+/* Prefill GEMM with the weight decoded on the fly: y [m][rows] bf16 =
+ * scale * W @ x^T for x bf16 [m][cols] (16-byte aligned), W in the GEMV
+ * stream format (tans_b200_gemv).  Tensor cores (tcgen05.mma, bf16 in, fp32
+ * accumulate in tensor memory); W never goes through HBM decoded.
+ * rows % 128 == 0; tokens are processed 256 per CTA (the weight is decoded
+ * once per 256 tokens).  A bounded wait that runs out sets bit 8 of the
+ * optional status word (no result for that CTA's rows).  No reference
+ * counterpart. */
+int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_bytes,
+                      const int32_t *offsets, const uint16_t *states,
+                      const uint8_t *partial, const uint8_t *sign_mantissa,
+                      const int32_t *decode_table, const float *scale,
+                      const uint16_t *x, uint16_t *y, int64_t rows,
+                      int64_t cols, int64_t col_splits, int64_t m,
+                      int32_t *status, void *stream);
+
 /* Prefill epilogue: y[m][r] = bf16(acc[m][r] * scale[r]) for an fp32 GEMM
  * output acc [m][rows] (rows % 4 == 0; acc and scale 16-byte aligned, y
  * 8-byte aligned); one rounding. */

@@ -1251,6 +1251,244 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_dense_kernel(const Den
     }
 }
 
+// ------------------------------------------- prefill: decode + tcgen05 MMA
+//
+// y[m][r] = bf16(scale[r] * sum_c e4m3(W[r][c]) * x[m][c]) for a tile of up
+// to kTcMaxTokens tokens, with W read in the GEMV stream layout and never
+// written out: a CTA owns 128 rows of W (8 row groups x 2 chains = 16 warps,
+// one tANS chain per lane) and walks the columns in 64-column chunks.  Per
+// chunk each warp decodes one 8-pair tile of its streams straight into a
+// bf16 A tile in shared memory (K-major, 128-byte swizzle), all threads copy
+// the x chunk into the B tile (same layout), and one thread issues four
+// tcgen05.mma (M = 128, N = tokens, K = 16, bf16 in, fp32 accumulate in
+// tensor memory) and commits them to the stage's mbarrier.  Two stages, so
+// the decode of chunk c+1 overlaps the MMAs of chunk c.  Warps 0-3 then read
+// the accumulator rows back (tcgen05.ld), scale, round once to bf16 and
+// store.  Every mbarrier wait is bounded; a wait that runs out sets
+// TANS_B200_DATA_BAD_TABLE | 8 in the status word and the CTA skips its
+// epilogue but still frees its tensor memory.
+
+constexpr int kTcWarps = 16;
+constexpr int kTcMaxTokens = 256;
+constexpr int kTcATile = 128 * 128;   // 128 rows x 64 bf16
+constexpr uint32_t kTcWaitLimit = 1u << 22;
+constexpr int32_t kTcTimeoutBit = 8;
+
+struct TcArgs {
+    const uint32_t *comp;
+    int64_t comp_bytes;
+    const int32_t *offsets;
+    const uint16_t *states;
+    const uint8_t *partial;
+    const uint8_t *sm;        // [N/16][K][8]
+    const int32_t *table;
+    const float *scale;       // [R]
+    const uint16_t *x;        // bf16 [M][C]
+    uint16_t *y;              // bf16 [M][R]
+    int64_t R, C, KS, M;
+    int32_t nt;               // tokens per CTA (multiple of 16, <= 256)
+    int32_t *status;
+    Opq q;
+};
+
+// K-major, 128-byte-swizzle shared-memory matrix descriptor: 8-row groups
+// 1024 bytes apart (stride byte offset), descriptor version 1.
+__device__ __forceinline__ uint64_t tc_smem_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Byte offset of bf16 element (row, k) in a 128-row x 64 K-major tile with
+// the 128-byte swizzle (16-byte chunk index XOR row % 8).
+__device__ __forceinline__ uint32_t tc_swz(uint32_t row, uint32_t k) {
+    return (row >> 3) * 1024u + (row & 7u) * 128u + ((((k >> 3) ^ row) & 7u) << 4) + (k & 7u) * 2u;
+}
+
+__device__ __forceinline__ bool tc_wait(uint32_t mbar, uint32_t parity) {
+    for (uint32_t i = 0; i < kTcWaitLimit; i++) {
+        uint32_t done;
+        asm volatile(
+            "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+            "selp.b32 %0, 1, 0, P1;\n\t}"
+            : "=r"(done)
+            : "r"(mbar), "r"(parity)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+template <int R>
+__global__ void __launch_bounds__(kTcWarps * 32, 1) gemm_tc_kernel(const TcArgs p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    __shared__ __align__(8) uint64_t mbar[2];
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int32_t failed_s;
+    load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t4 = lane & 3;
+    const uint32_t lane_off = 4u * (lane % kCopies);
+    const uint32_t mask = (uint32_t)(R - 1) << 7;
+    Ring rg;
+    rg.lane_base = ring_area<R>(smem, warp, 1) + 4u * lane;
+    // A and B stages after the rings, 1024-byte aligned
+    const uint32_t base_sa = smem_addr(smem);
+    const uint32_t a_sa = (ring_area<R>(smem, kTcWarps, 1) + 1023u) & ~1023u;
+    const uint32_t b_sa = a_sa + 2u * kTcATile;
+    const uint32_t b_bytes = (uint32_t)p.nt * 128u;
+    uint8_t *a_ptr = smem + (a_sa - base_sa);
+    uint8_t *b_ptr = smem + (b_sa - base_sa);
+    const uint32_t mb0 = smem_addr(&mbar[0]), mb1 = smem_addr(&mbar[1]);
+    const uint32_t ncols = p.nt <= 32 ? 32u : (p.nt <= 64 ? 64u : (p.nt <= 128 ? 128u : 256u));
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_addr(&tmem_base_s)), "r"(ncols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (threadIdx.x == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mb0));
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mb1));
+        asm volatile("fence.mbarrier_init.release.cluster;");
+        failed_s = 0;
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const uint32_t tmem = tmem_base_s;
+    const uint8_t *tb = smem;
+
+    const int64_t CS = p.C / p.KS, K = p.R * 4 * p.KS;
+    const int32_t tps = (int32_t)(CS / 64), nchunks = (int32_t)(p.C / 64);
+    const int rgrp = warp >> 1, chain = warp & 1;
+    const int64_t wg = (int64_t)blockIdx.x * 8 + rgrp;          // global 16-row group
+    const uint32_t row = (uint32_t)(16 * rgrp + g + 8 * chain);  // row within the tile
+    const int64_t m0 = (int64_t)blockIdx.y * p.nt;
+    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.nt >> 3) << 17) |
+                           ((uint32_t)(128 >> 4) << 24);
+    Chain ch;
+    chain_idle(ch, p.comp);
+    bool live = false;
+    const uint8_t *sp = p.sm;
+    uint2 m_n = make_uint2(0, 0);
+    bool ok = true;
+    for (int32_t c = 0; c < nchunks; c++) {
+        const int32_t kslice = c / tps, tt = c % tps;
+        if (tt == 0) {  // this slice's streams
+            const int64_t sid = ((wg * p.KS + kslice) * 2 + chain) * 32 + lane;
+            const int32_t G = chain_init(ch, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
+                                         sid, lane_off, p.status);
+            live = G > 0;
+            if (!live) chain_idle(ch, p.comp);
+            cp_async_wait<0>();
+            ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, live ? G : 0), live);
+            cp_async_commit();
+            cp_async_wait<0>();
+            sp = p.sm + sid * 8;
+            m_n = live ? ld_stream_v2(sp) : make_uint2(0, 0);
+        }
+        const int s = c & 1;
+        if (c >= 2 && ok && !tc_wait(s ? mb1 : mb0, (uint32_t)(((c >> 1) - 1) & 1))) ok = false;
+        // x chunk -> B stage s (rows past M are zero), in flight during the decode
+        const uint32_t bs = b_sa + (uint32_t)s * (uint32_t)kTcMaxTokens * 128u;
+        for (int pc = threadIdx.x; pc < p.nt * 8; pc += blockDim.x) {
+            const int n = pc >> 3, q8 = pc & 7;
+            const int64_t mrow = m0 + n;
+            const uint16_t *src = p.x + (mrow < p.M ? mrow : 0) * p.C + (int64_t)c * 64 + q8 * 8;
+            const uint32_t dst = bs + (uint32_t)(n >> 3) * 1024u + (uint32_t)(n & 7) * 128u +
+                                 ((uint32_t)((q8 ^ n) & 7) << 4);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+                         "r"(mrow < p.M ? 16 : 0)
+                         : "memory");
+        }
+        cp_async_commit();
+        // decode this warp's tile of chunk c into A stage s
+        const uint2 m = m_n;
+        sp += K * 8;
+        if (live && tt + 1 < tps) m_n = ld_stream_v2(sp);
+        const int32_t need = ring_fill<R>(rg, ch, live);
+        cp_async_commit();
+        // groups: ..., ring(c-1), x(c), ring(c): the decode needs only ring(c-1);
+        // the x chunk keeps loading under the decode
+        cp_async_wait<2>();
+        uint32_t e[kTablePairs];
+        if (need >= rg.done[kDecodeLag]) {
+#pragma unroll
+            for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
+        } else {
+#pragma unroll
+            for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_global(ch, tb, p.q);
+        }
+        uint32_t wd[4];
+        compose_pairs(gather_syms(e[0], e[1], e[2], e[3]), m.x, p.q, wd[0], wd[1]);
+        compose_pairs(gather_syms(e[4], e[5], e[6], e[7]), m.y, p.q, wd[2], wd[3]);
+        uint8_t *at = a_ptr + s * kTcATile;
+#pragma unroll
+        for (int j = 0; j < 4; j++) {  // 16-column sub-chunk j: columns 2t, 2t+1 | 8+2t, 9+2t
+            const uint32_t lo = live ? cvt_bf16x2_e4m3x2(wd[j] & 0xFFFFu) : 0u;
+            const uint32_t hi = live ? cvt_bf16x2_e4m3x2(wd[j] >> 16) : 0u;
+            *reinterpret_cast<uint32_t *>(at + tc_swz(row, 16 * j + 2 * t4)) = lo;
+            *reinterpret_cast<uint32_t *>(at + tc_swz(row, 16 * j + 8 + 2 * t4)) = hi;
+        }
+        cp_async_wait<1>();  // the x chunk (everything but this tile's ring fills)
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncthreads();
+        if (threadIdx.x == 0 && ok) {
+            asm volatile("tcgen05.fence::after_thread_sync;");
+            const uint32_t as = a_sa + (uint32_t)s * kTcATile;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const uint64_t ad = tc_smem_desc(as + 32u * j), bd = tc_smem_desc(bs + 32u * j);
+                asm volatile(
+                    "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                    "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+                        tmem),
+                    "l"(ad), "l"(bd), "r"(idesc), "r"((uint32_t)(c > 0 || j > 0)), "r"(0u), "r"(0u),
+                    "r"(0u), "r"(0u));
+            }
+            asm volatile(
+                "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                    s ? mb1 : mb0)
+                : "memory");
+        }
+    }
+    cp_async_wait<0>();
+    // all MMAs done (they complete in order): wait for the last commit
+    if (nchunks > 0 && ok) {
+        const int32_t cl = nchunks - 1;
+        if (!tc_wait((cl & 1) ? mb1 : mb0, (uint32_t)((cl >> 1) & 1))) ok = false;
+    }
+    if (!ok) atomicOr(&failed_s, 1);
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+    const bool good = failed_s == 0;
+    if (warp < 4 && good) {
+        const int64_t r = (int64_t)blockIdx.x * 128 + 32 * warp + lane;
+        const float sc = p.scale[r];
+        for (int col = 0; col < p.nt; col += 8) {
+            uint32_t v[8];
+            asm volatile(
+                "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
+                  "=r"(v[6]), "=r"(v[7])
+                : "r"(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)col));
+            asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int64_t mm = m0 + col + i;
+                if (mm < p.M)
+                    p.y[mm * p.R + r] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]) * sc));
+            }
+        }
+    }
+    if (!good && threadIdx.x == 0 && p.status) atomicOr(p.status, kTcTimeoutBit);
+    asm volatile("tcgen05.fence::before_thread_sync;");
+    __syncthreads();
+    if (warp == 0) {
+        asm volatile("tcgen05.fence::after_thread_sync;");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+    }
+}
+
 // ------------------------------------------------------------- host glue
 
 constexpr int kMaxDevices = 64;
@@ -1746,6 +1984,46 @@ extern "C" int tans_b200_scale_rows_bf16(const float *acc, const float *scale, u
                              (cudaStream_t)stream>>>(reinterpret_cast<const float4 *>(acc), scale,
                                                      reinterpret_cast<uint2 *>(y), n4, rows / 4);
     return launch_status("scale_rows_bf16_kernel");
+}
+
+extern "C" int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_bytes,
+                                 const int32_t *offsets, const uint16_t *states,
+                                 const uint8_t *partial, const uint8_t *sm,
+                                 const int32_t *decode_table, const float *scale,
+                                 const uint16_t *x, uint16_t *y, int64_t rows, int64_t cols,
+                                 int64_t col_splits, int64_t m, int32_t *status, void *stream) {
+    tans_b200::clear_error();
+    if (rows <= 0 || rows % 128 != 0)
+        return fail(TANS_B200_ERR_INVALID, "gemm_tc: rows must be a positive multiple of 128");
+    if (col_splits < 1 || cols <= 0 || cols % (64 * col_splits) != 0)
+        return fail(TANS_B200_ERR_INVALID, "gemv: cols must be a positive multiple of 64 * col_splits");
+    if (m < 1) return fail(TANS_B200_ERR_INVALID, "gemm_tc: m must be >= 1");
+    if (!compressed || !offsets || !states || !partial || !sm || !decode_table || !scale || !x || !y)
+        return fail(TANS_B200_ERR_INVALID, "gemm_tc: null pointer");
+    if (!aligned(compressed, 4) || !aligned(offsets, 4) || !aligned(states, 2) || !aligned(sm, 8) ||
+        !aligned(decode_table, 4) || !aligned(scale, 4) || !aligned(x, 16) || !aligned(y, 2))
+        return fail(TANS_B200_ERR_INVALID, "gemm_tc: misaligned buffer (x needs 16 bytes)");
+    if (compressed_bytes < 0 || compressed_bytes % 4 != 0)
+        return fail(TANS_B200_ERR_INVALID, "compressed length must be divisible by 4 bytes");
+    int sms;
+    int rc = device_setup(&sms);
+    if (rc) return rc;
+    // tokens per CTA: all of them up to 256 (multiple of 16), else 256-token tiles
+    int nt = (int)((m + 15) / 16 * 16);
+    if (nt > kTcMaxTokens) nt = kTcMaxTokens;
+    const int64_t ty = (m + nt - 1) / nt;
+    constexpr int rr = 16;  // ring rows: slices are at most a few hundred pair symbols long
+    const int smem = kTableBytes + rr * 128 + kTcWarps * rr * 128 + 1024 + 2 * kTcATile +
+                     2 * kTcMaxTokens * 128;
+    if (smem > kSmemMax) return fail(TANS_B200_ERR_INVALID, "gemm_tc: shared memory");
+    TcArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets, states,
+                partial, sm, decode_table, scale, x, y, rows, cols, col_splits, m, nt, status,
+                make_opq()};
+    rc = set_smem(gemm_tc_kernel<rr>, smem);
+    if (rc) return rc;
+    gemm_tc_kernel<rr><<<dim3((unsigned)(rows / 128), (unsigned)ty), kTcWarps * 32, smem,
+                         (cudaStream_t)stream>>>(args);
+    return launch_status("gemm_tc_kernel");
 }
 
 // ------------------------------------------------------- allocation-free decode

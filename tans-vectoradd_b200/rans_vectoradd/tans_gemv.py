@@ -177,6 +177,28 @@ def gemm(weight: EncodedWeight, x: torch.Tensor, w_dense: torch.Tensor | None = 
     return y
 
 
+def gemm_tc(weight: EncodedWeight, x: torch.Tensor, out: torch.Tensor | None = None
+            ) -> torch.Tensor:
+    """y [batch, rows] bf16 = scale * W @ x^T on the tensor cores with W
+    decoded on the fly into shared memory (tcgen05; rows % 128 == 0)."""
+    _req(x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(),
+         "x must be a contiguous CUDA bfloat16 [batch, cols] tensor")
+    B, C = x.shape
+    _req(C == weight.cols, f"x has {C} columns, the weight {weight.cols}")
+    dev = x.device
+    _same_device(dev, weight.compressed, weight.offsets, weight.states, weight.partial,
+                 weight.sm, weight.table, weight.scale)
+    with torch.cuda.device(dev):
+        if out is None:
+            out = torch.empty((B, weight.rows), dtype=torch.bfloat16, device=dev)
+        check(LIB.tans_b200_gemm_tc(
+            weight.compressed.data_ptr(), weight.compressed.numel(), weight.offsets.data_ptr(),
+            weight.states.data_ptr(), weight.partial.data_ptr(), weight.sm.data_ptr(),
+            weight.table.data_ptr(), weight.scale.data_ptr(), x.data_ptr(), out.data_ptr(),
+            weight.rows, C, weight.col_splits, B, _status(dev).data_ptr(), _stream(dev)))
+    return out
+
+
 def reference_gemv(w8: torch.Tensor, scale: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """Decode-then-dense fp32 reference: bf16((W8.float() * s) @ x.float()^T)."""
     w = w8.view(torch.float8_e4m3fn).float() * scale.float()[:, None]
@@ -189,4 +211,4 @@ def rel_err(y: torch.Tensor, y_ref: torch.Tensor) -> float:
 
 
 __all__ = ["EncodedWeight", "quantize_rows", "stream_matrix", "encode_weight", "gemv",
-           "dense_weight", "gemm", "reference_gemv", "rel_err"]
+           "dense_weight", "gemm", "gemm_tc", "reference_gemv", "rel_err"]

@@ -127,3 +127,20 @@ def test_gemm_large_batch_matches_reference(cuda, B):
     y = tans_gemv.gemm(enc, x)
     ref = tans_gemv.reference_gemv(w8.to(cuda), s.to(cuda), x)
     assert y.shape == (B, R) and tans_gemv.rel_err(y, ref) <= TOL
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("R,C,B,KS", [(128, 512, 16, 1), (256, 1024, 40, 1), (1024, 5120, 64, 5),
+                                      (512, 4352, 300, 4), (17408, 5120, 256, None)])
+def test_gemm_tc_matches_reference(cuda, R, C, B, KS):
+    """Decode into shared memory + tcgen05 MMA: rel err within the GEMV bound,
+    tokens beyond one 256-token tile and ragged token counts included."""
+    from rans_vectoradd import _C
+    w8, s = make(R, C, R + 7 * C)
+    enc = tans_gemv.encode_weight(w8.to(cuda), s.to(cuda), col_splits=KS)
+    x = torch.randn(B, C, generator=torch.Generator().manual_seed(B)).to(torch.bfloat16).to(cuda)
+    _C.data_status(cuda)
+    y = tans_gemv.gemm_tc(enc, x)
+    assert _C.data_status(cuda) == 0
+    ref = tans_gemv.reference_gemv(w8.to(cuda), s.to(cuda), x)
+    assert tans_gemv.rel_err(y, ref) <= TOL
