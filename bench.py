@@ -559,10 +559,11 @@ def run_gemv(args, dev, barrier):
 
 def run_gemm(args, dev, barrier):
     """Prefill-size batches on the cfg3 weight [17408 x 5120]: the dense
-    bf16 decode of the encoded weight (GB/s of e4m3 output) and
-    tans_gemv.gemm (decode + library bf16 GEMM with fp32 output + per-row
-    scale) against the GEMM alone on a pre-decoded weight; rel err vs the
-    decode-then-dense fp32 reference."""
+    bf16 decode of the encoded weight (GB/s of e4m3 output), tans_gemv.gemm
+    (the dispatching entry), both of its large-batch forms — gemm_tc (decode
+    into shared memory + tcgen05 MMA) and gemm_dense (dense decode + library
+    bf16 GEMM with fp32 output + per-row scale) — and the GEMM alone on a
+    pre-decoded weight; rel err vs the decode-then-dense fp32 reference."""
     from rans_vectoradd import tans_gemv
     stream = torch.cuda.current_stream(dev)
     R, C = 17408, 5120
@@ -582,6 +583,8 @@ def run_gemm(args, dev, barrier):
         err = tans_gemv.rel_err(y, tans_gemv.reference_gemv(w8, s, x))
         ms = timed(lambda: tans_gemv.gemm(enc, x), args.steps, args.warmup, stream,
                    barrier) / args.steps
+        ms_dense = timed(lambda: tans_gemv.gemm_dense(enc, x), args.steps, args.warmup, stream,
+                         barrier) / args.steps
         ms_mm = timed(lambda: torch.mm(x, w.t(), out_dtype=torch.float32), args.steps,
                       args.warmup, stream, barrier) / args.steps
         y_tc = tans_gemv.gemm_tc(enc, x)
@@ -591,6 +594,8 @@ def run_gemm(args, dev, barrier):
         fl = 2.0 * B * R * C
         line["batches"].append({"batch": B, "us": round(ms * 1e3, 1),
                                 "tflops": round(fl / (ms / 1e3) / 1e12, 1),
+                                "path": "tc_fused" if 8 < B <= tans_gemv.TC_MAX_BATCH else "dense",
+                                "dense_path_us": round(ms_dense * 1e3, 1),
                                 "gemm_only_us": round(ms_mm * 1e3, 1),
                                 "gemm_only_tflops": round(fl / (ms_mm / 1e3) / 1e12, 1),
                                 "rel_err": err,

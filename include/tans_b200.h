@@ -40,6 +40,7 @@ extern "C" {
 #define TANS_B200_DATA_BAD_OFFSETS 1 /* block offsets not monotone/in range */
 #define TANS_B200_DATA_BAD_STATE 2   /* initial state outside [4096, 8192)  */
 #define TANS_B200_DATA_BAD_TABLE 4   /* spread/freqs/table entry malformed  */
+#define TANS_B200_DATA_TIMEOUT 8     /* a bounded in-kernel wait ran out    */
 
 #define TANS_B200_TABLE_SIZE 4096   /* L = M, tans_codec.py:24-25 */
 #define TANS_B200_BLOCK_STREAMS 128 /* tans_codec.py:27          */
@@ -264,8 +265,9 @@ int tans_b200_gemv_weight_dense(const uint8_t *compressed,
  * stream format (tans_b200_gemv).  Tensor cores (tcgen05.mma, bf16 in, fp32
  * accumulate in tensor memory); W never goes through HBM decoded.
  * rows % 128 == 0; tokens are processed 256 per CTA (the weight is decoded
- * once per 256 tokens).  A bounded wait that runs out sets bit 8 of the
- * optional status word (no result for that CTA's rows).  No reference
+ * once per 256 tokens).  A bounded wait that runs out ORs
+ * TANS_B200_DATA_TIMEOUT into the optional status word (no result for that
+ * CTA's rows).  No reference
  * counterpart. */
 int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_bytes,
                       const int32_t *offsets, const uint16_t *states,

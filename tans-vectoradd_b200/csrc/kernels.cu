@@ -40,6 +40,7 @@
 
 #include "../../include/tans_b200.h"
 
+#include <cuda.h>  // CUtensorMap and its enums (the encoder is resolved at run time)
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -1255,26 +1256,36 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_dense_kernel(const Den
 //
 // y[m][r] = bf16(scale[r] * sum_c e4m3(W[r][c]) * x[m][c]) for a tile of up
 // to kTcMaxTokens tokens, with W read in the GEMV stream layout and never
-// written out: a CTA owns 128 rows of W (8 row groups x 2 chains = 16 warps,
-// one tANS chain per lane) and walks the columns in 64-column chunks.  Per
-// chunk each warp decodes one 8-pair tile of its streams straight into a
-// bf16 A tile in shared memory (K-major, 128-byte swizzle), all threads copy
-// the x chunk into the B tile (same layout), and one thread issues four
-// tcgen05.mma (M = 128, N = tokens, K = 16, bf16 in, fp32 accumulate in
-// tensor memory) and commits them to the stage's mbarrier.  Two stages, so
-// the decode of chunk c+1 overlaps the MMAs of chunk c.  Warps 0-3 then read
-// the accumulator rows back (tcgen05.ld), scale, round once to bf16 and
-// store.  Every mbarrier wait is bounded; a wait that runs out sets
-// TANS_B200_DATA_BAD_TABLE | 8 in the status word and the CTA skips its
-// epilogue but still frees its tensor memory.
+// written out.  A CTA owns 128 rows of W and walks the columns in 64-column
+// chunks through a ring of `stages` shared-memory stages, with the work split
+// by warp role:
+//   - 16 decode warps (8 row groups x 2 chains, one tANS chain per lane):
+//     per chunk each decodes one 8-pair tile of its streams straight into the
+//     stage's bf16 A tile (K-major, 128-byte swizzle), then arrives on the
+//     stage's a_full barrier.  A warp waits only for the stage to be empty
+//     (the MMAs that last read it have completed), so warps drift up to
+//     `stages` chunks apart instead of meeting at a block barrier per chunk;
+//   - one MMA warp, whose lane 0 loads the x chunk with a tensor-map copy
+//     (cp.async.bulk.tensor, 128-byte swizzle, rows past M zero-filled) into
+//     the stage's B tile, waits for a_full and x_full, issues four
+//     tcgen05.mma (M = 128, N = tokens, K = 16, bf16 in, fp32 accumulate in
+//     tensor memory) and commits them to the stage's `empty` barrier.
+// After the last chunk warps 0-3 read the accumulator rows back
+// (tcgen05.ld), scale, round once to bf16 and store.  Every mbarrier wait is
+// bounded and gives up early once another warp has given up; a wait that
+// runs out ORs TANS_B200_DATA_TIMEOUT into the status word, the CTA
+// waits (bounded) for its own tensor copies still in flight, skips its
+// epilogue and frees its tensor memory.
 
-constexpr int kTcWarps = 16;
+constexpr int kTcWarps = 16;                     // decode warps
+constexpr int kTcThreads = (kTcWarps + 1) * 32;  // + the MMA warp
 constexpr int kTcMaxTokens = 256;
+constexpr int kTcMaxStages = 4;
 constexpr int kTcATile = 128 * 128;   // 128 rows x 64 bf16
 constexpr uint32_t kTcWaitLimit = 1u << 22;
-constexpr int32_t kTcTimeoutBit = 8;
 
 struct TcArgs {
+    CUtensorMap xmap;         // x [M][C] bf16: box 64 columns x nt rows, 128-byte swizzle
     const uint32_t *comp;
     int64_t comp_bytes;
     const int32_t *offsets;
@@ -1283,10 +1294,10 @@ struct TcArgs {
     const uint8_t *sm;        // [N/16][K][8]
     const int32_t *table;
     const float *scale;       // [R]
-    const uint16_t *x;        // bf16 [M][C]
     uint16_t *y;              // bf16 [M][R]
     int64_t R, C, KS, M;
     int32_t nt;               // tokens per CTA (multiple of 16, <= 256)
+    int32_t stages;           // shared-memory stages (2..kTcMaxStages)
     int32_t *status;
     Opq q;
 };
@@ -1304,7 +1315,9 @@ __device__ __forceinline__ uint32_t tc_swz(uint32_t row, uint32_t k) {
     return (row >> 3) * 1024u + (row & 7u) * 128u + ((((k >> 3) ^ row) & 7u) << 4) + (k & 7u) * 2u;
 }
 
-__device__ __forceinline__ bool tc_wait(uint32_t mbar, uint32_t parity) {
+// Wait for the phase of `mbar` with the given parity to complete; false when
+// the wait runs out or (checked every 256 polls) *failed became non-zero.
+__device__ __forceinline__ bool tc_wait(uint32_t mbar, uint32_t parity, const volatile int32_t *failed) {
     for (uint32_t i = 0; i < kTcWaitLimit; i++) {
         uint32_t done;
         asm volatile(
@@ -1314,40 +1327,58 @@ __device__ __forceinline__ bool tc_wait(uint32_t mbar, uint32_t parity) {
             : "r"(mbar), "r"(parity)
             : "memory");
         if (done) return true;
+        if ((i & 255u) == 255u && failed && *failed) return false;
     }
     return false;
 }
 
+__device__ __forceinline__ void tc_arrive(uint32_t mbar) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(mbar)
+                 : "memory");
+}
+
+// x chunk c (columns 64c..64c+63 of tokens m0..m0+nt-1) -> B tile at `dst`,
+// completing `bytes` on mbarrier `bar`.
+__device__ __forceinline__ void tc_load_x(const CUtensorMap *map, uint32_t dst, uint32_t bar,
+                                          int32_t c, int32_t m0, uint32_t bytes) {
+    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
+                     bar),
+                 "r"(bytes)
+                 : "memory");
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
+        "{%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c * 64), "r"(m0), "r"(bar)
+        : "memory");
+}
+
 template <int R>
-__global__ void __launch_bounds__(kTcWarps * 32, 1) gemm_tc_kernel(const TcArgs p) {
+__global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ TcArgs p) {
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ __align__(8) uint64_t mbar[2];
+    __shared__ __align__(8) uint64_t a_full[kTcMaxStages], x_full[kTcMaxStages], empty[kTcMaxStages];
     __shared__ uint32_t tmem_base_s;
     __shared__ int32_t failed_s;
+    volatile int32_t *failed = &failed_s;
     load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 2, t4 = lane & 3;
-    const uint32_t lane_off = 4u * (lane % kCopies);
-    const uint32_t mask = (uint32_t)(R - 1) << 7;
-    Ring rg;
-    rg.lane_base = ring_area<R>(smem, warp, 1) + 4u * lane;
-    // A and B stages after the rings, 1024-byte aligned
+    const int S = p.stages;
     const uint32_t base_sa = smem_addr(smem);
-    const uint32_t a_sa = (ring_area<R>(smem, kTcWarps, 1) + 1023u) & ~1023u;
-    const uint32_t b_sa = a_sa + 2u * kTcATile;
+    const uint32_t a_sa = (ring_area<R>(smem, kTcWarps, 1) + 1023u) & ~1023u;  // A stages
     const uint32_t b_bytes = (uint32_t)p.nt * 128u;
-    uint8_t *a_ptr = smem + (a_sa - base_sa);
-    uint8_t *b_ptr = smem + (b_sa - base_sa);
-    const uint32_t mb0 = smem_addr(&mbar[0]), mb1 = smem_addr(&mbar[1]);
+    const uint32_t b_sa = a_sa + (uint32_t)S * kTcATile;                      // B stages
+    const uint32_t af0 = smem_addr(&a_full[0]), xf0 = smem_addr(&x_full[0]), em0 = smem_addr(&empty[0]);
     const uint32_t ncols = p.nt <= 32 ? 32u : (p.nt <= 64 ? 64u : (p.nt <= 128 ? 128u : 256u));
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_addr(&tmem_base_s)), "r"(ncols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    if (threadIdx.x == 0) {
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mb0));
-        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(mb1));
+    if (threadIdx.x == 32 * kTcWarps) {
+        for (int s = 0; s < S; s++) {
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(af0 + 8u * s), "r"(kTcWarps));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(xf0 + 8u * s));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(em0 + 8u * s));
+        }
         asm volatile("fence.mbarrier_init.release.cluster;");
         failed_s = 0;
     }
@@ -1355,112 +1386,142 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) gemm_tc_kernel(const TcArgs 
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;");
     const uint32_t tmem = tmem_base_s;
-    const uint8_t *tb = smem;
-
     const int64_t CS = p.C / p.KS, K = p.R * 4 * p.KS;
     const int32_t tps = (int32_t)(CS / 64), nchunks = (int32_t)(p.C / 64);
-    const int rgrp = warp >> 1, chain = warp & 1;
-    const int64_t wg = (int64_t)blockIdx.x * 8 + rgrp;          // global 16-row group
-    const uint32_t row = (uint32_t)(16 * rgrp + g + 8 * chain);  // row within the tile
-    const int64_t m0 = (int64_t)blockIdx.y * p.nt;
-    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.nt >> 3) << 17) |
-                           ((uint32_t)(128 >> 4) << 24);
-    Chain ch;
-    chain_idle(ch, p.comp);
-    bool live = false;
-    const uint8_t *sp = p.sm;
-    uint2 m_n = make_uint2(0, 0);
-    bool ok = true;
-    for (int32_t c = 0; c < nchunks; c++) {
-        const int32_t kslice = c / tps, tt = c % tps;
-        if (tt == 0) {  // this slice's streams
-            const int64_t sid = ((wg * p.KS + kslice) * 2 + chain) * 32 + lane;
-            const int32_t G = chain_init(ch, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
-                                         sid, lane_off, p.status);
-            live = G > 0;
-            if (!live) chain_idle(ch, p.comp);
-            cp_async_wait<0>();
-            ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, live ? G : 0), live);
-            cp_async_commit();
-            cp_async_wait<0>();
-            sp = p.sm + sid * 8;
-            m_n = live ? ld_stream_v2(sp) : make_uint2(0, 0);
-        }
-        const int s = c & 1;
-        if (c >= 2 && ok && !tc_wait(s ? mb1 : mb0, (uint32_t)(((c >> 1) - 1) & 1))) ok = false;
-        // x chunk -> B stage s (rows past M are zero), in flight during the decode
-        const uint32_t bs = b_sa + (uint32_t)s * (uint32_t)kTcMaxTokens * 128u;
-        for (int pc = threadIdx.x; pc < p.nt * 8; pc += blockDim.x) {
-            const int n = pc >> 3, q8 = pc & 7;
-            const int64_t mrow = m0 + n;
-            const uint16_t *src = p.x + (mrow < p.M ? mrow : 0) * p.C + (int64_t)c * 64 + q8 * 8;
-            const uint32_t dst = bs + (uint32_t)(n >> 3) * 1024u + (uint32_t)(n & 7) * 128u +
-                                 ((uint32_t)((q8 ^ n) & 7) << 4);
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
-                         "r"(mrow < p.M ? 16 : 0)
-                         : "memory");
-        }
-        cp_async_commit();
-        // decode this warp's tile of chunk c into A stage s
-        const uint2 m = m_n;
-        sp += K * 8;
-        if (live && tt + 1 < tps) m_n = ld_stream_v2(sp);
-        const int32_t need = ring_fill<R>(rg, ch, live);
-        cp_async_commit();
-        // groups: ..., ring(c-1), x(c), ring(c): the decode needs only ring(c-1);
-        // the x chunk keeps loading under the decode
-        cp_async_wait<2>();
-        uint32_t e[kTablePairs];
-        if (need >= rg.done[kDecodeLag]) {
+    const int32_t m0 = (int32_t)blockIdx.y * p.nt;
+
+    if (warp == kTcWarps) {
+        // ------------------------------------------------ MMA warp (lane 0)
+        if (lane == 0) {
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.nt >> 3) << 17) |
+                                   ((uint32_t)(128 >> 4) << 24);
+            bool ok = true;
+            int32_t loaded = 0, consumed = 0, issued = 0;  // x chunks issued / waited for; MMA chunks
+            for (; loaded < (nchunks < S ? nchunks : S); loaded++)
+                tc_load_x(&p.xmap, b_sa + (uint32_t)loaded * b_bytes, xf0 + 8u * loaded, loaded, m0,
+                          b_bytes);
+            for (int32_t c = 0; c < nchunks && ok; c++) {
+                const int s = c % S;
+                const uint32_t ph = (uint32_t)((c / S) & 1);
+                if (!tc_wait(af0 + 8u * s, ph, failed) || !tc_wait(xf0 + 8u * s, ph, failed)) {
+                    ok = false;
+                    break;
+                }
+                consumed = c + 1;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t as = a_sa + (uint32_t)s * kTcATile, bs = b_sa + (uint32_t)s * b_bytes;
 #pragma unroll
-            for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
-        } else {
-#pragma unroll
-            for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_global(ch, tb, p.q);
-        }
-        uint32_t wd[4];
-        compose_pairs(gather_syms(e[0], e[1], e[2], e[3]), m.x, p.q, wd[0], wd[1]);
-        compose_pairs(gather_syms(e[4], e[5], e[6], e[7]), m.y, p.q, wd[2], wd[3]);
-        uint8_t *at = a_ptr + s * kTcATile;
-#pragma unroll
-        for (int j = 0; j < 4; j++) {  // 16-column sub-chunk j: columns 2t, 2t+1 | 8+2t, 9+2t
-            const uint32_t lo = live ? cvt_bf16x2_e4m3x2(wd[j] & 0xFFFFu) : 0u;
-            const uint32_t hi = live ? cvt_bf16x2_e4m3x2(wd[j] >> 16) : 0u;
-            *reinterpret_cast<uint32_t *>(at + tc_swz(row, 16 * j + 2 * t4)) = lo;
-            *reinterpret_cast<uint32_t *>(at + tc_swz(row, 16 * j + 8 + 2 * t4)) = hi;
-        }
-        cp_async_wait<1>();  // the x chunk (everything but this tile's ring fills)
-        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (threadIdx.x == 0 && ok) {
-            asm volatile("tcgen05.fence::after_thread_sync;");
-            const uint32_t as = a_sa + (uint32_t)s * kTcATile;
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                const uint64_t ad = tc_smem_desc(as + 32u * j), bd = tc_smem_desc(bs + 32u * j);
+                for (int j = 0; j < 4; j++) {
+                    const uint64_t ad = tc_smem_desc(as + 32u * j), bd = tc_smem_desc(bs + 32u * j);
+                    asm volatile(
+                        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
+                            tmem),
+                        "l"(ad), "l"(bd), "r"(idesc), "r"((uint32_t)(c > 0 || j > 0)), "r"(0u), "r"(0u),
+                        "r"(0u), "r"(0u));
+                }
                 asm volatile(
-                    "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                    "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
-                        tmem),
-                    "l"(ad), "l"(bd), "r"(idesc), "r"((uint32_t)(c > 0 || j > 0)), "r"(0u), "r"(0u),
-                    "r"(0u), "r"(0u));
+                    "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                        em0 + 8u * s)
+                    : "memory");
+                issued = c + 1;
+                // refill the stage of chunk c-1 (its MMAs were issued one chunk ago)
+                if (c >= 1 && loaded < nchunks) {
+                    const int s1 = (c - 1) % S;
+                    if (!tc_wait(em0 + 8u * s1, (uint32_t)(((c - 1) / S) & 1), failed)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_load_x(&p.xmap, b_sa + (uint32_t)s1 * b_bytes, xf0 + 8u * s1, loaded, m0, b_bytes);
+                    loaded++;
+                }
             }
-            asm volatile(
-                "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                    s ? mb1 : mb0)
-                : "memory");
+            // the MMAs complete in order: the last commit covers them all
+            if (ok && nchunks > 0) {
+                const int32_t cl = nchunks - 1;
+                if (!tc_wait(em0 + 8u * (cl % S), (uint32_t)((cl / S) & 1), failed)) ok = false;
+            }
+            if (!ok) {
+                *failed = 1;
+                // copies and MMAs still in flight finish before the CTA frees
+                // its tensor memory and exits
+                for (int32_t c = consumed; c < loaded; c++)
+                    tc_wait(xf0 + 8u * (c % S), (uint32_t)((c / S) & 1), nullptr);
+                if (issued > 0)
+                    tc_wait(em0 + 8u * ((issued - 1) % S), (uint32_t)(((issued - 1) / S) & 1), nullptr);
+            }
         }
+        __syncwarp();
+    } else {
+        // ----------------------------------------------------- decode warps
+        const uint8_t *tb = smem;
+        const uint32_t lane_off = 4u * (lane % kCopies);
+        const uint32_t mask = (uint32_t)(R - 1) << 7;
+        Ring rg;
+        rg.lane_base = ring_area<R>(smem, warp, 1) + 4u * lane;
+        uint8_t *a_ptr = smem + (a_sa - base_sa);
+        const int g = lane >> 2, t4 = lane & 3;
+        const int rgrp = warp >> 1, chain = warp & 1;
+        const int64_t wg = (int64_t)blockIdx.x * 8 + rgrp;          // global 16-row group
+        const uint32_t row = (uint32_t)(16 * rgrp + g + 8 * chain);  // row within the tile
+        Chain ch;
+        chain_idle(ch, p.comp);
+        bool live = false, ok = true;
+        const uint8_t *sp = p.sm;
+        uint2 m_n = make_uint2(0, 0);
+        for (int32_t c = 0; c < nchunks; c++) {
+            const int32_t kslice = c / tps, tt = c % tps;
+            if (tt == 0) {  // this slice's streams
+                const int64_t sid = ((wg * p.KS + kslice) * 2 + chain) * 32 + lane;
+                const int32_t G = chain_init(ch, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
+                                             sid, lane_off, p.status);
+                live = G > 0;
+                if (!live) chain_idle(ch, p.comp);
+                cp_async_wait<0>();
+                ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, live ? G : 0), live);
+                cp_async_commit();
+                cp_async_wait<0>();
+                sp = p.sm + sid * 8;
+                m_n = live ? ld_stream_v2(sp) : make_uint2(0, 0);
+            }
+            const int s = c % S;
+            const uint2 m = m_n;
+            sp += K * 8;
+            if (live && tt + 1 < tps) m_n = ld_stream_v2(sp);
+            const int32_t need = ring_fill<R>(rg, ch, live);
+            cp_async_commit();
+            cp_async_wait<1>();  // ring(c-1); ring(c) keeps loading under the decode
+            uint32_t e[kTablePairs];
+            if (need >= rg.done[kDecodeLag]) {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
+            } else {
+#pragma unroll
+                for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_global(ch, tb, p.q);
+            }
+            uint32_t wd[4];
+            compose_pairs(gather_syms(e[0], e[1], e[2], e[3]), m.x, p.q, wd[0], wd[1]);
+            compose_pairs(gather_syms(e[4], e[5], e[6], e[7]), m.y, p.q, wd[2], wd[3]);
+            // the stage is free once the MMAs of chunk c - S have completed
+            if (c >= S && ok && !tc_wait(em0 + 8u * s, (uint32_t)(((c / S) - 1) & 1), failed)) ok = false;
+            uint8_t *at = a_ptr + s * kTcATile;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {  // 16-column sub-chunk j: columns 2t, 2t+1 | 8+2t, 9+2t
+                const uint32_t lo = live ? cvt_bf16x2_e4m3x2(wd[j] & 0xFFFFu) : 0u;
+                const uint32_t hi = live ? cvt_bf16x2_e4m3x2(wd[j] >> 16) : 0u;
+                *reinterpret_cast<uint32_t *>(at + tc_swz(row, 16 * j + 2 * t4)) = lo;
+                *reinterpret_cast<uint32_t *>(at + tc_swz(row, 16 * j + 8 + 2 * t4)) = hi;
+            }
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncwarp();
+            if (lane == 0) tc_arrive(af0 + 8u * s);
+        }
+        cp_async_wait<0>();
+        if (!ok) *failed = 1;
     }
-    cp_async_wait<0>();
-    // all MMAs done (they complete in order): wait for the last commit
-    if (nchunks > 0 && ok) {
-        const int32_t cl = nchunks - 1;
-        if (!tc_wait((cl & 1) ? mb1 : mb0, (uint32_t)((cl >> 1) & 1))) ok = false;
-    }
-    if (!ok) atomicOr(&failed_s, 1);
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;");
-    const bool good = failed_s == 0;
+    const bool good = *failed == 0;
     if (warp < 4 && good) {
         const int64_t r = (int64_t)blockIdx.x * 128 + 32 * warp + lane;
         const float sc = p.scale[r];
@@ -1474,13 +1535,13 @@ __global__ void __launch_bounds__(kTcWarps * 32, 1) gemm_tc_kernel(const TcArgs 
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
             for (int i = 0; i < 8; i++) {
-                const int64_t mm = m0 + col + i;
+                const int64_t mm = (int64_t)m0 + col + i;
                 if (mm < p.M)
                     p.y[mm * p.R + r] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]) * sc));
             }
         }
     }
-    if (!good && threadIdx.x == 0 && p.status) atomicOr(p.status, kTcTimeoutBit);
+    if (!good && threadIdx.x == 0 && p.status) atomicOr(p.status, TANS_B200_DATA_TIMEOUT);
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
     if (warp == 0) {
@@ -1986,6 +2047,30 @@ extern "C" int tans_b200_scale_rows_bf16(const float *acc, const float *scale, u
     return launch_status("scale_rows_bf16_kernel");
 }
 
+// cuTensorMapEncodeTiled, resolved through the runtime so that the library
+// needs no link against the driver library.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_tiled_fn(EncodeTiledFn *fn) {
+    static EncodeTiledFn cached = nullptr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!cached) {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000,
+                                                         cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !f)
+            return fail(TANS_B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable: %s",
+                        cudaGetErrorString(e));
+        cached = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    *fn = cached;
+    return TANS_B200_OK;
+}
+
 extern "C" int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_bytes,
                                  const int32_t *offsets, const uint16_t *states,
                                  const uint8_t *partial, const uint8_t *sm,
@@ -1997,7 +2082,8 @@ extern "C" int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_b
         return fail(TANS_B200_ERR_INVALID, "gemm_tc: rows must be a positive multiple of 128");
     if (col_splits < 1 || cols <= 0 || cols % (64 * col_splits) != 0)
         return fail(TANS_B200_ERR_INVALID, "gemv: cols must be a positive multiple of 64 * col_splits");
-    if (m < 1) return fail(TANS_B200_ERR_INVALID, "gemm_tc: m must be >= 1");
+    if (m < 1 || m > INT32_MAX - kTcMaxTokens)
+        return fail(TANS_B200_ERR_INVALID, "gemm_tc: m must be in [1, 2^31 - 257]");
     if (!compressed || !offsets || !states || !partial || !sm || !decode_table || !scale || !x || !y)
         return fail(TANS_B200_ERR_INVALID, "gemm_tc: null pointer");
     if (!aligned(compressed, 4) || !aligned(offsets, 4) || !aligned(states, 2) || !aligned(sm, 8) ||
@@ -2013,15 +2099,47 @@ extern "C" int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_b
     if (nt > kTcMaxTokens) nt = kTcMaxTokens;
     const int64_t ty = (m + nt - 1) / nt;
     constexpr int rr = 16;  // ring rows: slices are at most a few hundred pair symbols long
-    const int smem = kTableBytes + rr * 128 + kTcWarps * rr * 128 + 1024 + 2 * kTcATile +
-                     2 * kTcMaxTokens * 128;
-    if (smem > kSmemMax) return fail(TANS_B200_ERR_INVALID, "gemm_tc: shared memory");
-    TcArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets, states,
-                partial, sm, decode_table, scale, x, y, rows, cols, col_splits, m, nt, status,
-                make_opq()};
+    const int fixed = kTableBytes + rr * 128 + kTcWarps * rr * 128 + 1024;
+    const int per_stage = kTcATile + nt * 128;
+    int stages = (kSmemMax - 1024 - fixed) / per_stage;  // 1 KiB left for static shared memory
+    if (stages > kTcMaxStages) stages = kTcMaxStages;
+    if (stages < 2) return fail(TANS_B200_ERR_INVALID, "gemm_tc: shared memory");
+    const int smem = fixed + stages * per_stage;
+    EncodeTiledFn encode;
+    rc = encode_tiled_fn(&encode);
+    if (rc) return rc;
+    TcArgs args{};
+    // x [m][cols] bf16: dimension 0 = columns (contiguous), dimension 1 = tokens;
+    // one box = 64 columns (128 bytes, the swizzle span) x nt tokens; tokens
+    // past m read as zeros
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)m};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)nt};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult cr = encode(&args.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS) return fail(TANS_B200_ERR_CUDA, "gemm_tc: tensor map encode failed (%d)", (int)cr);
+    args.comp = reinterpret_cast<const uint32_t *>(compressed);
+    args.comp_bytes = compressed_bytes;
+    args.offsets = offsets;
+    args.states = states;
+    args.partial = partial;
+    args.sm = sm;
+    args.table = decode_table;
+    args.scale = scale;
+    args.y = y;
+    args.R = rows;
+    args.C = cols;
+    args.KS = col_splits;
+    args.M = m;
+    args.nt = nt;
+    args.stages = stages;
+    args.status = status;
+    args.q = make_opq();
     rc = set_smem(gemm_tc_kernel<rr>, smem);
     if (rc) return rc;
-    gemm_tc_kernel<rr><<<dim3((unsigned)(rows / 128), (unsigned)ty), kTcWarps * 32, smem,
+    gemm_tc_kernel<rr><<<dim3((unsigned)(rows / 128), (unsigned)ty), kTcThreads, smem,
                          (cudaStream_t)stream>>>(args);
     return launch_status("gemm_tc_kernel");
 }
