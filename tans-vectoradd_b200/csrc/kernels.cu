@@ -406,6 +406,12 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, bool pr
         "l"(src), "r"((uint32_t)pred)
         : "memory");
 }
+// 8-byte copy; zero-fills the destination when !pred.
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void *src, bool pred) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src),
+                 "r"(pred ? 8u : 0u)
+                 : "memory");
+}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -427,14 +433,16 @@ constexpr int kGemvLag = 2;     // and by the GEMV kernel
 constexpr int kRingBurst = 12;  // rows filled when a group starts
 constexpr int kRingPerTile = 2; // rows filled per tile after that
 
-struct Ring {
-    uint32_t lane_base;          // shared address of this lane's column, row slot 0
-    int32_t fill;                // next row to fill (warp-uniform)
-    int32_t done[kRingLag + 1];  // lowest filled row after the last fills
+template <int kDepth>
+struct RingT {
+    uint32_t lane_base;        // shared address of this lane's column, row slot 0
+    int32_t fill;              // next row to fill (warp-uniform)
+    int32_t done[kDepth + 1];  // lowest filled row after the last kDepth + 1 fills
 };
+using Ring = RingT<kRingLag>;
 
-template <int R>
-__device__ __forceinline__ void ring_start(Ring &rg, const Chain &ch, int32_t G, bool live) {
+template <int R, int D>
+__device__ __forceinline__ void ring_start(RingT<D> &rg, const Chain &ch, int32_t G, bool live) {
     rg.fill = G - 3;
 #pragma unroll
     for (int k = 0; k < kRingBurst; k++) {
@@ -445,13 +453,13 @@ __device__ __forceinline__ void ring_start(Ring &rg, const Chain &ch, int32_t G,
     // the caller commits and waits for this burst (cp.async.wait_group 0)
     // before the first tile, so every tile can refill from the ring
 #pragma unroll
-    for (int i = 0; i <= kRingLag; i++) rg.done[i] = rg.fill + 1;
+    for (int i = 0; i <= D; i++) rg.done[i] = rg.fill + 1;
 }
 
 // This tile's fills; returns the lowest row a lane may refill from during
 // the tile (the fast path needs it at or above done[kRingLag]).
-template <int R>
-__device__ __forceinline__ int32_t ring_fill(Ring &rg, const Chain &ch, bool live) {
+template <int R, int D>
+__device__ __forceinline__ int32_t ring_fill(RingT<D> &rg, const Chain &ch, bool live) {
     const int32_t row = ch.v >> 7;
     const int32_t r_fast = __reduce_min_sync(0xffffffffu, live ? row : INT_MAX);
     // lanes without a stream report a far-negative row (no overflow in r_slow - R)
@@ -465,7 +473,7 @@ __device__ __forceinline__ int32_t ring_fill(Ring &rg, const Chain &ch, bool liv
         rg.fill -= go ? 1 : 0;
     }
 #pragma unroll
-    for (int i = kRingLag; i > 0; i--) rg.done[i] = rg.done[i - 1];
+    for (int i = D; i > 0; i--) rg.done[i] = rg.done[i - 1];
     rg.done[0] = rg.fill + 1;
     return r_fast == INT_MAX ? INT_MAX : max(r_fast - 2, 0);
 }
@@ -1282,7 +1290,13 @@ constexpr int kTcThreads = (kTcWarps + 1) * 32;  // + the MMA warp
 constexpr int kTcMaxTokens = 256;
 constexpr int kTcMaxStages = 4;
 constexpr int kTcATile = 128 * 128;   // 128 rows x 64 bf16
-constexpr uint32_t kTcWaitLimit = 1u << 22;
+constexpr uint32_t kTcWaitLimit = 1u << 16;  // polls per wait
+constexpr uint32_t kTcPollNs = 10000;        // suspend-time hint per poll (ns): bound ~0.66 s
+constexpr int kTcLag = 3;    // cp.async groups (ring rows + sign/mantissa) in flight under the decode
+constexpr int kTcSmAhead = 3;  // chunks whose sign/mantissa words are requested ahead
+constexpr int kTcSmSlots = 4;  // their per-warp queue slots (32 lanes x 8 bytes each)
+static_assert(kTcSmAhead >= kTcLag && kTcSmSlots > kTcSmAhead, "sign/mantissa queue too short");
+static_assert((kTcSmSlots & (kTcSmSlots - 1)) == 0, "queue slots: a power of two");
 
 struct TcArgs {
     CUtensorMap xmap;         // x [M][C] bf16: box 64 columns x nt rows, 128-byte swizzle
@@ -1316,18 +1330,21 @@ __device__ __forceinline__ uint32_t tc_swz(uint32_t row, uint32_t k) {
 }
 
 // Wait for the phase of `mbar` with the given parity to complete; false when
-// the wait runs out or (checked every 256 polls) *failed became non-zero.
+// the wait runs out or (checked every 16 polls) *failed became non-zero.
+// Each poll lets the hardware suspend the thread for up to kTcPollNs until
+// the phase completes, so waiting warps take no issue slots from the
+// decoding ones; the whole wait is bounded by kTcWaitLimit polls.
 __device__ __forceinline__ bool tc_wait(uint32_t mbar, uint32_t parity, const volatile int32_t *failed) {
     for (uint32_t i = 0; i < kTcWaitLimit; i++) {
         uint32_t done;
         asm volatile(
-            "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+            "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2, %3;\n\t"
             "selp.b32 %0, 1, 0, P1;\n\t}"
             : "=r"(done)
-            : "r"(mbar), "r"(parity)
+            : "r"(mbar), "r"(parity), "n"(kTcPollNs)
             : "memory");
         if (done) return true;
-        if ((i & 255u) == 255u && failed && *failed) return false;
+        if ((i & 15u) == 15u && failed && *failed) return false;
     }
     return false;
 }
@@ -1363,7 +1380,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int S = p.stages;
     const uint32_t base_sa = smem_addr(smem);
-    const uint32_t a_sa = (ring_area<R>(smem, kTcWarps, 1) + 1023u) & ~1023u;  // A stages
+    const uint32_t smq_sa = ring_area<R>(smem, kTcWarps, 1);                   // sign/mantissa queues
+    const uint32_t a_sa = (smq_sa + kTcWarps * kTcSmSlots * 256u + 1023u) & ~1023u;  // A stages
     const uint32_t b_bytes = (uint32_t)p.nt * 128u;
     const uint32_t b_sa = a_sa + (uint32_t)S * kTcATile;                      // B stages
     const uint32_t af0 = smem_addr(&a_full[0]), xf0 = smem_addr(&x_full[0]), em0 = smem_addr(&empty[0]);
@@ -1400,9 +1418,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             for (; loaded < (nchunks < S ? nchunks : S); loaded++)
                 tc_load_x(&p.xmap, b_sa + (uint32_t)loaded * b_bytes, xf0 + 8u * loaded, loaded, m0,
                           b_bytes);
+            int s = 0, ps = 0;          // stage of chunk c and of chunk c - 1
+            uint32_t ph = 0, pph = 0;   // their phase parities
             for (int32_t c = 0; c < nchunks && ok; c++) {
-                const int s = c % S;
-                const uint32_t ph = (uint32_t)((c / S) & 1);
                 if (!tc_wait(af0 + 8u * s, ph, failed) || !tc_wait(xf0 + 8u * s, ph, failed)) {
                     ok = false;
                     break;
@@ -1427,13 +1445,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 issued = c + 1;
                 // refill the stage of chunk c-1 (its MMAs were issued one chunk ago)
                 if (c >= 1 && loaded < nchunks) {
-                    const int s1 = (c - 1) % S;
-                    if (!tc_wait(em0 + 8u * s1, (uint32_t)(((c - 1) / S) & 1), failed)) {
+                    if (!tc_wait(em0 + 8u * ps, pph, failed)) {
                         ok = false;
                         break;
                     }
-                    tc_load_x(&p.xmap, b_sa + (uint32_t)s1 * b_bytes, xf0 + 8u * s1, loaded, m0, b_bytes);
+                    tc_load_x(&p.xmap, b_sa + (uint32_t)ps * b_bytes, xf0 + 8u * ps, loaded, m0, b_bytes);
                     loaded++;
+                }
+                ps = s;
+                pph = ph;
+                if (++s == S) {
+                    s = 0;
+                    ph ^= 1u;
                 }
             }
             // the MMAs complete in order: the last commit covers them all
@@ -1457,21 +1480,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
         const uint8_t *tb = smem;
         const uint32_t lane_off = 4u * (lane % kCopies);
         const uint32_t mask = (uint32_t)(R - 1) << 7;
-        Ring rg;
+        RingT<kTcLag> rg;
         rg.lane_base = ring_area<R>(smem, warp, 1) + 4u * lane;
         uint8_t *a_ptr = smem + (a_sa - base_sa);
         const int g = lane >> 2, t4 = lane & 3;
         const int rgrp = warp >> 1, chain = warp & 1;
         const int64_t wg = (int64_t)blockIdx.x * 8 + rgrp;          // global 16-row group
         const uint32_t row = (uint32_t)(16 * rgrp + g + 8 * chain);  // row within the tile
+        // this lane's sign/mantissa queue: chunk c's 8 bytes in slot c % kTcSmSlots
+        const uint32_t smq = smq_sa + (uint32_t)warp * (kTcSmSlots * 256u) + 8u * lane;
         Chain ch;
         chain_idle(ch, p.comp);
         bool live = false, ok = true;
         const uint8_t *sp = p.sm;
-        uint2 m_n = make_uint2(0, 0);
+        int32_t kslice = 0, tt = 0;  // slice of chunk c and chunk within it
+        int s = 0;                   // stage of chunk c
+        uint32_t ph = 0;             // (c / S) & 1
         for (int32_t c = 0; c < nchunks; c++) {
-            const int32_t kslice = c / tps, tt = c % tps;
-            if (tt == 0) {  // this slice's streams
+            if (tt == 0) {  // this slice's streams, its first rows and sign/mantissa words
                 const int64_t sid = ((wg * p.KS + kslice) * 2 + chain) * 32 + lane;
                 const int32_t G = chain_init(ch, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
                                              sid, lane_off, p.status);
@@ -1479,20 +1505,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 if (!live) chain_idle(ch, p.comp);
                 cp_async_wait<0>();
                 ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, live ? G : 0), live);
+                sp = p.sm + sid * 8;
+#pragma unroll
+                for (int d = 0; d < kTcSmAhead; d++)
+                    cp_async8(smq + ((uint32_t)(c + d) & (kTcSmSlots - 1)) * 256u, sp + (int64_t)d * K * 8,
+                              live && d < tps);
                 cp_async_commit();
                 cp_async_wait<0>();
-                sp = p.sm + sid * 8;
-                m_n = live ? ld_stream_v2(sp) : make_uint2(0, 0);
             }
-            const int s = c % S;
-            const uint2 m = m_n;
-            sp += K * 8;
-            if (live && tt + 1 < tps) m_n = ld_stream_v2(sp);
+            // one group per chunk: ring rows and the sign/mantissa words of
+            // chunk c + kTcSmAhead.  A chunk is short next to a DRAM round
+            // trip, so the decode reads groups kTcLag chunks old
             const int32_t need = ring_fill<R>(rg, ch, live);
+            cp_async8(smq + ((uint32_t)(c + kTcSmAhead) & (kTcSmSlots - 1)) * 256u,
+                      sp + (int64_t)(tt + kTcSmAhead) * K * 8, live && tt + kTcSmAhead < tps);
             cp_async_commit();
-            cp_async_wait<1>();  // ring(c-1); ring(c) keeps loading under the decode
+            cp_async_wait<kTcLag>();
+            uint2 m;
+            asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
+                         : "=r"(m.x), "=r"(m.y)
+                         : "r"(smq + ((uint32_t)c & (kTcSmSlots - 1)) * 256u));
             uint32_t e[kTablePairs];
-            if (need >= rg.done[kDecodeLag]) {
+            if (need >= rg.done[kTcLag]) {
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
             } else {
@@ -1503,7 +1537,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             compose_pairs(gather_syms(e[0], e[1], e[2], e[3]), m.x, p.q, wd[0], wd[1]);
             compose_pairs(gather_syms(e[4], e[5], e[6], e[7]), m.y, p.q, wd[2], wd[3]);
             // the stage is free once the MMAs of chunk c - S have completed
-            if (c >= S && ok && !tc_wait(em0 + 8u * s, (uint32_t)(((c / S) - 1) & 1), failed)) ok = false;
+            if (c >= S && ok && !tc_wait(em0 + 8u * s, ph ^ 1u, failed)) ok = false;
             uint8_t *at = a_ptr + s * kTcATile;
 #pragma unroll
             for (int j = 0; j < 4; j++) {  // 16-column sub-chunk j: columns 2t, 2t+1 | 8+2t, 9+2t
@@ -1515,6 +1549,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) tc_arrive(af0 + 8u * s);
+            if (++tt == tps) {
+                tt = 0;
+                kslice++;
+            }
+            if (++s == S) {
+                s = 0;
+                ph ^= 1u;
+            }
         }
         cp_async_wait<0>();
         if (!ok) *failed = 1;
@@ -2098,9 +2140,10 @@ extern "C" int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_b
     int nt = (int)((m + 15) / 16 * 16);
     if (nt > kTcMaxTokens) nt = kTcMaxTokens;
     const int64_t ty = (m + nt - 1) / nt;
-    constexpr int rr = 16;  // ring rows: slices are at most a few hundred pair symbols long
-    const int fixed = kTableBytes + rr * 128 + kTcWarps * rr * 128 + 1024;
+    // ring rows: 32 where two stages still fit beside them, else 16
     const int per_stage = kTcATile + nt * 128;
+    const int rr = nt <= 128 ? 32 : 16;
+    const int fixed = kTableBytes + rr * 128 + kTcWarps * rr * 128 + kTcWarps * kTcSmSlots * 256 + 1024;
     int stages = (kSmemMax - 1024 - fixed) / per_stage;  // 1 KiB left for static shared memory
     if (stages > kTcMaxStages) stages = kTcMaxStages;
     if (stages < 2) return fail(TANS_B200_ERR_INVALID, "gemm_tc: shared memory");
@@ -2137,10 +2180,16 @@ extern "C" int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_b
     args.stages = stages;
     args.status = status;
     args.q = make_opq();
-    rc = set_smem(gemm_tc_kernel<rr>, smem);
-    if (rc) return rc;
-    gemm_tc_kernel<rr><<<dim3((unsigned)(rows / 128), (unsigned)ty), kTcThreads, smem,
-                         (cudaStream_t)stream>>>(args);
+    const dim3 grid((unsigned)(rows / 128), (unsigned)ty);
+    if (rr == 32) {
+        rc = set_smem(gemm_tc_kernel<32>, smem);
+        if (rc) return rc;
+        gemm_tc_kernel<32><<<grid, kTcThreads, smem, (cudaStream_t)stream>>>(args);
+    } else {
+        rc = set_smem(gemm_tc_kernel<16>, smem);
+        if (rc) return rc;
+        gemm_tc_kernel<16><<<grid, kTcThreads, smem, (cudaStream_t)stream>>>(args);
+    }
     return launch_status("gemm_tc_kernel");
 }
 
