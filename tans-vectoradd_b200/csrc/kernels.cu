@@ -1007,11 +1007,12 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
     const int64_t pitch = CS + 8;  // halves
     uint16_t *xs = reinterpret_cast<uint16_t *>(smem + kTableBytes);
     // x slice -> f16 in shared memory (rows >= B are zero)
-    for (int64_t i = threadIdx.x; i < kGemvMaxBatch * CS; i += blockDim.x) {
-        const int64_t b = i / CS, c = i % CS;
-        float v = 0.f;
-        if (b < p.B) v = __uint_as_float((uint32_t)p.x[b * p.C + k * CS + c] << 16);
-        xs[b * pitch + c] = __half_as_ushort(__float2half_rn(v));
+    for (int b = 0; b < kGemvMaxBatch; b++) {
+        const uint16_t *xr = p.x + b * p.C + k * CS;
+        for (int32_t c = threadIdx.x; c < (int32_t)CS; c += blockDim.x) {
+            const float v = b < p.B ? __uint_as_float((uint32_t)xr[c] << 16) : 0.f;
+            xs[b * pitch + c] = __half_as_ushort(__float2half_rn(v));
+        }
     }
     __syncthreads();
     const uint8_t *tb = smem;
@@ -1030,9 +1031,10 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
     }
     const int64_t K = p.R * 4 * p.KS;  // streams
     const int64_t N = CS / 4;          // fp8 per stream
-    const int64_t n_tiles = N / 16;
+    const int32_t n_tiles = (int32_t)(N / 16);  // CS / 64
     const int64_t groups = p.R / 16;
     const uint32_t *xw = reinterpret_cast<const uint32_t *>(xs) + g * (pitch / 2) + t;
+    const int64_t tstep = K * 8, pf_ahead = 3 * tstep;  // sign/mantissa bytes per tile row
     for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; w < groups;
          w += (int64_t)gridDim.x * (blockDim.x >> 5)) {
         const int64_t sa_id = ((w * p.KS + k) * 2 + 0) * 32 + lane;
@@ -1053,19 +1055,24 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
         cp_async_wait<0>();
         float d[4] = {0.f, 0.f, 0.f, 0.f};
         uint2 sa_n = make_uint2(0, 0), sb_n = make_uint2(0, 0);
+        // running pointers: this tile's sign/mantissa words and x fragments
+        const uint8_t *spa = p.sm + sa_id * 8, *spb = p.sm + sb_id * 8;
+        const uint32_t *xp = xw;
         if (live && n_tiles > 0) {
-            sa_n = ld_stream_v2(p.sm + sa_id * 8);
-            sb_n = ld_stream_v2(p.sm + sb_id * 8);
+            sa_n = ld_stream_v2(spa);
+            sb_n = ld_stream_v2(spb);
         }
-        for (int64_t tt = 0; tt < n_tiles; tt++) {
+        for (int32_t tt = 0; tt < n_tiles; tt++) {
             const uint2 sa = sa_n, sb = sb_n;
+            spa += tstep;
+            spb += tstep;
             if (live && tt + 1 < n_tiles) {
-                sa_n = ld_stream_v2(p.sm + ((tt + 1) * K + sa_id) * 8);
-                sb_n = ld_stream_v2(p.sm + ((tt + 1) * K + sb_id) * 8);
+                sa_n = ld_stream_v2(spa);
+                sb_n = ld_stream_v2(spb);
             }
             if (live && tt + 4 < n_tiles) {
-                prefetch_l2(p.sm + ((tt + 4) * K + sa_id) * 8);
-                prefetch_l2(p.sm + ((tt + 4) * K + sb_id) * 8);
+                prefetch_l2(spa + pf_ahead);
+                prefetch_l2(spb + pf_ahead);
             }
             const int32_t need_a = ring_fill<R>(ra, ca, live);
             const int32_t need_b = ring_fill<R>(rb, cb, live);
@@ -1091,15 +1098,15 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
             compose_pairs(gather_syms(eb[0], eb[1], eb[2], eb[3]), sb.x, p.q, wb[0], wb[1]);
             compose_pairs(gather_syms(eb[4], eb[5], eb[6], eb[7]), sb.y, p.q, wb[2], wb[3]);
 #pragma unroll
-            for (int j = 0; j < 4; j++) {  // chunk = 16 columns
-                const int64_t col = (tt * 4 + j) * 16;
-                const uint32_t b0 = xw[col / 2], b1 = xw[col / 2 + 4];
+            for (int j = 0; j < 4; j++) {  // chunk = 16 columns: words 8j (k 0-7) and 8j + 4 (k 8-15)
+                const uint32_t b0 = xp[8 * j], b1 = xp[8 * j + 4];
                 const uint32_t a0 = cvt_f16x2_e4m3x2(wa[j] & 0xFFFFu);
                 const uint32_t a2 = cvt_f16x2_e4m3x2(wa[j] >> 16);
                 const uint32_t a1 = cvt_f16x2_e4m3x2(wb[j] & 0xFFFFu);
                 const uint32_t a3 = cvt_f16x2_e4m3x2(wb[j] >> 16);
                 mma_16x8x16(d, a0, a1, a2, a3, b0, b1);
             }
+            xp += 32;  // 64 columns
         }
         cp_async_wait<0>();
         const int64_t r0 = w * 16 + g, r1 = r0 + 8;
