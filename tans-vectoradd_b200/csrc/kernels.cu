@@ -1224,12 +1224,13 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_dense_kernel(const Den
                        (lane & 7) * 16;
         (void)row;
         const uint8_t *sp = p.sm + sid * 8;
+        const int64_t tstep = K * 8, pf_ahead = 3 * tstep, hstep = 4 * p.C * 2;
         uint2 m_n = live ? ld_stream_v2(sp) : make_uint2(0, 0);
         for (int32_t t = 0; t < n_tiles; t++) {
             const uint2 m = m_n;
-            sp += K * 8;
+            sp += tstep;
             if (live && t + 1 < n_tiles) m_n = ld_stream_v2(sp);
-            if (live && t + 4 < n_tiles) prefetch_l2(sp + 3 * K * 8);
+            if (live && t + 4 < n_tiles) prefetch_l2(sp + pf_ahead);
             const int32_t need = ring_fill<R>(rg, ch, live);
             cp_async_commit();
             cp_async_wait<kDecodeLag>();
@@ -1256,11 +1257,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_dense_kernel(const Den
 #pragma unroll
             for (int h = 0; h < 2; h++) {  // rows (lane >> 3) + 4h
                 const uint4 v = *reinterpret_cast<const uint4 *>(sr + h * 4 * kStageRowWords);
-                asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(
-                                 dst + (int64_t)h * 4 * p.C * 2 + (int64_t)t * 128),
+                asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(dst + h * hstep),
                              "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
                              : "memory");
             }
+            dst += 128;  // 64 bf16 columns
             __syncwarp();
         }
         cp_async_wait<0>();
