@@ -275,6 +275,8 @@ def cpu_decode_add(a, b, tbl, N, n_total, budget_s=10.0):
 
     sa, sb = shard(a), shard(b)
     elems = k_s * N
+    # every core this process may run on (torchrun sets OMP_NUM_THREADS=1)
+    oracle.set_num_threads(len(os.sched_getaffinity(0)))
     reps, t_used = 0, 0.0
     t_start = time.perf_counter()
     while t_used < budget_s and reps < 100000:

@@ -60,6 +60,8 @@ def lib() -> ctypes.CDLL:
         L.oracle_vecadd_fused.restype = ctypes.c_int
         L.oracle_vecadd_fused.argtypes = [p, i64, p, p, p, p, p, i64, p, p, p, p, p, i64, i64, p]
         L.oracle_num_threads.restype = ctypes.c_int
+        L.oracle_set_num_threads.restype = None
+        L.oracle_set_num_threads.argtypes = [ctypes.c_int]
         _LIB = L
     return _LIB
 
@@ -81,6 +83,11 @@ def _np(x, dtype) -> np.ndarray:
 
 def num_threads() -> int:
     return int(lib().oracle_num_threads())
+
+
+def set_num_threads(n: int) -> None:
+    """OpenMP threads of the oracle's parallel loops (n > 0)."""
+    lib().oracle_set_num_threads(int(n))
 
 
 def fp8_add(a: int, b: int) -> int:

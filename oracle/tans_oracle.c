@@ -363,3 +363,14 @@ int oracle_num_threads(void) {
     return 1;
 #endif
 }
+
+/* Thread count of the OpenMP loops above (launchers such as torchrun set
+ * OMP_NUM_THREADS=1 in every rank; the timed CPU baseline wants all cores). */
+void oracle_set_num_threads(int n) {
+#ifdef _OPENMP
+    extern void omp_set_num_threads(int);
+    if (n > 0) omp_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
