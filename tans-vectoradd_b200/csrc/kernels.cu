@@ -513,7 +513,10 @@ Geometry balance(int64_t n_groups, int sms, int max_warps_per_cta) {
 }
 
 constexpr int kTableBytes = kL * kCopies * 4;
-constexpr int kMaxWarps = 16;  // 512 threads per CTA, one CTA per SM (24 measured slower on cfg2)
+constexpr int kMaxWarps = 16;  // 512 threads per CTA, one CTA per SM
+// The decode kernel: up to 6 teams of 4 warps (its registers fit 768
+// threads without spills; cfg2: 2.82 ms vs 2.92 ms with 4 teams)
+constexpr int kDecodeMaxWarps = 24;
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
@@ -568,7 +571,7 @@ constexpr int kStageRowWords = 36;  // 32 + 4 padding: conflict-free staging wri
 constexpr int kStageBytes = 2 * 16 * kStageRowWords * 4;  // double-buffered tile
 
 template <int R, bool kTeams>
-__global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeArgs p) {
+__global__ void __launch_bounds__(kDecodeMaxWarps * 32, 1) decode_kernel(const DecodeArgs p) {
     extern __shared__ __align__(16) uint8_t smem[];
     load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
     __syncthreads();
@@ -617,8 +620,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
         uint32_t *stage = reinterpret_cast<uint32_t *>(
             smem + (ring_area<R>(smem, blockDim.x >> 5, 1) - smem_addr(smem)) +
             (warp / kTeamWarps) * kStageBytes);
-        uint8_t *otp = out_seg + (int64_t)(4 * wi) * K + (col0 - 32 * wi) + 4 * lane;
+        // lane l stores 16 bytes of row 4 wi + l / 8 of the tile (its 128-byte
+        // piece is bytes 16 (l % 8) .. of the team's 128 columns)
+        uint8_t *otp = out_seg + (int64_t)(4 * wi + (lane >> 3)) * K + (col0 - 32 * wi) + 16 * (lane & 7);
         const int64_t srow = kTablePairs * K, orow = 2 * kTablePairs * K;
+        const int64_t k4 = 4 * K, pf_ahead = 3 * srow + (qa & 1) * 4 * K;
         uint32_t w0n = 0, w1n = 0;
         if (full_tiles > 0) {
             w0n = ld_stream_u32(smw);
@@ -629,9 +635,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
             smw += srow;
             if (t + 1 < full_tiles) {
                 w0n = ld_stream_u32(smw);
-                w1n = ld_stream_u32(smw + 4 * K);
+                w1n = ld_stream_u32(smw + k4);
             }
-            if (t + 4 < full_tiles) prefetch_l2(smw + 3 * srow + (qa & 1) * 4 * K);
+            if (t + 4 < full_tiles) prefetch_l2(smw + pf_ahead);
             const int32_t need = ring_fill<R>(rg, ch, live);
             cp_async_commit();
             cp_async_wait<kDecodeLag>();
@@ -664,9 +670,8 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const DecodeA
                 asm volatile("bar.sync %0, %1;" ::"r"(1 + warp / kTeamWarps), "n"(kTeamWarps * 32)
                              : "memory");
                 const uint32_t *rb = stage + (t & 1) * (16 * kStageRowWords) +
-                                     (4 * wi) * kStageRowWords + lane;
-#pragma unroll
-                for (int r = 0; r < 4; r++) st_stream_u32(otp + r * K, rb[r * kStageRowWords]);
+                                     (4 * wi + (lane >> 3)) * kStageRowWords + 4 * (lane & 7);
+                st_stream_v4(otp, *reinterpret_cast<const uint4 *>(rb));
                 otp += orow;
             } else {
                 st_stream_u32(ow, E0);          // element 2b
@@ -1767,17 +1772,18 @@ extern "C" int tans_b200_build_decode_table(const int32_t *spread, const int32_t
     return launch_status("build_table_kernel");
 }
 
-// Decode launch: the team form (output staged per 128-stream block) when
-// rows are word-aligned and the layout's stream count is a multiple of 128,
-// else the per-warp form.
+// Decode launch: the team form (output staged per 128-stream block, 16-byte
+// row stores) when rows are word-aligned, the output is 16-byte aligned and
+// the layout's stream count is a multiple of 128, else the per-warp form.
 template <int R>
 int launch_decode(const DecodeArgs &args, int64_t chains, int sms, cudaStream_t st) {
-    if (!(args.word_rows && args.stride % (kTeamWarps * 32) == 0))
+    if (!(args.word_rows && args.stride % (kTeamWarps * 32) == 0 &&
+          reinterpret_cast<uintptr_t>(args.out) % 16 == 0))
         return launch_ring_kernel<R>(decode_kernel<R, false>, args, 1, chains, sms, st,
                                      "decode_kernel");
     const int per_team = kTeamWarps * R * 128 + kStageBytes;
     int max_t = (kSmemMax - kTableBytes - R * 128) / per_team;
-    if (max_t > kMaxWarps / kTeamWarps) max_t = kMaxWarps / kTeamWarps;
+    if (max_t > kDecodeMaxWarps / kTeamWarps) max_t = kDecodeMaxWarps / kTeamWarps;
     const Geometry geo = balance(chains / (kTeamWarps * 32), sms, max_t);
     const int smem = kTableBytes + R * 128 + geo.warps_per_cta * per_team;
     int rc = set_smem(decode_kernel<R, true>, smem);

@@ -133,6 +133,30 @@ def test_decode_ragged_vs_oracle(cuda, K, N):
     assert np.array_equal(out.T, fp8.numpy())
 
 
+@pytest.mark.parametrize("shift", [0, 4, 16])
+def test_decode_output_alignment(cuda, shift):
+    """K a multiple of 128: a 16-byte aligned output takes the team form
+    (16-byte row stores), a 4-byte aligned one the per-warp word form; both
+    exact, through the C ABI."""
+    from rans_vectoradd._lib import LIB, check
+    K, N = 256, 96
+    gen = torch.Generator().manual_seed(shift)
+    fp8 = random_fp8_bytes(K * N, device="cpu", generator=gen).reshape(K, N)
+    comp, st, off, part, sm, pf, sp = tans_codec.encode(fp8, QWEN)
+    tab = torch.as_tensor(tans_codec.build_decode_table(sp.numpy(), pf.numpy())).to(cuda)
+    d = [t.to(cuda) for t in (comp, off, st, part, sm)]
+    buf = torch.zeros(N * K + 64, dtype=torch.uint8, device=cuda)
+    out = buf[shift:shift + N * K]
+    _C.data_status(cuda)
+    check(LIB.tans_b200_decode(d[0].data_ptr(), d[0].numel(), d[1].data_ptr(), d[2].data_ptr(),
+                               d[3].data_ptr(), d[4].data_ptr(), tab.data_ptr(), out.data_ptr(),
+                               K, N, _C._status(cuda).data_ptr(),
+                               torch.cuda.current_stream(cuda).cuda_stream))
+    assert _C.data_status(cuda) == 0
+    assert torch.equal(out.view(N, K).t().cpu(), fp8)
+    assert not buf[:shift].any() and not buf[shift + N * K:].any()
+
+
 def test_decode_flags_bad_metadata_without_fault(cuda):
     fp8, (comp, st, off, part, sm, pf, sp) = encode_qwen(256, 64, 5)
     _C.data_status(cuda)
