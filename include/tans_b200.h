@@ -260,6 +260,41 @@ int tans_b200_gemv_weight_dense(const uint8_t *compressed,
                                 int64_t rows, int64_t cols, int64_t col_splits,
                                 int32_t *status, void *stream);
 
+/* Peer all-gather of a row-sharded GEMV, fused into its epilogue (no
+ * NCCL): `world` ranks, one per GPU, each own `rows` rows of W starting at
+ * row col0 of the full output; every rank holds the gathered output
+ * [batch][y_ld] in memory that the others can store to (peer or symmetric
+ * memory, one pointer per rank in the device array y_peers).  flag_peers:
+ * device array of each rank's uint32 flag array [world]; flags: this rank's
+ * (= flag_peers[rank]); seq, done: this rank's device uint32 counters, both
+ * zero before the first gather, flags zero on every rank before any rank
+ * starts.  No reference counterpart. */
+typedef struct tans_b200_gather {
+    int32_t rank, world;
+    uint16_t *const *y_peers; /* device array [world] of bf16 [batch][y_ld] buffers */
+    int64_t y_ld;             /* row length of the gathered output */
+    int64_t col0;             /* this rank's first row (column of the gathered output); even */
+    uint32_t *const *flag_peers;
+    uint32_t *flags;
+    uint32_t *seq, *done;
+} tans_b200_gather;
+
+/* y = scale * W @ x^T as tans_b200_gemv (this rank's rows), stored into
+ * every rank's gathered buffer at columns [col0, col0 + rows), then this
+ * rank's flag raised on every rank.  The kernel first waits until all of
+ * this rank's flags have reached the number of gathers it has published, so
+ * x may be (and the call may overwrite) the gathered buffer of an earlier
+ * step: call it in the same order on every rank.  partials: f32
+ * [col_splits][batch][rows], required.  A wait that runs out (a rank that
+ * stopped) ORs TANS_B200_DATA_TIMEOUT into the status word. */
+int tans_b200_gemv_gather(const uint8_t *compressed, int64_t compressed_bytes,
+                          const int32_t *offsets, const uint16_t *states,
+                          const uint8_t *partial, const uint8_t *sign_mantissa,
+                          const int32_t *decode_table, const float *scale,
+                          const uint16_t *x, float *partials, int64_t rows,
+                          int64_t cols, int64_t batch, int64_t col_splits,
+                          const tans_b200_gather *g, int32_t *status, void *stream);
+
 /* Prefill GEMM with the weight decoded on the fly: y [m][rows] bf16 =
  * scale * W @ x^T for x bf16 [m][cols] (16-byte aligned), W in the GEMV
  * stream format (tans_b200_gemv).  Tensor cores (tcgen05.mma, bf16 in, fp32

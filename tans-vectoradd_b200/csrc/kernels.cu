@@ -969,11 +969,39 @@ struct GemvArgs {
     const float *scale;       // [R]
     const uint16_t *x;        // bf16 [B][C]
     uint16_t *y;              // bf16 [B][R]   (KS == 1)
-    float *part;              // f32 [KS][B][R] (KS > 1)
+    float *part;              // f32 [KS][B][R] (KS > 1, or to_partials)
     int64_t R, C, B, KS;
     int32_t *status;
     Opq q;
+    // fused all-gather (tans_b200_gemv_gather): wait until every
+    // wait_flags[q] has reached *wait_seq before reading x; results go to
+    // `part` even for KS == 1
+    const uint32_t *wait_flags;
+    const uint32_t *wait_seq;
+    int32_t wait_n;
+    int32_t to_partials;
 };
+
+constexpr uint32_t kPeerWaitLimit = 1u << 24;  // polls of ~64 ns or more: >1 s
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Bounded wait (one thread) until flags[0..n) have all reached `target`
+// (wrap-safe); false if the limit ran out.
+__device__ __forceinline__ bool peer_wait(const uint32_t *flags, uint32_t target, int n) {
+    for (int q = 0; q < n; q++) {
+        uint32_t i = 0;
+        while ((int32_t)(ld_acquire_sys(flags + q) - target) < 0) {
+            if (++i > kPeerWaitLimit) return false;
+            __nanosleep(64);
+        }
+    }
+    return true;
+}
 
 __device__ __forceinline__ uint32_t cvt_f16x2_e4m3x2(uint32_t v16) {
     uint32_t r;
@@ -1006,6 +1034,11 @@ constexpr int kGemvMaxWarps = 20;
 template <int R>
 __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvArgs p) {
     extern __shared__ __align__(16) uint8_t smem[];
+    if (p.wait_n > 0) {  // x is gathered by the peers' epilogues: wait for all of them
+        if (threadIdx.x == 0 && !peer_wait(p.wait_flags, *p.wait_seq, p.wait_n) && p.status)
+            atomicOr(p.status, TANS_B200_DATA_TIMEOUT);
+        __syncthreads();
+    }
     load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
     const int64_t CS = p.C / p.KS;
     const int k = blockIdx.y;
@@ -1117,7 +1150,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
         const int64_t r0 = w * 16 + g, r1 = r0 + 8;
         const int64_t b0 = 2 * t, b1 = 2 * t + 1;
         if (!live) d[0] = d[1] = d[2] = d[3] = 0.f;
-        if (p.KS == 1) {
+        if (!p.to_partials) {
             const float s0 = p.scale[r0], s1 = p.scale[r1];
             if (b0 < p.B) {
                 p.y[b0 * p.R + r0] = __bfloat16_as_ushort(__float2bfloat16_rn(d[0] * s0));
@@ -1150,6 +1183,56 @@ __global__ void gemv_reduce_kernel(const float *__restrict__ part, const float *
         float acc = 0.f;
         for (int64_t k = 0; k < KS; k++) acc += part[k * n + i];
         y[i] = __bfloat16_as_ushort(__float2bfloat16_rn(acc * scale[i % R]));
+    }
+}
+
+// Fused all-gather epilogue of a row-sharded GEMV: y[b][r] as in
+// gemv_reduce_kernel (same summation order, so the same bits), stored
+// straight into every rank's gathered buffer y_peers[q][b][col0 + r] over
+// NVLink (plain peer stores, two rows per 4-byte store).  The last CTA to
+// finish then publishes: after a system-scope fence it raises this rank's
+// flag in every rank's flag array to seq + 1 (release, system scope) and
+// advances seq.  A reader that has seen all flags reach its own seq (see
+// peer_wait) sees every rank's shard of the step.
+struct PublishArgs {
+    const float *part;  // f32 [KS][B][R]
+    const float *scale; // [R]
+    int64_t R, B, KS;
+    uint16_t *const *y_peers;
+    int64_t y_ld, col0;
+    uint32_t *const *flag_peers;
+    uint32_t *seq, *done;
+    int32_t world, rank;
+};
+
+__global__ void gemv_publish_kernel(const PublishArgs p) {
+    const int64_t half = p.R / 2, n = half * p.B, plane = p.R * p.B;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = i / half, r = 2 * (i - b * half), e = b * p.R + r;
+        float a0 = 0.f, a1 = 0.f;
+        for (int64_t k = 0; k < p.KS; k++) {
+            a0 += p.part[k * plane + e];
+            a1 += p.part[k * plane + e + 1];
+        }
+        const uint32_t v = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a0 * p.scale[r])) |
+                           ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a1 * p.scale[r + 1])) << 16);
+        const int64_t off = b * p.y_ld + p.col0 + r;
+        for (int q = 0; q < p.world; q++)
+            *reinterpret_cast<uint32_t *>(p.y_peers[q] + off) = v;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        if (atomicAdd(p.done, 1u) == gridDim.x - 1) {  // every CTA's stores are fenced
+            *p.done = 0;
+            __threadfence_system();
+            const uint32_t v = *p.seq + 1u;
+            for (int q = 0; q < p.world; q++)
+                asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p.flag_peers[q] + p.rank), "r"(v)
+                             : "memory");
+            *p.seq = v;
+        }
     }
 }
 
@@ -1956,6 +2039,39 @@ extern "C" int tans_b200_fp8_vecadd_fused_split(
     return launch_fused(args, n_streams * segs, segment_pairs, sms, (cudaStream_t)stream);
 }
 
+// Geometry and launch of gemv_kernel (the plain GEMV and the gathering one).
+static int launch_gemv_kernel(const GemvArgs &args, int sms, cudaStream_t st) {
+    const int64_t rows = args.R, cols = args.C, col_splits = args.KS;
+    int rc = TANS_B200_OK;
+    const int64_t cs = cols / col_splits;
+    const int rr = ring_rows(cs / 8);
+    const int64_t xbytes = ((kGemvMaxBatch * (cs + 8) * 2) + 127) / 128 * 128;
+    const int64_t fixed = kTableBytes + xbytes + rr * 128;
+    const int64_t per_warp = 2 * rr * 128;
+    int64_t max_w = (kSmemMax - fixed) / per_warp;
+    if (max_w > kGemvMaxWarps) max_w = kGemvMaxWarps;
+    if (max_w < 1)
+        return fail(TANS_B200_ERR_INVALID,
+                    "gemv: a column slice of %lld does not fit in shared memory; use more col_splits",
+                    (long long)cs);
+    const int64_t groups = rows / 16;
+    int64_t gx = sms / col_splits;
+    if (gx < 1) gx = 1;
+    const int64_t rounds = (groups + gx * max_w - 1) / (gx * max_w);
+    const int64_t wpc = (groups + gx * rounds - 1) / (gx * rounds);
+    gx = (groups + wpc * rounds - 1) / (wpc * rounds);
+    const int smem = (int)(fixed + wpc * per_warp);
+    const dim3 grid((unsigned)gx, (unsigned)col_splits);
+    switch (rr) {
+        case 16: rc = set_smem(gemv_kernel<16>, smem); if (!rc) gemv_kernel<16><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
+        case 32: rc = set_smem(gemv_kernel<32>, smem); if (!rc) gemv_kernel<32><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
+        case 64: rc = set_smem(gemv_kernel<64>, smem); if (!rc) gemv_kernel<64><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
+        default: rc = set_smem(gemv_kernel<128>, smem); if (!rc) gemv_kernel<128><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
+    }
+    if (rc) return rc;
+    return launch_status("gemv_kernel");
+}
+
 extern "C" int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_bytes,
                               const int32_t *offsets, const uint16_t *states,
                               const uint8_t *partial, const uint8_t *sm,
@@ -1980,37 +2096,12 @@ extern "C" int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_byte
     int sms;
     int rc = device_setup(&sms);
     if (rc) return rc;
-    const int64_t cs = cols / col_splits;
-    const int rr = ring_rows(cs / 8);
-    const int64_t xbytes = ((kGemvMaxBatch * (cs + 8) * 2) + 127) / 128 * 128;
-    const int64_t fixed = kTableBytes + xbytes + rr * 128;
-    const int64_t per_warp = 2 * rr * 128;
-    int64_t max_w = (kSmemMax - fixed) / per_warp;
-    if (max_w > kGemvMaxWarps) max_w = kGemvMaxWarps;
-    if (max_w < 1)
-        return fail(TANS_B200_ERR_INVALID,
-                    "gemv: a column slice of %lld does not fit in shared memory; use more col_splits",
-                    (long long)cs);
-    const int64_t groups = rows / 16;
-    int64_t gx = sms / col_splits;
-    if (gx < 1) gx = 1;
-    const int64_t rounds = (groups + gx * max_w - 1) / (gx * max_w);
-    const int64_t wpc = (groups + gx * rounds - 1) / (gx * rounds);
-    gx = (groups + wpc * rounds - 1) / (wpc * rounds);
-    const int smem = (int)(fixed + wpc * per_warp);
     GemvArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets, states,
                   partial, sm, decode_table, scale, x, y, partials, rows, cols, batch, col_splits,
                   status, make_opq()};
+    args.to_partials = col_splits > 1;
     cudaStream_t st = (cudaStream_t)stream;
-    const dim3 grid((unsigned)gx, (unsigned)col_splits);
-    switch (rr) {
-        case 16: rc = set_smem(gemv_kernel<16>, smem); if (!rc) gemv_kernel<16><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
-        case 32: rc = set_smem(gemv_kernel<32>, smem); if (!rc) gemv_kernel<32><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
-        case 64: rc = set_smem(gemv_kernel<64>, smem); if (!rc) gemv_kernel<64><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
-        default: rc = set_smem(gemv_kernel<128>, smem); if (!rc) gemv_kernel<128><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
-    }
-    if (rc) return rc;
-    rc = launch_status("gemv_kernel");
+    rc = launch_gemv_kernel(args, sms, st);
     if (rc || col_splits == 1) return rc;
     const int64_t n = rows * batch;
     const int threads = 256;
@@ -2018,6 +2109,57 @@ extern "C" int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_byte
     gemv_reduce_kernel<<<(unsigned)(blocks < 4 * sms ? blocks : 4 * sms), threads, 0, st>>>(
         partials, scale, y, rows, batch, col_splits);
     return launch_status("gemv_reduce_kernel");
+}
+
+extern "C" int tans_b200_gemv_gather(const uint8_t *compressed, int64_t compressed_bytes,
+                                     const int32_t *offsets, const uint16_t *states,
+                                     const uint8_t *partial, const uint8_t *sm,
+                                     const int32_t *decode_table, const float *scale,
+                                     const uint16_t *x, float *partials, int64_t rows, int64_t cols,
+                                     int64_t batch, int64_t col_splits, const tans_b200_gather *g,
+                                     int32_t *status, void *stream) {
+    tans_b200::clear_error();
+    if (rows <= 0 || rows % 16 != 0) return fail(TANS_B200_ERR_INVALID, "gemv: rows must be a positive multiple of 16");
+    if (col_splits < 1 || cols <= 0 || cols % (64 * col_splits) != 0)
+        return fail(TANS_B200_ERR_INVALID, "gemv: cols must be a positive multiple of 64 * col_splits");
+    if (batch < 1 || batch > kGemvMaxBatch) return fail(TANS_B200_ERR_INVALID, "gemv: batch must be 1..8");
+    if (!compressed || !offsets || !states || !partial || !sm || !decode_table || !scale || !x ||
+        !partials || !g)
+        return fail(TANS_B200_ERR_INVALID, "gemv_gather: null pointer");
+    if (g->world < 1 || g->world > kMaxDevices || g->rank < 0 || g->rank >= g->world)
+        return fail(TANS_B200_ERR_INVALID, "gemv_gather: rank %d of %d", (int)g->rank, (int)g->world);
+    if (!g->y_peers || !g->flag_peers || !g->flags || !g->seq || !g->done)
+        return fail(TANS_B200_ERR_INVALID, "gemv_gather: null pointer in the gather descriptor");
+    if (g->col0 < 0 || g->col0 % 2 != 0 || g->y_ld % 2 != 0 || g->col0 + rows > g->y_ld)
+        return fail(TANS_B200_ERR_INVALID,
+                    "gemv_gather: this rank's rows [col0, col0 + rows) must lie in the gathered row "
+                    "length y_ld; col0 and y_ld even");
+    if (!aligned(compressed, 4) || !aligned(offsets, 4) || !aligned(states, 2) || !aligned(sm, 8) ||
+        !aligned(decode_table, 4) || !aligned(scale, 4) || !aligned(x, 2) || !aligned(partials, 4) ||
+        !aligned(g->flags, 4) || !aligned(g->seq, 4) || !aligned(g->done, 4))
+        return fail(TANS_B200_ERR_INVALID, "gemv_gather: misaligned buffer");
+    if (compressed_bytes < 0 || compressed_bytes % 4 != 0)
+        return fail(TANS_B200_ERR_INVALID, "compressed length must be divisible by 4 bytes");
+    int sms;
+    int rc = device_setup(&sms);
+    if (rc) return rc;
+    GemvArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets, states,
+                  partial, sm, decode_table, scale, x, nullptr, partials, rows, cols, batch,
+                  col_splits, status, make_opq()};
+    args.wait_flags = g->flags;
+    args.wait_seq = g->seq;
+    args.wait_n = g->world;
+    args.to_partials = 1;
+    cudaStream_t st = (cudaStream_t)stream;
+    rc = launch_gemv_kernel(args, sms, st);
+    if (rc) return rc;
+    const PublishArgs pa{partials, scale, rows, batch, col_splits, g->y_peers, g->y_ld, g->col0,
+                         g->flag_peers, g->seq, g->done, g->world, g->rank};
+    const int64_t n = rows / 2 * batch;
+    const int threads = 256;
+    const int64_t blocks = (n + threads - 1) / threads;
+    gemv_publish_kernel<<<(unsigned)(blocks < 2 * sms ? blocks : 2 * sms), threads, 0, st>>>(pa);
+    return launch_status("gemv_publish_kernel");
 }
 
 // y[m][r] = bf16(acc[m][r] * scale[r]): the prefill epilogue after the

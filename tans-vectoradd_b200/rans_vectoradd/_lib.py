@@ -46,6 +46,8 @@ def _load() -> ctypes.CDLL:
                                              i64, i64, p, p]),
         "tans_b200_decode_noalloc": (i32, [p, i64, p, p, p, p, p, p, i64, p, i64, i64, p, p]),
         "tans_b200_gemv": (i32, [p, i64, p, p, p, p, p, p, p, p, p, i64, i64, i64, i64, p, p]),
+        "tans_b200_gemv_gather": (i32, [p, i64, p, p, p, p, p, p, p, p, i64, i64, i64, i64, p, p,
+                                        p]),
         "tans_b200_gemv_weight_dense": (i32, [p, i64, p, p, p, p, p, p, i64, i64, i64, p, p]),
         "tans_b200_scale_rows_bf16": (i32, [p, p, p, i64, i64, p]),
         "tans_b200_gemm_tc": (i32, [p, i64, p, p, p, p, p, p, p, p, i64, i64, i64, i64, p, p]),

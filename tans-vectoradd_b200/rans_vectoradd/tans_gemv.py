@@ -19,6 +19,7 @@ each stream:
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -133,6 +134,39 @@ def gemv(weight: EncodedWeight, x: torch.Tensor, out: torch.Tensor | None = None
             weight.table.data_ptr(), weight.scale.data_ptr(), x.data_ptr(), out.data_ptr(),
             partials.data_ptr() if partials is not None else None, R, C, B, KS,
             _status(dev).data_ptr(), _stream(dev)))
+    return out
+
+
+def gemv_gather(weight: EncodedWeight, x: torch.Tensor, gather, k: int, col0: int,
+                partials: torch.Tensor | None = None) -> torch.Tensor:
+    """This rank's row shard of a GEMV (rows col0 .. col0 + weight.rows of the
+    full output), stored into every rank's gathered buffer `gather.views[k]`
+    by the GEMV epilogue itself (rans_vectoradd.peer.PeerGather); returns
+    this rank's view of the gathered [batch, width] output.  The kernel
+    first waits for every rank's previous gather, so x may be a gathered
+    buffer of an earlier step."""
+    _req(x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(),
+         "x must be a contiguous CUDA bfloat16 [batch, cols] tensor")
+    B, C = x.shape
+    _req(C == weight.cols, f"x has {C} columns, the weight {weight.cols}")
+    _req(1 <= B <= 8, "batch must be 1..8")
+    out = gather.views[k]
+    _req(out.shape[0] == B, f"gathered buffer holds batch {out.shape[0]}, x has {B}")
+    dev = x.device
+    _same_device(dev, weight.compressed, weight.offsets, weight.states, weight.partial,
+                 weight.sm, weight.table, weight.scale, out)
+    R, KS = weight.rows, weight.col_splits
+    with torch.cuda.device(dev):
+        if partials is None:
+            partials = torch.empty((KS, B, R), dtype=torch.float32, device=dev)
+        _req(partials.numel() >= KS * B * R and partials.dtype == torch.float32,
+             "partials must be f32 with col_splits * batch * rows elements")
+        desc = gather.descriptor(k, col0)
+        check(LIB.tans_b200_gemv_gather(
+            weight.compressed.data_ptr(), weight.compressed.numel(), weight.offsets.data_ptr(),
+            weight.states.data_ptr(), weight.partial.data_ptr(), weight.sm.data_ptr(),
+            weight.table.data_ptr(), weight.scale.data_ptr(), x.data_ptr(), partials.data_ptr(),
+            R, C, B, KS, ctypes.addressof(desc), _status(dev).data_ptr(), _stream(dev)))
     return out
 
 

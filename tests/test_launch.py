@@ -94,3 +94,19 @@ def test_launcher_two_ranks(tmp_path):
     line = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
     assert line["ranks"] == 2 and line["ranks_bit_exact"] == 2
     assert line["elements_per_input"] == 1024 * 256
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_gather_stack_two_ranks():
+    """Fused peer all-gather of a row-sharded GEMV stack == GEMV + NCCL
+    all-gather, bit for bit, eagerly and over CUDA-graph replays."""
+    env = dict(os.environ, PYTHONPATH=os.pathsep.join(
+        [os.path.join(ROOT, "tans-vectoradd_b200"), os.environ.get("PYTHONPATH", "")]))
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+           "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
+           os.path.join(ROOT, "tests", "peer_gather_worker.py")]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
+    assert line == {"world": 2, "exact": True, "replay_exact": True, "status_clean": True}
