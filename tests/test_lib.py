@@ -112,3 +112,35 @@ def test_streams_per_block_env_validation(monkeypatch):
         _C._streams_per_block_from_env()
     monkeypatch.setenv("TANS_STREAMS_PER_BLOCK", "4")
     assert _C._streams_per_block_from_env() == 4
+
+
+def test_gather_descriptor_matches_header(tmp_path):
+    """rans_vectoradd.peer.GatherDesc has the layout of tans_b200_gather."""
+    from rans_vectoradd.peer import GatherDesc, layout
+    src = tmp_path / "g.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "tans_b200.h"\n'
+                   "int main(void) { printf(\"%zu\", sizeof(tans_b200_gather));\n"
+                   + "".join(f' printf(" %zu", offsetof(tans_b200_gather, {f}));'
+                             for f, _ in GatherDesc._fields_) + " return 0; }\n")
+    exe = tmp_path / "g"
+    subprocess.run(["gcc", "-std=c11", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)],
+                   check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True,
+                                          check=True).stdout.split()]
+    assert got == [ctypes.sizeof(GatherDesc)] + [getattr(GatherDesc, f).offset
+                                                 for f, _ in GatherDesc._fields_]
+    offs, total = layout([1024, 512], 3, 8)
+    assert offs[0] >= 32 and all(o % 256 == 0 for o in offs) and total % 256 == 0
+    assert offs[1] - offs[0] >= 3 * 1024 * 2 and total - offs[1] >= 3 * 512 * 2
+
+
+def test_gemv_gather_rejects_bad_descriptors_without_device():
+    from rans_vectoradd.peer import GatherDesc
+    d = ctypes.c_void_p(16)  # never dereferenced: the checks come first
+    args = [d, 4, d, d, d, d, d, d, d, d, 32, 64, 1, 1]
+    assert LIB.tans_b200_gemv_gather(*args, None, None, None) == 1
+    bad = GatherDesc(2, 2, 16, 64, 0, 16, 16, 16, 16)  # rank outside [0, world)
+    assert LIB.tans_b200_gemv_gather(*args, ctypes.addressof(bad), None, None) == 1
+    assert "rank 2 of 2" in LIB.tans_b200_last_error().decode()
+    odd = GatherDesc(0, 2, 16, 64, 1, 16, 16, 16, 16)  # odd column offset
+    assert LIB.tans_b200_gemv_gather(*args, ctypes.addressof(odd), None, None) == 1
