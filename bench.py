@@ -725,7 +725,7 @@ def run_stack(args, ws, rank, dev, barrier):
               "collective": ("fused: GEMV epilogue stores its y shard into every rank's gathered "
                              "buffer over NVLink (symmetric memory), flag wait in the next GEMV"
                              if ws > 1 else "none (one rank)"),
-              "ms_per_forward_nccl_all_gather": round(ms_nccl / args.steps, 4),
+              "ms_per_forward_nccl_all_gather": round(ms_nccl / args.steps, 4) if ws > 1 else None,
               "fused_bit_exact_vs_nccl": exact}, args)
 
 

@@ -75,18 +75,28 @@ def stream_matrix(w8: torch.Tensor, col_splits: int = 1) -> torch.Tensor:
     return v.permute(0, 3, 1, 2, 6, 4, 5, 7).reshape(R * 4 * KS, CS // 4).contiguous()
 
 
-def default_col_splits(rows: int, cols: int, sms: int = 148, warps_per_sm: int = 40) -> int:
-    """Column slices giving each SM up to about `warps_per_sm` warps (one warp
-    per 16-row group and slice), keeping a slice a multiple of 64 columns and
-    at least 1024 columns (shorter streams spend more on per-stream setup).
-    On B200, [17408 x 5120] -> 5 slices (68 us vs 72 us with 2) and
-    [5120 x 17408] -> 16 (70 us vs 72 us with 8)."""
-    want = max(1, round(sms * warps_per_sm / max(1, rows // 16)))
-    best = 1
-    for ks in range(1, want + 1):
-        if cols % (64 * ks) == 0 and cols // ks >= 1024:
-            best = ks
-    return best
+def default_col_splits(rows: int, cols: int, sms: int = 148, warps_per_sm: int = 40,
+                       min_warps_per_sm: int = 16) -> int:
+    """Column slices (one GEMV warp per 16-row group and slice).  First the
+    most slices up to about `warps_per_sm` warps per SM with slices of at
+    least 1024 columns (shorter streams spend more on per-stream setup);
+    if that leaves fewer than `min_warps_per_sm` warps per SM (row shards of
+    a multi-GPU stack), the fewest slices of at least 512, then 256, columns
+    that reach it.  Slices are multiples of 64 columns.  On B200 at batch 8:
+    [17408 x 5120] -> 5, [5120 x 17408] -> 17, [4352 x 5120] -> 10 (25 us vs
+    33 us with 5), [1280 x 17408] -> 34 (27 vs 33 us with 17), [640 x 17408]
+    -> 68 (21 vs 33 us with 17)."""
+    groups = max(1, rows // 16)
+    ok = lambda ks, min_cs: cols % (64 * ks) == 0 and cols // ks >= min_cs  # noqa: E731
+    want = max(1, round(sms * warps_per_sm / groups))
+    ks = max([k for k in range(1, want + 1) if ok(k, 1024)], default=1)
+    for min_cs in (512, 256):
+        if groups * ks >= sms * min_warps_per_sm:
+            break
+        more = [k for k in range(ks + 1, cols // 64 + 1) if ok(k, min_cs)]
+        hit = [k for k in more if groups * k >= sms * min_warps_per_sm]
+        ks = hit[0] if hit else (more[-1] if more else ks)
+    return ks
 
 
 def encode_weight(w8: torch.Tensor, scale: torch.Tensor, exp_freqs=None,
