@@ -432,7 +432,7 @@ extern "C" int tans_b200_encode_device_workspace_bytes(int64_t K, int64_t n, int
                                                        int64_t segment_pairs, int64_t *bytes) {
     tans_b200::clear_error();
     if (!bytes) return fail(TANS_B200_ERR_INVALID, "encode_device_workspace_bytes: bytes is null");
-    int64_t P, segs;
+    int64_t P = 0, segs = 0;
     int rc = check_shape(input_kind, K, n, segment_pairs, &P, &segs);
     if (rc) return rc;
     const int64_t chains = K * segs, B = (chains + kBlk - 1) / kBlk;
@@ -447,7 +447,7 @@ extern "C" int tans_b200_encode_device_plan(const uint8_t *in, int input_kind, i
                                             uint16_t *states_out, uint8_t *partial_out,
                                             int32_t *offsets_out, void *workspace, void *stream) {
     tans_b200::clear_error();
-    int64_t P, segs;
+    int64_t P = 0, segs = 0;
     int rc = check_shape(input_kind, K, n, segment_pairs, &P, &segs);
     if (rc) return rc;
     const bool fp8 = input_kind == TANS_B200_ENC_INPUT_FP8;
@@ -502,7 +502,7 @@ extern "C" int tans_b200_encode_device_emit(int input_kind, int64_t K, int64_t n
                                             const void *workspace, uint8_t *compressed,
                                             void *stream) {
     tans_b200::clear_error();
-    int64_t P, segs;
+    int64_t P = 0, segs = 0;
     int rc = check_shape(input_kind, K, n, segment_pairs, &P, &segs);
     if (rc) return rc;
     if (K == 0) return TANS_B200_OK;

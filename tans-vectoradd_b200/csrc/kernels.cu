@@ -2098,8 +2098,7 @@ extern "C" int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_byte
     if (rc) return rc;
     GemvArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets, states,
                   partial, sm, decode_table, scale, x, y, partials, rows, cols, batch, col_splits,
-                  status, make_opq()};
-    args.to_partials = col_splits > 1;
+                  status, make_opq(), nullptr, nullptr, 0, (int32_t)(col_splits > 1)};
     cudaStream_t st = (cudaStream_t)stream;
     rc = launch_gemv_kernel(args, sms, st);
     if (rc || col_splits == 1) return rc;
@@ -2145,11 +2144,7 @@ extern "C" int tans_b200_gemv_gather(const uint8_t *compressed, int64_t compress
     if (rc) return rc;
     GemvArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets, states,
                   partial, sm, decode_table, scale, x, nullptr, partials, rows, cols, batch,
-                  col_splits, status, make_opq()};
-    args.wait_flags = g->flags;
-    args.wait_seq = g->seq;
-    args.wait_n = g->world;
-    args.to_partials = 1;
+                  col_splits, status, make_opq(), g->flags, g->seq, g->world, 1};
     cudaStream_t st = (cudaStream_t)stream;
     rc = launch_gemv_kernel(args, sms, st);
     if (rc) return rc;
