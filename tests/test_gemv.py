@@ -131,7 +131,8 @@ def test_gemm_large_batch_matches_reference(cuda, B):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("R,C,B,KS", [(128, 512, 16, 1), (256, 1024, 40, 1), (1024, 5120, 64, 5),
-                                      (512, 4352, 300, 4), (17408, 5120, 256, None)])
+                                      (512, 4352, 300, 4), (17408, 5120, 256, None),
+                                      (128, 512, 1, 1), (384, 2048, 5, 2)])
 def test_gemm_tc_matches_reference(cuda, R, C, B, KS):
     """Decode into shared memory + tcgen05 MMA: rel err within the GEMV bound,
     tokens beyond one 256-token tile and ragged token counts included."""
