@@ -968,8 +968,8 @@ struct GemvArgs {
     const int32_t *table;
     const float *scale;       // [R]
     const uint16_t *x;        // bf16 [B][C]
-    uint16_t *y;              // bf16 [B][R]   (KS == 1)
-    float *part;              // f32 [KS][B][R] (KS > 1, or to_partials)
+    uint16_t *y;              // bf16 [B][R]   (written directly when !to_partials)
+    float *part;              // f32 [KS][B][R] (when to_partials: KS > 1, or a gathering GEMV)
     int64_t R, C, B, KS;
     int32_t *status;
     Opq q;
