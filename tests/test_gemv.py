@@ -145,3 +145,63 @@ def test_gemm_tc_matches_reference(cuda, R, C, B, KS):
     assert _C.data_status(cuda) == 0
     ref = tans_gemv.reference_gemv(w8.to(cuda), s.to(cuda), x)
     assert tans_gemv.rel_err(y, ref) <= TOL
+
+
+class _LocalGather:
+    """A gather descriptor over local buffers only (one GPU): `world` ranks
+    whose gathered buffers and flag arrays all live on this device."""
+
+    def __init__(self, dev, batch, rows, world):
+        from rans_vectoradd.peer import GatherDesc
+        self._desc = GatherDesc
+        self.world = world
+        self.bufs = [torch.zeros((batch, rows * world), dtype=torch.bfloat16, device=dev)
+                     for _ in range(world)]
+        self.flag_arrays = [torch.zeros(world, dtype=torch.int32, device=dev) for _ in range(world)]
+        self.y_peers = torch.tensor([b.data_ptr() for b in self.bufs], dtype=torch.int64, device=dev)
+        self.flag_peers = torch.tensor([f.data_ptr() for f in self.flag_arrays], dtype=torch.int64,
+                                       device=dev)
+        self.seq = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.done = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.views = [self.bufs[0]]
+
+    def descriptor(self, k, col0):
+        return self._desc(0, self.world, self.y_peers.data_ptr(), self.bufs[0].shape[1], col0,
+                          self.flag_peers.data_ptr(), self.flag_arrays[0].data_ptr(),
+                          self.seq.data_ptr(), self.done.data_ptr())
+
+
+@pytest.mark.gpu
+def test_gemv_gather_one_rank_equals_gemv(cuda):
+    """World 1: the gathering GEMV publishes to itself; same bits as gemv,
+    flag and counter advance by one per call."""
+    from rans_vectoradd import _C
+    w8, s = make(256, 2048, 5)
+    enc = tans_gemv.encode_weight(w8.to(cuda), s.to(cuda), col_splits=2)
+    x = torch.randn(3, 2048, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16).to(cuda)
+    g = _LocalGather(cuda, 3, 256, 1)
+    _C.data_status(cuda)
+    for step in (1, 2):
+        y = tans_gemv.gemv_gather(enc, x, g, 0, 0)
+        assert torch.equal(y.view(torch.int16), tans_gemv.gemv(enc, x).view(torch.int16))
+        assert int(g.seq.item()) == step and int(g.flag_arrays[0][0].item()) == step
+    assert _C.data_status(cuda) == 0
+
+
+@pytest.mark.gpu
+def test_gemv_gather_wait_runs_out_without_hang(cuda):
+    """A peer that never publishes: the GEMV's bounded wait gives up (about a
+    second per flag), the kernel returns and reports TANS_B200_DATA_TIMEOUT."""
+    import time
+    from rans_vectoradd import _C
+    w8, s = make(128, 512, 6)
+    enc = tans_gemv.encode_weight(w8.to(cuda), s.to(cuda), col_splits=1)
+    x = torch.randn(1, 512, generator=torch.Generator().manual_seed(6)).to(torch.bfloat16).to(cuda)
+    g = _LocalGather(cuda, 1, 128, 2)
+    g.seq.fill_(1)  # this rank has "published" once; no peer ever has
+    _C.data_status(cuda)
+    t0 = time.time()
+    tans_gemv.gemv_gather(enc, x, g, 0, 0)
+    st = _C.data_status(cuda)
+    assert st & 8, f"status {st}: the wait did not report running out"
+    assert time.time() - t0 < 30
