@@ -230,8 +230,8 @@ int tans_b200_fp8_vecadd_fused_host(
     int64_t n_fp8_per_stream, int64_t chunk_streams, void *workspace,
     int64_t workspace_bytes, int32_t *status, void *stream);
 
-/* Fused tANS-decode GEMV (no counterpart in the reference; the BASELINE
- * configuration cfg3/cfg4):
+/* Fused tANS-decode GEMV (no counterpart in the reference; the workload is
+ * an e4m3 weight matrix such as a 17408 x 5120 MLP projection):
  *   y[b][r] = bf16(scale[r] * sum_c e4m3(W[r][c]) * x[b][c]), fp32 accumulate,
  * W rows x cols e4m3 stored as tANS streams in the GEMV stream order
  * (rans_vectoradd.tans_gemv.encode_weight): K = rows*4*col_splits streams of

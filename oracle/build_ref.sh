@@ -10,13 +10,14 @@
 # Tests and the CPU-baseline leg of bench.py load it as the checker.  Nothing
 # in the product links it.
 #
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default: /root/reference)
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default: $TANS_REFERENCE_ROOT, else a
+# sibling checkout named "reference" next to this repository)
 # Flags follow the reference's setup.py:40-63 (-O3 --use_fast_math -lineinfo,
 # cxx -O3 -fopenmp) with the arch fixed to sm_100a.
 set -euo pipefail
 
-REF="${1:-/root/reference}"
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
+REF="${1:-${TANS_REFERENCE_ROOT:-$HERE/../../reference}}"
 OUT="$HERE/_ref"
 BUILD="$OUT/build"
 

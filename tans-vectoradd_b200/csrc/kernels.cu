@@ -2393,9 +2393,8 @@ extern "C" int tans_b200_decode_noalloc(const uint8_t *compressed, int64_t compr
     tans_b200::clear_error();
     if (n_syms <= 0 || n_syms > 256)
         return fail(TANS_B200_ERR_INVALID,
-                    "decode_noalloc: alphabet of %lld symbols exceeds the scratch table "
-                    "(1..256 symbols, %d entries)",
-                    (long long)n_syms, kNoAllocTableEntries);
+                    "decode_noalloc: alphabet must be 1..256 symbols (got %lld)",
+                    (long long)n_syms);
     if (n_fp8_per_stream < 0 || n_fp8_per_stream % 2 != 0)
         return fail(TANS_B200_ERR_INVALID, "n_fp8_per_stream must be even");
     if (compressed_bytes < 0 || compressed_bytes % 4 != 0)

@@ -154,7 +154,10 @@ def gemv_gather(weight: EncodedWeight, x: torch.Tensor, gather, k: int, col0: in
     by the GEMV epilogue itself (rans_vectoradd.peer.PeerGather); returns
     this rank's view of the gathered [batch, width] output.  The kernel
     first waits for every rank's previous gather, so x may be a gathered
-    buffer of an earlier step."""
+    buffer of an earlier step, but never `gather.views[k]` itself (or any
+    tensor sharing its memory): a faster peer's epilogue of this step may
+    already be writing there while this rank's GEMV still reads x.
+    Consecutive gathers must therefore alternate between buffers."""
     _req(x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(),
          "x must be a contiguous CUDA bfloat16 [batch, cols] tensor")
     B, C = x.shape
@@ -162,6 +165,11 @@ def gemv_gather(weight: EncodedWeight, x: torch.Tensor, gather, k: int, col0: in
     _req(1 <= B <= 8, "batch must be 1..8")
     out = gather.views[k]
     _req(out.shape[0] == B, f"gathered buffer holds batch {out.shape[0]}, x has {B}")
+    xs, xe = x.data_ptr(), x.data_ptr() + x.numel() * x.element_size()
+    os_, oe = out.data_ptr(), out.data_ptr() + out.numel() * out.element_size()
+    _req(xe <= os_ or oe <= xs,
+         f"x overlaps the gathered buffer views[{k}] that this GEMV writes; "
+         "use a different gathered buffer for consecutive gathers")
     dev = x.device
     _same_device(dev, weight.compressed, weight.offsets, weight.states, weight.partial,
                  weight.sm, weight.table, weight.scale, out)

@@ -80,7 +80,9 @@ def cfg0_inputs(n: int):
 
 
 def main() -> None:
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get(
+        "TANS_REFERENCE_ROOT",
+        os.path.join(os.path.dirname(os.path.abspath(__file__)), "..", "..", "..", "reference"))
     tc, data = load_reference(root)
     qwen = torch.tensor(data.QWEN3_14B_FP8_EXP, dtype=torch.float64)
     digests: dict = {"torch": torch.__version__, "numpy": np.__version__, "cases": {}}

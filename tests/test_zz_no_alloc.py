@@ -51,8 +51,46 @@ def test_noalloc_decode_matches_regular_decode_twice(cuda):
         assert int(status.item()) == 0
 
 
-def test_noalloc_rejects_alphabet_beyond_scratch():
+def test_noalloc_rejects_alphabet_beyond_table_build():
     rc = LIB.tans_b200_decode_noalloc(None, 4, None, None, None, None, None, None, 257, None,
                                       1, 2, None, None)
     assert rc == 1
-    assert "exceeds the scratch table" in LIB.tans_b200_last_error().decode()
+    assert "alphabet must be 1..256 symbols" in LIB.tans_b200_last_error().decode()
+
+
+@pytest.mark.gpu
+def test_noalloc_decode_allocates_no_device_memory(cuda):
+    """The defining property: after a first call (which resolves the scratch
+    array's device address), further calls on the current and on a second
+    stream leave the device's free memory unchanged."""
+    gen = torch.Generator().manual_seed(23)
+    K, N = 512, 512
+    fp8 = random_fp8_bytes(K * N, device="cpu", generator=gen).reshape(K, N)
+    comp, st, off, part, sm, pf, sp = tans_codec.encode(
+        fp8, torch.tensor(QWEN3_14B_FP8_EXP, dtype=torch.float64))
+    args = [t.to(cuda) for t in (comp, off, st, part, sm, sp, pf)]
+    status = torch.zeros(1, dtype=torch.int32, device=cuda)
+    outs = [torch.empty((N, K), dtype=torch.uint8, device=cuda) for _ in range(2)]
+    side = torch.cuda.Stream(cuda)
+
+    def call(out, stream):
+        rc = LIB.tans_b200_decode_noalloc(
+            args[0].data_ptr(), args[0].numel(), args[1].data_ptr(), args[2].data_ptr(),
+            args[3].data_ptr(), args[4].data_ptr(), args[5].data_ptr(), args[6].data_ptr(),
+            args[6].numel(), out.data_ptr(), K, N, status.data_ptr(), stream.cuda_stream)
+        assert rc == 0, LIB.tans_b200_last_error().decode()
+
+    call(outs[0], torch.cuda.current_stream(cuda))
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info(cuda)
+    for _ in range(3):
+        call(outs[0], torch.cuda.current_stream(cuda))
+    torch.cuda.synchronize()
+    side.wait_stream(torch.cuda.current_stream(cuda))
+    for _ in range(3):
+        call(outs[1], side)
+    side.synchronize()
+    torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info(cuda)
+    assert free1 == free0
+    assert torch.equal(outs[0].cpu().t(), fp8) and torch.equal(outs[1].cpu().t(), fp8)
