@@ -5,7 +5,7 @@
 //   vecadd_raw_kernel    csrc/vecadd.cu:41-73         (uncompressed FP8 add)
 //   build_table_kernel   csrc/tans_decode.cu:23-59    (host table build, per call)
 //   decode_kernel        csrc/tans_decode.cu:125-155  (standalone decode, [N,K] out)
-//   fused_split_kernel   csrc/vecadd.cu:156-243       (decode A and B + add, tiled out)
+//   fused_pair_kernel    csrc/vecadd.cu:156-243       (decode A and B + add, tiled out)
 //
 // Design (B200-first, not a translation of the reference):
 //  * FP8 add: e4m3x2 -> f16x2 (exact), add.rn.f16x2, cvt.rn.satfinite.e4m3x2.
@@ -274,6 +274,9 @@ struct Opq {
     uint32_t x8;     // 8:    x * 8 = x << 3
     uint32_t step;   // 4 * kCopies (bytes between successive entries of a copy)
     int32_t back;    // -128: one slab row down, in words
+    int32_t back64;  // -64: one slab row down in the fused kernel's 64-unit rows
+    uint32_t p26;    // 2^26: mul.hi.s32(v, p26) = v >> 6 (row of a 64-unit v)
+    uint32_t ru, rq; // 2^(26 - lg R), 2^(lg R + 6): ring row offset of a 64-unit v (set per launch)
 };
 
 __device__ __forceinline__ uint32_t mul_lo(uint32_t x, uint32_t y) {
@@ -284,6 +287,11 @@ __device__ __forceinline__ uint32_t mul_lo(uint32_t x, uint32_t y) {
 __device__ __forceinline__ uint32_t mul_hi(uint32_t x, uint32_t y) {
     uint32_t r;
     asm("mul.hi.u32 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(y));
+    return r;
+}
+__device__ __forceinline__ uint32_t mad_hi(uint32_t x, uint32_t y, uint32_t z) {
+    uint32_t r;
+    asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(y), "r"(z));
     return r;
 }
 
@@ -715,6 +723,155 @@ __global__ void __launch_bounds__(kDecodeMaxWarps * 32, 1) decode_kernel(const D
 
 // ----------------------------------------------------------------- fused
 
+// Slab ring of the fused kernel.  Each half-warp (16 streams of one input)
+// keeps a ring of R slab rows of its 16 stream columns (64 bytes per row) in
+// shared memory; row r sits in ring row r mod R.  The warp fills it with
+// 16-byte cp.async copies: lane li of half h copies bytes 16 (li % 4) ..
+// of row fill - li / 4 of its half's block, so one instruction moves four
+// rows of both halves' rings.  A fill never overwrites a row that any lane of
+// the half may still read (rows above the slowest lane's next row minus R,
+// with one row of margin for a refill load still in flight).  After the copy
+// groups one fill old have landed (cp.async.wait_group 1, then __syncwarp so
+// that every lane sees the copies of the others), a tile may refill from the
+// ring if every row its lanes can reach is at or above that older fill
+// frontier; otherwise it waits for the newest group too, and if even that
+// does not cover it, it refills from global memory, which is always exact.
+constexpr int kPairFillRows = 4;  // rows per half filled by one copy instruction
+
+struct PairRing {
+    int32_t fill;    // next row to fill (< 0: every row is filled)
+    int32_t done0;   // lowest filled row including the newest group (INT_MIN: all rows)
+    int32_t done1;   // ... excluding it (complete once wait_group 1 returns)
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool pred) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t"
+        "@p cp.async.cg.shared.global [%0], [%1], 16;\n\t}" ::"r"(dst),
+        "l"(src), "r"((uint32_t)pred)
+        : "memory");
+}
+
+// Copy rows fill - li/4 (li = lane % 16) of this half that lie above `lim`
+// and at or above row 0; returns the new fill row.  `src` is this lane's
+// 16-byte piece of row 0 of its half's block (rows 512 bytes apart) and
+// `dst` its piece of ring row 0; ring row of row r: mul.hi(64 r * q.ru, q.rq).
+__device__ __forceinline__ int32_t ring_fill16(int32_t fill, int32_t lim, bool on, int li,
+                                               const uint8_t *src, uint32_t dst, const Opq &q) {
+    const int32_t r = fill - (li >> 2);
+    const bool go = on && r > lim && r >= 0;
+    cp_async16(mad_hi((uint32_t)(r * 64) * q.ru, q.rq, dst), src + (int64_t)r * 512, go);
+    return on ? min(fill, max(fill - kPairFillRows, max(lim, -1))) : fill;
+}
+
+// Two tANS steps with one slab-exhaustion test.  Two steps consume at most 24
+// bits and the window w (bits cnt .. cnt + 31 of hi:lo) holds them all, so the
+// second step reads w << nb1; cnt < 32 before and < 56 after, so at most one
+// slab is exhausted and one refill (hi <- lo, lo <- next row) follows.  Here v
+// counts rows in units of 64 (row r: v = 64 r), matching 64-byte ring rows.
+// Shifts, adds and moves are multiplies by the opaque constants of Opq so
+// that they run on the FMA pipe; the funnel shifts and the slab test stay on
+// the ALU.
+#define TANS_STEP2_FIRST                                                                  \
+    asm("{\n\t.reg .u32 b, f;\n\t"                                                        \
+        "shf.l.wrap.b32 %0, %3, %4, %5;\n\t" /* w = top 32 bits of (hi:lo) << cnt */      \
+        "shf.l.wrap.b32 b, %0, 0, %2;\n\t"   /* bits1 = w >> (32 - nb1), 0 if nb1 = 0 */ \
+        "mul.hi.u32 f, %2, %6;\n\t"          /* e1 >> 16 */                               \
+        "mad.lo.u32 %1, b, %7, f;\n\t}"      /* entry of step 2 */                        \
+        : "=r"(w), "=r"(a1)                                                               \
+        : "r"(e1), "r"(ch.lo), "r"(ch.hi), "r"(ch.cnt), "r"(q.p16), "r"(q.step))
+
+#define TANS_STEP2_HEAD                                                            \
+    "shf.l.wrap.b32 w2, 0, %6, %5;\n\t" /* w << nb1 */                             \
+    "shf.l.wrap.b32 b, w2, 0, %7;\n\t"  /* bits2 */                                \
+    "mul.hi.u32 f, %7, %9;\n\t"                                                    \
+    "mad.lo.u32 %0, b, %10, f;\n\t"     /* next entry */                           \
+    "mad.lo.u32 c, %5, %8, %1;\n\t"     /* cnt + e1 + e2: bit 5 flips per slab */ \
+    "mad.lo.u32 c, %7, %8, c;\n\t"                                                 \
+    "xor.b32 t, c, %1;\n\t"                                                        \
+    "and.b32 t, t, 32;\n\t"                                                        \
+    "setp.ne.u32 pa, t, 0;\n\t"                                                    \
+    "mov.u32 %1, c;\n\t"
+
+// Refill from this half-warp's bulk ring.  The ring row of row r = v / 64 is
+// (r mod R) * 64 = mul.hi(v * 2^(26 - lg R), 2^(lg R + 6)) (q.ru, q.rq): two
+// multiplies on the FMA pipe instead of a mask on the ALU.
+__device__ __forceinline__ void chain_step2_ring(Chain &ch, const uint8_t *tb, uint32_t ring_lane,
+                                                 const Opq &q, uint32_t &e1, uint32_t &e2) {
+    e1 = *reinterpret_cast<const uint32_t *>(tb + ch.addr);
+    uint32_t w, a1;
+    TANS_STEP2_FIRST;
+    e2 = *reinterpret_cast<const uint32_t *>(tb + a1);
+    asm volatile(
+        "{\n\t.reg .u32 w2, b, f, c, t, u, sa;\n\t.reg .pred pa;\n\t" TANS_STEP2_HEAD
+        "mul.lo.u32 u, %4, %12;\n\t"
+        "mad.hi.u32 sa, u, %13, %14;\n\t"
+        "@pa mad.lo.u32 %2, %3, %8, 0;\n\t"    /* hi <- lo */
+        "@pa ld.shared.u32 %3, [sa];\n\t"      /* lo <- next row of this stream */
+        "@pa mad.lo.s32 %4, %8, %11, %4;\n\t"  /* one row down */
+        "}"
+        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.v)
+        : "r"(e1), "r"(w), "r"(e2), "r"(q.one), "r"(q.p16), "r"(q.step), "r"(q.back64),
+          "r"(q.ru), "r"(q.rq), "r"(ring_lane));
+}
+
+// Refill from global memory (any row, any time); past the block's first row
+// nothing is loaded and lo keeps a stale word whose bits are never consumed.
+__device__ __forceinline__ void chain_step2_global(Chain &ch, const uint8_t *tb, const Opq &q,
+                                                   uint32_t &e1, uint32_t &e2) {
+    e1 = *reinterpret_cast<const uint32_t *>(tb + ch.addr);
+    uint32_t w, a1;
+    TANS_STEP2_FIRST;
+    e2 = *reinterpret_cast<const uint32_t *>(tb + a1);
+    asm volatile(
+        "{\n\t.reg .u32 w2, b, f, c, t;\n\t.reg .pred pa, pl;\n\t.reg .u64 ga;\n\t" TANS_STEP2_HEAD
+        "setp.ge.and.s32 pl, %4, 0, pa;\n\t"
+        "mul.wide.s32 ga, %4, 8;\n\t"
+        "add.u64 ga, ga, %12;\n\t"
+        "@pa mad.lo.u32 %2, %3, %8, 0;\n\t"    /* hi <- lo */
+        "@pl ld.global.nc.u32 %3, [ga];\n\t"   /* lo <- next row of this stream */
+        "@pa mad.lo.s32 %4, %8, %11, %4;\n\t"  /* one row down */
+        "}"
+        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.v)
+        : "r"(e1), "r"(w), "r"(e2), "r"(q.one), "r"(q.p16), "r"(q.step), "r"(q.back64),
+          "l"(ch.src));
+}
+
+// NP pair steps (NP % 4 == 0), pair symbols packed four to a word.
+template <bool kRing, int NP>
+__device__ __forceinline__ void chain_tile(Chain &ch, const uint8_t *tb, uint32_t ring_lane,
+                                           const Opq &q, uint32_t (&S)[NP / 4]) {
+#pragma unroll
+    for (int j = 0; j < NP / 4; j++) {
+        uint32_t e0, e1, e2, e3;
+        if (kRing) {
+            chain_step2_ring(ch, tb, ring_lane, q, e0, e1);
+            chain_step2_ring(ch, tb, ring_lane, q, e2, e3);
+        } else {
+            chain_step2_global(ch, tb, q, e0, e1);
+            chain_step2_global(ch, tb, q, e2, e3);
+        }
+        S[j] = gather_syms(e0, e1, e2, e3);
+    }
+}
+
+// init_tans_ctx (csrc/tans_decode.cu:65-92) for 64-unit rows, with in-kernel
+// validation.  Returns the block's slab count G (0 if the metadata is
+// malformed) and in row0 the tensor row of the block's row 0 (-1 when the
+// block does not start on a 512-byte row of the buffer).
+__device__ __forceinline__ int32_t chain_init64(Chain &ch, const uint32_t *__restrict__ comp,
+                                                int64_t comp_bytes,
+                                                const int32_t *__restrict__ offsets,
+                                                const uint16_t *__restrict__ states,
+                                                const uint8_t *__restrict__ partial, int64_t sid,
+                                                uint32_t lane_off, int32_t *status, int32_t &row0) {
+    const int32_t G = chain_init(ch, comp, comp_bytes, offsets, states, partial, sid, lane_off, status);
+    const int64_t base = __ldg(offsets + sid / kBlk);
+    row0 = (G > 0 && base % 512 == 0) ? (int32_t)(base / 512) : -1;
+    ch.v = (G - 3) * 64;
+    return G;
+}
+
 struct FusedArgs {
     const uint32_t *a_comp, *b_comp;
     int64_t a_bytes, b_bytes;
@@ -726,213 +883,210 @@ struct FusedArgs {
     uint8_t *out;                // [N/16][K][16]
     int64_t K, N;                // K: chains decoded (pointers start at the first one)
     int64_t stride;              // streams of the layout: row stride of the sm/out tiles
-    int64_t seg_tiles;           // tiles per chain: N/16, or S/8 for split streams
+    int64_t seg_tiles;           // 8-pair tiles per chain: N/16, or S/8 for split streams
     int32_t *status;
     Opq q;
 };
 
-// Fused kernel, split form: each 32-stream group is handled by a pair of
-// warps, one decoding input A and one input B (one tANS chain per lane each),
-// so the SM holds twice as many warps for the same streams.  Per 8-pair tile
-// the two warps swap packed pair symbols through a small double-buffered
-// shared-memory slot (one 64-thread named barrier per tile); the A warp then
-// composes, adds and stores pairs 0-3 of the tile, the B warp pairs 4-7.
-constexpr int kSplitMaxPairs = 15;  // named barriers 1..15
+// Fused kernel, paired-lane form.  A warp owns 16 streams: lane l < 16
+// decodes stream l of input A, lane l + 16 the same stream of input B (one
+// tANS chain per lane), so 28 warps per SM keep all four schedulers equally
+// loaded.  Per 16-pair tile the two halves swap the packed pair symbols they
+// do not keep with two shuffles; lane half h then composes, adds and stores
+// the 8-pair output tile 2T + h of its stream with one 16-byte store (a warp
+// writes two contiguous 256-byte runs), loading the sign/mantissa bytes of
+// both inputs for that tile itself.  Slab rows come from a ring per
+// half-warp (see PairRing).
+constexpr int kPairMaxWarps = 28;
 
-__device__ __forceinline__ bool block_ok(const int32_t *__restrict__ offsets, int64_t comp_bytes,
-                                         int64_t sid) {
-    const int64_t b = sid / kBlk;
-    const int64_t base = __ldg(offsets + b), next = __ldg(offsets + b + 1);
-    return base >= 0 && next > base && next <= comp_bytes && ((next - base) % 512) == 0 &&
-           (base % 4) == 0;
+// Row of a 64-unit v, on the FMA pipe (arithmetic: rows below 0 stay negative).
+__device__ __forceinline__ int32_t row_of(int32_t v, const Opq &q) {
+    int32_t r;
+    asm("mul.hi.s32 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(q.p26));
+    return r;
 }
 
-// Two predicated 4-byte copies (rows r and r-1 of this lane's column) into
-// the row ring; the predicates are formed in PTX from the warp-uniform count.
-__device__ __forceinline__ void ring_copy2(uint32_t dst0, uint32_t dst1, const uint32_t *src0,
-                                           int32_t n, bool live) {
-    asm volatile(
-        "{\n\t.reg .pred p0, p1, lv;\n\t"
-        "setp.ne.u32 lv, %5, 0;\n\t"
-        "setp.gt.and.s32 p0, %4, 0, lv;\n\t"
-        "setp.gt.and.s32 p1, %4, 1, lv;\n\t"
-        "@p0 cp.async.ca.shared.global [%0], [%2], 4;\n\t"
-        "@p1 cp.async.ca.shared.global [%1], [%3], 4;\n\t}" ::"r"(dst0),
-        "r"(dst1), "l"(src0), "l"(src0 - kBlk), "r"(n), "r"((uint32_t)live)
-        : "memory");
+// Per-tile ring upkeep: fill up to four rows of each half's ring, then vote
+// on whether every lane's rows for this tile (down to row - 5: 16 steps read
+// at most 6 slabs) are in landed fills.
+template <int R, bool kAll>
+__device__ __forceinline__ bool ring_tile(PairRing &rg, int32_t row, bool live, bool on, int h,
+                                          int li, const uint8_t *src, uint32_t dst, const Opq &q) {
+    const uint32_t full = 0xffffffffu;
+    const int32_t sa = __reduce_max_sync(full, (h == 0 && (kAll || live)) ? row : kNoRow);
+    const int32_t sb = __reduce_max_sync(full, (h == 1 && (kAll || live)) ? row : kNoRow);
+    const int32_t f = ring_fill16(rg.fill, (h ? sb : sa) - R + 1, on, li, src, dst, q);
+    cp_async_commit();
+    rg.done1 = rg.done0;
+    rg.done0 = f < 0 ? INT_MIN : (f < rg.fill ? f + 1 : rg.done0);
+    rg.fill = f;
+    cp_async_wait<1>();
+    __syncwarp();
+    if (__all_sync(full, (!kAll && !live) || row - 5 >= rg.done1)) return true;
+    cp_async_wait<0>();
+    __syncwarp();
+    return __all_sync(full, (!kAll && !live) || row - 5 >= rg.done0);
 }
 
-// Four predicated 4-byte copies (rows r .. r-3 of this lane's column).
-__device__ __forceinline__ void ring_copy4(uint32_t base, uint32_t f, uint32_t wrap,
-                                           const uint32_t *src0, int32_t n, bool live) {
-    asm volatile(
-        "{\n\t.reg .pred p0, p1, p2, p3, lv;\n\t.reg .u32 d;\n\t"
-        "setp.ne.u32 lv, %4, 0;\n\t"
-        "setp.gt.and.s32 p0, %3, 0, lv;\n\t"
-        "setp.gt.and.s32 p1, %3, 1, lv;\n\t"
-        "setp.gt.and.s32 p2, %3, 2, lv;\n\t"
-        "setp.gt.and.s32 p3, %3, 3, lv;\n\t"
-        "and.b32 d, %1, %2;\n\t"
-        "shl.b32 d, d, 7;\n\t"
-        "add.u32 d, d, %0;\n\t"
-        "@p0 cp.async.ca.shared.global [d], [%5], 4;\n\t"
-        "sub.u32 d, %1, 1;\n\t"
-        "and.b32 d, d, %2;\n\t"
-        "shl.b32 d, d, 7;\n\t"
-        "add.u32 d, d, %0;\n\t"
-        "@p1 cp.async.ca.shared.global [d], [%6], 4;\n\t"
-        "sub.u32 d, %1, 2;\n\t"
-        "and.b32 d, d, %2;\n\t"
-        "shl.b32 d, d, 7;\n\t"
-        "add.u32 d, d, %0;\n\t"
-        "@p2 cp.async.ca.shared.global [d], [%7], 4;\n\t"
-        "sub.u32 d, %1, 3;\n\t"
-        "and.b32 d, d, %2;\n\t"
-        "shl.b32 d, d, 7;\n\t"
-        "add.u32 d, d, %0;\n\t"
-        "@p3 cp.async.ca.shared.global [d], [%8], 4;\n\t}" ::"r"(base),
-        "r"(f), "r"(wrap), "r"(n), "r"((uint32_t)live), "l"(src0), "l"(src0 - kBlk),
-        "l"(src0 - 2 * kBlk), "l"(src0 - 3 * kBlk)
-        : "memory");
+// The 16-pair tiles (and a last 8-pair tile) of one group.  kAll: every lane
+// has a live stream (no masking of loads, outputs or votes).
+template <int R, bool kAll>
+__device__ __forceinline__ void pair_group(const FusedArgs &p, Chain &ch, PairRing &rg,
+                                           const uint8_t *tb, uint32_t ring_lane, bool on, int li,
+                                           const uint8_t *fsrc, uint32_t fdst, bool live,
+                                           bool active, int h, const uint8_t *so,
+                                           const uint8_t *sx, uint8_t *op, int64_t tail) {
+    const uint32_t full = 0xffffffffu;
+    const int32_t n8 = (int32_t)p.seg_tiles, n16 = n8 / 2;
+    const int64_t t8 = p.stride * 8, o8 = p.stride * 16;
+    uint2 mo_n = make_uint2(0, 0), mx_n = make_uint2(0, 0);
+    if ((kAll || live) && n16 > 0) {
+        mo_n = ld_stream_v2(so);
+        mx_n = ld_stream_v2(sx);
+    }
+    for (int32_t t = 0; t < n16; t++) {
+        const uint2 mo = mo_n, mx = mx_n;
+        so += 2 * t8;
+        sx += 2 * t8;
+        if ((kAll || live) && t + 1 < n16) {
+            mo_n = ld_stream_v2(so);
+            mx_n = ld_stream_v2(sx);
+        }
+        if ((kAll || live) && t + 3 < n16) {
+            prefetch_l2(so + 4 * t8);
+            prefetch_l2(sx + 4 * t8);
+        }
+        uint32_t S[4];
+        if (ring_tile<R, kAll>(rg, row_of(ch.v, p.q), live, on, h, li, fsrc, fdst, p.q))
+            chain_tile<true, 16>(ch, tb, ring_lane, p.q, S);
+        else
+            chain_tile<false, 16>(ch, tb, ring_lane, p.q, S);
+        // half h keeps pairs 8h .. 8h + 7 and sends the other eight
+        const uint32_t k0 = h ? S[2] : S[0], k1 = h ? S[3] : S[1];
+        const uint32_t x0 = __shfl_xor_sync(full, h ? S[0] : S[2], 16);
+        const uint32_t x1 = __shfl_xor_sync(full, h ? S[1] : S[3], 16);
+        const uint32_t re0 = add_e4m3x4(compose_even(k0, mo.x, p.q), compose_even(x0, mx.x, p.q));
+        const uint32_t ro0 = add_e4m3x4(compose_odd(k0, mo.x, p.q), compose_odd(x0, mx.x, p.q));
+        const uint32_t re1 = add_e4m3x4(compose_even(k1, mo.y, p.q), compose_even(x1, mx.y, p.q));
+        const uint32_t ro1 = add_e4m3x4(compose_odd(k1, mo.y, p.q), compose_odd(x1, mx.y, p.q));
+        uint4 o = make_uint4(__byte_perm(re0, ro0, 0x5140), __byte_perm(re0, ro0, 0x7362),
+                             __byte_perm(re1, ro1, 0x5140), __byte_perm(re1, ro1, 0x7362));
+        if (!kAll && !live) o = make_uint4(0, 0, 0, 0);
+        if (kAll || active) st_stream_v4(op, o);
+        op += 2 * o8;
+    }
+    if (n8 & 1) {
+        // a last 8-pair tile (element tile `tail` of this stream): half h
+        // composes pairs 4h .. 4h + 3 (8 output bytes)
+        uint32_t S[2];
+        if (ring_tile<R, kAll>(rg, row_of(ch.v, p.q), live, on, h, li, fsrc, fdst, p.q))
+            chain_tile<true, 8>(ch, tb, ring_lane, p.q, S);
+        else
+            chain_tile<false, 8>(ch, tb, ring_lane, p.q, S);
+        const uint32_t k0 = h ? S[1] : S[0];
+        const uint32_t x0 = __shfl_xor_sync(full, h ? S[0] : S[1], 16);
+        const uint8_t *own = h ? p.b_sm : p.a_sm, *oth = h ? p.a_sm : p.b_sm;
+        uint32_t mo = 0, mx = 0;
+        if (kAll || live) {
+            mo = ld_stream_u32(own + tail * 8 + 4 * h);
+            mx = ld_stream_u32(oth + tail * 8 + 4 * h);
+        }
+        const uint32_t re = add_e4m3x4(compose_even(k0, mo, p.q), compose_even(x0, mx, p.q));
+        const uint32_t ro = add_e4m3x4(compose_odd(k0, mo, p.q), compose_odd(x0, mx, p.q));
+        uint32_t ox = __byte_perm(re, ro, 0x5140), oy = __byte_perm(re, ro, 0x7362);
+        if (!kAll && !live) ox = oy = 0;
+        if (kAll || active) st_stream_v2(p.out + tail * 16 + 8 * h, ox, oy);
+    }
 }
-
-// Warp vote: may every lane refill from the ring for the next tile?  Each
-// row a lane can reach in one tile (at most 3 refills: rows row .. row - 2)
-// must belong to a fill group that cp.async.wait_group has completed
-// (frontier done[kLag]).
-template <int kLag>
-__device__ __forceinline__ bool ring_vote(const Ring &rg, const Chain &ch, bool live) {
-    static_assert(kLag >= 1 && kLag <= kRingLag, "lag beyond the recorded fill frontiers");
-    const int32_t row = ch.v >> 7;
-    return __all_sync(0xffffffffu, !live || max(row - 2, 0) >= rg.done[kLag]);
-}
-
-// Ring fill for a warp with one chain: up to kMaxRows rows (never over a
-// slot the slowest lane still needs); shifts the frontier history.  The
-// caller commits the group.
-template <int R, int kMaxRows>
-__device__ __forceinline__ void ring_refill(Ring &rg, const Chain &ch, bool live) {
-    static_assert(kMaxRows == 2 || kMaxRows == 4, "two or four row copies per fill");
-    const int32_t row = ch.v >> 7;
-    const int32_t r_slow = __reduce_max_sync(0xffffffffu, live ? row : kNoRow);
-    int32_t n = min(rg.fill + 1, rg.fill - (r_slow - R));
-    n = max(min(n, kMaxRows), 0);
-    const uint32_t f = (uint32_t)rg.fill;
-    if (kMaxRows == 2)
-        ring_copy2(rg.lane_base + ((f & (R - 1)) << 7), rg.lane_base + (((f - 1) & (R - 1)) << 7),
-                   ch.src + (int64_t)rg.fill * kBlk, n, live);
-    else
-        ring_copy4(rg.lane_base, f, R - 1, ch.src + (int64_t)rg.fill * kBlk, n, live);
-    rg.fill -= n;
-#pragma unroll
-    for (int i = kRingLag; i > 0; i--) rg.done[i] = rg.done[i - 1];
-    rg.done[0] = rg.fill + 1;
-}
-
-// Fused kernel ring schedule: a fill of up to kRingPerTile rows per tile
-// every kFusedFillTiles tiles, and the fast/slow vote every tile against
-// the frontier of the fill kFusedLag fills back (cp.async.wait_group depth).
-constexpr int kFusedFillTiles = 2;
-constexpr int kFusedLag = 1;
 
 template <int R>
-__global__ void __launch_bounds__(kSplitMaxPairs * 64, 1) fused_split_kernel(const FusedArgs p) {
+__global__ void __launch_bounds__(kPairMaxWarps * 32, 1)
+    fused_pair_kernel(const __grid_constant__ FusedArgs p) {
+    static_assert(R >= 16 && (R & (R - 1)) == 0, "ring rows: a power of two");
     extern __shared__ __align__(16) uint8_t smem[];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+    const int h = lane >> 4, li = lane & 15;
+    const uint32_t rbytes = R * 64u;
+    const uint32_t rings = (smem_addr(smem) + kTableBytes + rbytes - 1) & ~(rbytes - 1);
+    const uint32_t ring_h = rings + (uint32_t)(2 * warp + h) * rbytes;  // this half's ring
     load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
     __syncthreads();
     const uint8_t *tb = smem;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int pair = warp >> 1, side = warp & 1;  // side 0 decodes A, side 1 decodes B
-    const int pairs = blockDim.x >> 6;
     const uint32_t lane_off = 4u * (lane % kCopies);
-    const uint32_t mask = (uint32_t)(R - 1) << 7;
-    // exchange slots: [buffer][sender side][lane] x (pair symbols, sm half)
-    uint2 *xch = reinterpret_cast<uint2 *>(smem + kTableBytes) + pair * 128;
-    Ring rg;
-    {
-        const uint32_t bytes = R * 128u;
-        const uint32_t first =
-            (smem_addr(smem) + kTableBytes + (uint32_t)pairs * 1024u + bytes - 1) & ~(bytes - 1);
-        rg.lane_base = first + (uint32_t)warp * bytes + 4u * lane;
-    }
-    const uint32_t *comp = side ? p.b_comp : p.a_comp;
-    const int64_t comp_bytes = side ? p.b_bytes : p.a_bytes;
-    const int32_t *off = side ? p.b_off : p.a_off;
-    const uint16_t *st = side ? p.b_st : p.a_st;
-    const uint8_t *part = side ? p.b_part : p.a_part;
-    const uint8_t *smv = side ? p.b_sm : p.a_sm;
-    const int64_t n_groups = (p.K + 31) / 32;
-    const int32_t n_tiles = (int32_t)p.seg_tiles;
-    const int64_t K = p.K, tstep = p.stride * 8, ostep = p.stride * 16;
-    uint2 *my_slot = xch + side * 32 + lane, *their_slot = xch + (side ^ 1) * 32 + lane;
-    for (int64_t g = (int64_t)blockIdx.x * pairs + pair; g < n_groups;
-         g += (int64_t)gridDim.x * pairs) {
-        const int64_t sid = g * 32 + lane;
+    const uint32_t ring_lane = ring_h + 4u * li;                // this lane's column: reads
+    const uint32_t fdst = ring_h + 16u * (li & 3);              // this lane's fill piece
+    const uint32_t *comp = h ? p.b_comp : p.a_comp;
+    const int64_t comp_bytes = h ? p.b_bytes : p.a_bytes;
+    const int32_t *off = h ? p.b_off : p.a_off;
+    const uint16_t *st = h ? p.b_st : p.a_st;
+    const uint8_t *part = h ? p.b_part : p.a_part;
+    // sign/mantissa bytes of this lane's own input and of the other input
+    const uint8_t *sm_own = h ? p.b_sm : p.a_sm, *sm_oth = h ? p.a_sm : p.b_sm;
+    const int32_t *off_oth = h ? p.a_off : p.b_off;
+    const int64_t bytes_oth = h ? p.a_bytes : p.b_bytes;
+    const int64_t n_groups = (p.K + 15) / 16;
+    const int64_t K = p.K, t8 = p.stride * 8, o8 = p.stride * 16;
+    const uint32_t full = 0xffffffffu;
+    for (int64_t g = (int64_t)blockIdx.x * warps + warp; g < n_groups; g += (int64_t)gridDim.x * warps) {
+        const int64_t sid = g * 16 + li;
         const bool active = sid < K;
         Chain ch;
         chain_idle(ch, comp);
-        int32_t G = 0;
+        int32_t G = 0, row0 = -1;
         bool ok = false;
         if (active) {
-            G = chain_init(ch, comp, comp_bytes, off, st, part, sid, lane_off, p.status);
-            ok = block_ok(p.a_off, p.a_bytes, sid) && block_ok(p.b_off, p.b_bytes, sid);
+            G = chain_init64(ch, comp, comp_bytes, off, st, part, sid, lane_off, p.status, row0);
+            // the other input's block must be valid too (its lane reports its
+            // own metadata; this keeps both lanes of a stream in step)
+            const int64_t bb = sid / kBlk;
+            const int64_t ob = __ldg(off_oth + bb), on = __ldg(off_oth + bb + 1);
+            ok = ob >= 0 && on > ob && on <= bytes_oth && ((on - ob) % 512) == 0 && (ob % 4) == 0;
         }
         const bool live = active && ok && G > 0;
-        if (!live) chain_idle(ch, comp);
-        ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, live ? G : 0), live);
-        cp_async_commit();
-        cp_async_wait<0>();
-        // this warp's input: 8 sign/mantissa bytes per tile, loaded a tile
-        // ahead; this side prefetches its own input four tiles ahead
-        // chain sid is segment j of output stream col (split streams: chains
-        // are segment-major, 32 | stride; otherwise j = 0 and col = sid)
-        const int64_t j = (g * 32) / p.stride;
-        const int64_t col = sid - j * p.stride, tile0 = j * p.seg_tiles * p.stride;
-        const uint8_t *sp = smv + (tile0 + col) * 8;
-        uint8_t *op = p.out + (tile0 + col) * 16 + 8 * side;
-        uint2 m_n = make_uint2(0, 0);
-        if (live && n_tiles > 0) m_n = ld_stream_v2(sp);
-        for (int32_t t = 0; t < n_tiles; t++) {
-            const uint2 m = m_n;
-            sp += tstep;
-            if (live && t + 1 < n_tiles) m_n = ld_stream_v2(sp);
-            if (live && t + 4 < n_tiles) prefetch_l2(sp + 3 * tstep);
-            if (t % kFusedFillTiles == 0) {
-                ring_refill<R, kRingPerTile * kFusedFillTiles>(rg, ch, live);
-                cp_async_commit();
-                cp_async_wait<kFusedLag>();
-            }
-            const bool fast = ring_vote<kFusedLag>(rg, ch, live);
-            uint32_t e[kTablePairs];
-            if (fast) {
-#pragma unroll
-                for (int j = 0; j < kTablePairs; j++)
-                    e[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
-            } else {
-#pragma unroll
-                for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_global(ch, tb, p.q);
-            }
-            const uint32_t lo = gather_syms(e[0], e[1], e[2], e[3]);
-            const uint32_t hi = gather_syms(e[4], e[5], e[6], e[7]);
-            // side 0 keeps pairs 0-3 and sends 4-7; side 1 keeps 4-7, sends 0-3
-            const int buf = (t & 1) * 64;
-            my_slot[buf] = side ? make_uint2(lo, m.x) : make_uint2(hi, m.y);
-            asm volatile("bar.sync %0, 64;" ::"r"(1 + pair) : "memory");
-            const uint2 o = their_slot[buf];
-            uint32_t SA, SB, MA, MB;
-            if (side) {
-                SA = o.x; MA = o.y; SB = hi; MB = m.y;
-            } else {
-                SA = lo; MA = m.x; SB = o.x; MB = o.y;
-            }
-            const uint32_t re = add_e4m3x4(compose_even(SA, MA, p.q), compose_even(SB, MB, p.q));
-            const uint32_t ro = add_e4m3x4(compose_odd(SA, MA, p.q), compose_odd(SB, MB, p.q));
-            uint32_t ox = __byte_perm(re, ro, 0x5140), oy = __byte_perm(re, ro, 0x7362);
-            if (!live) ox = oy = 0;
-            if (active) st_stream_v2(op, ox, oy);
-            op += ostep;
+        // this half's ring: its block's slab count, and row 0 of the half's
+        // 16 stream columns (the same for every live lane of the half), which
+        // the ring copies 16 bytes at a time when it is 16-byte aligned
+        const uint64_t row0_cols = reinterpret_cast<uint64_t>(ch.src) - 4u * (uint64_t)li;
+        const int32_t ga = __reduce_max_sync(full, (live && !h) ? G : 0);
+        const int32_t gb = __reduce_max_sync(full, (live && h) ? G : 0);
+        const uint32_t hm = (__ballot_sync(full, live && (row0_cols & 15u) == 0) >> (16 * h)) & 0xFFFFu;
+        const int32_t Gh = h ? gb : ga;
+        const bool on = Gh >= 3 && hm != 0;
+        const uint64_t rc = __shfl_sync(full, row0_cols, 16 * h + (hm ? __ffs(hm) - 1 : 0));
+        const uint8_t *fsrc = reinterpret_cast<const uint8_t *>(rc) + 16 * (li & 3);  // unused when !on
+        if (!live) {
+            chain_idle(ch, comp);
+            ch.v = -64;
         }
+        PairRing rg;
+        rg.fill = Gh - 3;
+        rg.done0 = rg.done1 = Gh >= 3 ? Gh - 2 : INT_MIN;
+        if (on) {
+            // the first rows: three fills of four, then wait for all of them
+#pragma unroll
+            for (int k = 0; k < 3; k++) rg.fill = ring_fill16(rg.fill, -1, true, li, fsrc, fdst, p.q);
+            cp_async_commit();
+            cp_async_wait<0>();
+            rg.done0 = rg.done1 = rg.fill < 0 ? INT_MIN : rg.fill + 1;
+        }
+        __syncwarp();
+        // chain sid is segment j of output stream col (split streams: chains
+        // are segment-major, 16 | stride; otherwise j = 0 and col = sid)
+        const int64_t j = (g * 16) / p.stride;
+        const int64_t col = sid - j * p.stride, tile0 = j * p.seg_tiles * p.stride;
+        const uint8_t *so = sm_own + (tile0 + col) * 8 + h * t8;
+        const uint8_t *sx = sm_oth + (tile0 + col) * 8 + h * t8;
+        uint8_t *op = p.out + (tile0 + col) * 16 + h * o8;
+        const int64_t tail = tile0 + (p.seg_tiles - 1) * p.stride + col;
+        if (__all_sync(full, live))
+            pair_group<R, true>(p, ch, rg, tb, ring_lane, on, li, fsrc, fdst, live, active, h, so,
+                                sx, op, tail);
+        else
+            pair_group<R, false>(p, ch, rg, tb, ring_lane, on, li, fsrc, fdst, live, active, h, so,
+                                 sx, op, tail);
+        // every copy lands before the ring is reused
         cp_async_wait<0>();
+        __syncwarp();
     }
 }
 
@@ -1766,6 +1920,9 @@ Opq make_opq() {
     q.x8 = 8;
     q.step = 4 * kCopies;
     q.back = -kBlk;
+    q.back64 = -64;
+    q.p26 = 1u << 26;
+    q.ru = q.rq = 0;
     return q;
 }
 
@@ -1778,26 +1935,54 @@ int stream_grid(int64_t n_vec, int sms) {
 
 }  // namespace
 
-template <int R>
-int launch_fused_split(const FusedArgs &args, int64_t n_streams, int sms, cudaStream_t stream) {
-    const int per_pair = 2 * R * 128 + 1024;
-    int max_p = (kSmemMax - kTableBytes - R * 128) / per_pair;
-    if (max_p > kSplitMaxPairs) max_p = kSplitMaxPairs;
-    const Geometry geo = balance((n_streams + 31) / 32, sms, max_p);
-    const int smem = kTableBytes + R * 128 + geo.warps_per_cta * per_pair;
-    int rc = set_smem(fused_split_kernel<R>, smem);
-    if (rc) return rc;
-    fused_split_kernel<R><<<geo.grid, geo.warps_per_cta * 64, smem, stream>>>(args);
-    return launch_status("fused_split_kernel");
+// cuTensorMapEncodeTiled, resolved through the runtime so that the library
+// needs no link against the driver library.
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_tiled_fn(EncodeTiledFn *fn) {
+    static EncodeTiledFn cached = nullptr;
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!cached) {
+        void *f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000,
+                                                         cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !f)
+            return fail(TANS_B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable: %s",
+                        cudaGetErrorString(e));
+        cached = reinterpret_cast<EncodeTiledFn>(f);
+    }
+    *fn = cached;
+    return TANS_B200_OK;
 }
 
-static int launch_fused(const FusedArgs &args, int64_t chains, int64_t pairs_per_chain, int sms,
-                 cudaStream_t st) {
+template <int R>
+int launch_fused_pair(FusedArgs &args, int64_t chains, int sms, cudaStream_t stream) {
+    const int per_warp = 2 * R * 64;  // two rings
+    int max_w = (kSmemMax - kTableBytes - R * 64) / per_warp;
+    if (max_w > kPairMaxWarps) max_w = kPairMaxWarps;
+    const Geometry geo = balance((chains + 15) / 16, sms, max_w);
+    const int smem = kTableBytes + R * 64 + geo.warps_per_cta * per_warp;
+    int lg = 0;
+    while ((1 << lg) < R) lg++;
+    args.q.ru = 1u << (26 - lg);
+    args.q.rq = 1u << (lg + 6);
+    int rc = set_smem(fused_pair_kernel<R>, smem);
+    if (rc) return rc;
+    fused_pair_kernel<R><<<geo.grid, geo.warps_per_cta * 32, smem, stream>>>(args);
+    return launch_status("fused_pair_kernel");
+}
+
+static int launch_fused(FusedArgs &args, int64_t chains, int64_t pairs_per_chain, int sms,
+                        cudaStream_t st) {
     switch (ring_rows(pairs_per_chain)) {
-        case 16: return launch_fused_split<16>(args, chains, sms, st);
-        case 32: return launch_fused_split<32>(args, chains, sms, st);
-        case 64: return launch_fused_split<64>(args, chains, sms, st);
-        default: return launch_fused_split<128>(args, chains, sms, st);
+        case 16: return launch_fused_pair<16>(args, chains, sms, st);
+        case 32: return launch_fused_pair<32>(args, chains, sms, st);
+        case 64: return launch_fused_pair<64>(args, chains, sms, st);
+        default: return launch_fused_pair<128>(args, chains, sms, st);
     }
 }
 
@@ -1986,12 +2171,27 @@ extern "C" int tans_b200_fp8_vecadd_fused_range(
     // a range is the full layout seen from its first stream: per-stream and
     // per-block arrays start there, tiles keep the full row stride
     const int64_t s0 = stream_begin, b0 = stream_begin / kBlk;
-    FusedArgs args{reinterpret_cast<const uint32_t *>(a_compressed),
-                   reinterpret_cast<const uint32_t *>(b_compressed),
-                   a_compressed_bytes, b_compressed_bytes, a_offsets + b0, b_offsets + b0,
-                   a_states + s0, b_states + s0, a_partial + s0, b_partial + s0, a_sm + 8 * s0,
-                   b_sm + 8 * s0, decode_table, out + 16 * s0, stream_end - stream_begin,
-                   n_fp8_per_stream, n_streams, n_fp8_per_stream / 16, status, make_opq()};
+    FusedArgs args{};
+    args.a_comp = reinterpret_cast<const uint32_t *>(a_compressed);
+    args.b_comp = reinterpret_cast<const uint32_t *>(b_compressed);
+    args.a_bytes = a_compressed_bytes;
+    args.b_bytes = b_compressed_bytes;
+    args.a_off = a_offsets + b0;
+    args.b_off = b_offsets + b0;
+    args.a_st = a_states + s0;
+    args.b_st = b_states + s0;
+    args.a_part = a_partial + s0;
+    args.b_part = b_partial + s0;
+    args.a_sm = a_sm + 8 * s0;
+    args.b_sm = b_sm + 8 * s0;
+    args.table = decode_table;
+    args.out = out + 16 * s0;
+    args.K = stream_end - stream_begin;
+    args.N = n_fp8_per_stream;
+    args.stride = n_streams;
+    args.seg_tiles = n_fp8_per_stream / 16;
+    args.status = status;
+    args.q = make_opq();
     return launch_fused(args, stream_end - stream_begin, n_fp8_per_stream / 2, sms,
                         (cudaStream_t)stream);
 }
@@ -2030,12 +2230,27 @@ extern "C" int tans_b200_fp8_vecadd_fused_split(
     int sms;
     int rc = device_setup(&sms);
     if (rc) return rc;
-    FusedArgs args{reinterpret_cast<const uint32_t *>(a_compressed),
-                   reinterpret_cast<const uint32_t *>(b_compressed),
-                   a_compressed_bytes, b_compressed_bytes, a_offsets, b_offsets, a_states,
-                   b_states, a_partial, b_partial, a_sm, b_sm, decode_table, out,
-                   n_streams * segs, n_fp8_per_stream, n_streams, segment_pairs / kTablePairs,
-                   status, make_opq()};
+    FusedArgs args{};
+    args.a_comp = reinterpret_cast<const uint32_t *>(a_compressed);
+    args.b_comp = reinterpret_cast<const uint32_t *>(b_compressed);
+    args.a_bytes = a_compressed_bytes;
+    args.b_bytes = b_compressed_bytes;
+    args.a_off = a_offsets;
+    args.b_off = b_offsets;
+    args.a_st = a_states;
+    args.b_st = b_states;
+    args.a_part = a_partial;
+    args.b_part = b_partial;
+    args.a_sm = a_sm;
+    args.b_sm = b_sm;
+    args.table = decode_table;
+    args.out = out;
+    args.K = n_streams * segs;
+    args.N = n_fp8_per_stream;
+    args.stride = n_streams;
+    args.seg_tiles = segment_pairs / kTablePairs;
+    args.status = status;
+    args.q = make_opq();
     return launch_fused(args, n_streams * segs, segment_pairs, sms, (cudaStream_t)stream);
 }
 
@@ -2238,30 +2453,6 @@ extern "C" int tans_b200_scale_rows_bf16(const float *acc, const float *scale, u
                              (cudaStream_t)stream>>>(reinterpret_cast<const float4 *>(acc), scale,
                                                      reinterpret_cast<uint2 *>(y), n4, rows / 4);
     return launch_status("scale_rows_bf16_kernel");
-}
-
-// cuTensorMapEncodeTiled, resolved through the runtime so that the library
-// needs no link against the driver library.
-typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
-                                  const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
-                                  const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-int encode_tiled_fn(EncodeTiledFn *fn) {
-    static EncodeTiledFn cached = nullptr;
-    std::lock_guard<std::mutex> lk(g_mu);
-    if (!cached) {
-        void *f = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000,
-                                                         cudaEnableDefault, &q);
-        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !f)
-            return fail(TANS_B200_ERR_CUDA, "cuTensorMapEncodeTiled unavailable: %s",
-                        cudaGetErrorString(e));
-        cached = reinterpret_cast<EncodeTiledFn>(f);
-    }
-    *fn = cached;
-    return TANS_B200_OK;
 }
 
 extern "C" int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_bytes,
