@@ -276,7 +276,7 @@ struct Opq {
     int32_t back;    // -128: one slab row down, in words
     int32_t back64;  // -64: one slab row down in the fused kernel's 64-unit rows
     uint32_t p26;    // 2^26: mul.hi.s32(v, p26) = v >> 6 (row of a 64-unit v)
-    uint32_t ru, rq; // 2^(26 - lg R), 2^(lg R + 6): ring row offset of a 64-unit v (set per launch)
+    uint32_t rmask;  // (R - 1) * 64: ring row offset of a 64-unit v (set per launch)
 };
 
 __device__ __forceinline__ uint32_t mul_lo(uint32_t x, uint32_t y) {
@@ -287,11 +287,6 @@ __device__ __forceinline__ uint32_t mul_lo(uint32_t x, uint32_t y) {
 __device__ __forceinline__ uint32_t mul_hi(uint32_t x, uint32_t y) {
     uint32_t r;
     asm("mul.hi.u32 %0, %1, %2;" : "=r"(r) : "r"(x), "r"(y));
-    return r;
-}
-__device__ __forceinline__ uint32_t mad_hi(uint32_t x, uint32_t y, uint32_t z) {
-    uint32_t r;
-    asm("mad.hi.u32 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(y), "r"(z));
     return r;
 }
 
@@ -497,12 +492,20 @@ __device__ __forceinline__ uint32_t gather_syms(uint32_t e0, uint32_t e1, uint32
 // even: byte k = element 2k; odd: byte k = element 2k+1.
 // Byte = (sm & 8) << 4 | exp << 3 | (sm & 7)  (csrc/vecadd.cu:37-39).
 // Shifts go through the FMA pipe (see Opq).
+// Each is two bitwise selects (lop3 (a & m) | (b & ~m), LUT 0xE4) of the
+// shifted operands: the sign bit from one, the mantissa bits from another,
+// the exponent bits from the third.
 __device__ __forceinline__ uint32_t compose_even(uint32_t S, uint32_t M, const Opq &q) {
-    return (mul_lo(M, q.x16) & 0x80808080u) | (mul_hi(S, q.p31) & 0x78787878u) |
-           (M & 0x07070707u);
+    uint32_t t, r;
+    asm("lop3.b32 %0, %1, %2, 0x80808080, 0xE4;" : "=r"(t) : "r"(mul_lo(M, q.x16)), "r"(mul_hi(S, q.p31)));
+    asm("lop3.b32 %0, %1, %2, 0x07070707, 0xE4;" : "=r"(r) : "r"(M), "r"(t));
+    return r;
 }
 __device__ __forceinline__ uint32_t compose_odd(uint32_t S, uint32_t M, const Opq &q) {
-    return (M & 0x80808080u) | (mul_lo(S, q.x8) & 0x78787878u) | (mul_hi(M, q.p28) & 0x07070707u);
+    uint32_t t, r;
+    asm("lop3.b32 %0, %1, %2, 0x80808080, 0xE4;" : "=r"(t) : "r"(M), "r"(mul_lo(S, q.x8)));
+    asm("lop3.b32 %0, %1, %2, 0x07070707, 0xE4;" : "=r"(r) : "r"(mul_hi(M, q.p28)), "r"(t));
+    return r;
 }
 
 // Persistent-grid geometry: every warp runs `rounds` 32-stream groups.
@@ -755,12 +758,12 @@ __device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool p
 // Copy rows fill - li/4 (li = lane % 16) of this half that lie above `lim`
 // and at or above row 0; returns the new fill row.  `src` is this lane's
 // 16-byte piece of row 0 of its half's block (rows 512 bytes apart) and
-// `dst` its piece of ring row 0; ring row of row r: mul.hi(64 r * q.ru, q.rq).
+// `dst` its piece of ring row 0; ring row of row r at (64 r) & q.rmask.
 __device__ __forceinline__ int32_t ring_fill16(int32_t fill, int32_t lim, bool on, int li,
                                                const uint8_t *src, uint32_t dst, const Opq &q) {
     const int32_t r = fill - (li >> 2);
     const bool go = on && r > lim && r >= 0;
-    cp_async16(mad_hi((uint32_t)(r * 64) * q.ru, q.rq, dst), src + (int64_t)r * 512, go);
+    cp_async16(dst | ((uint32_t)(r * 64) & q.rmask), src + (int64_t)r * 512, go);
     return on ? min(fill, max(fill - kPairFillRows, max(lim, -1))) : fill;
 }
 
@@ -793,9 +796,8 @@ __device__ __forceinline__ int32_t ring_fill16(int32_t fill, int32_t lim, bool o
     "setp.ne.u32 pa, t, 0;\n\t"                                                    \
     "mov.u32 %1, c;\n\t"
 
-// Refill from this half-warp's bulk ring.  The ring row of row r = v / 64 is
-// (r mod R) * 64 = mul.hi(v * 2^(26 - lg R), 2^(lg R + 6)) (q.ru, q.rq): two
-// multiplies on the FMA pipe instead of a mask on the ALU.
+// Refill from this half-warp's ring: the ring row of row r = v / 64 is at
+// (v & (R - 1) * 64) | ring_lane (q.rmask; the ring is aligned to its size).
 __device__ __forceinline__ void chain_step2_ring(Chain &ch, const uint8_t *tb, uint32_t ring_lane,
                                                  const Opq &q, uint32_t &e1, uint32_t &e2) {
     e1 = *reinterpret_cast<const uint32_t *>(tb + ch.addr);
@@ -804,15 +806,15 @@ __device__ __forceinline__ void chain_step2_ring(Chain &ch, const uint8_t *tb, u
     e2 = *reinterpret_cast<const uint32_t *>(tb + a1);
     asm volatile(
         "{\n\t.reg .u32 w2, b, f, c, t, u, sa;\n\t.reg .pred pa;\n\t" TANS_STEP2_HEAD
-        "mul.lo.u32 u, %4, %12;\n\t"
-        "mad.hi.u32 sa, u, %13, %14;\n\t"
+        "and.b32 u, %4, %12;\n\t"
+        "or.b32 sa, u, %13;\n\t"
         "@pa mad.lo.u32 %2, %3, %8, 0;\n\t"    /* hi <- lo */
         "@pa ld.shared.u32 %3, [sa];\n\t"      /* lo <- next row of this stream */
         "@pa mad.lo.s32 %4, %8, %11, %4;\n\t"  /* one row down */
         "}"
         : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.v)
         : "r"(e1), "r"(w), "r"(e2), "r"(q.one), "r"(q.p16), "r"(q.step), "r"(q.back64),
-          "r"(q.ru), "r"(q.rq), "r"(ring_lane));
+          "r"(q.rmask), "r"(ring_lane));
 }
 
 // Refill from global memory (any row, any time); past the block's first row
@@ -1922,7 +1924,7 @@ Opq make_opq() {
     q.back = -kBlk;
     q.back64 = -64;
     q.p26 = 1u << 26;
-    q.ru = q.rq = 0;
+    q.rmask = 0;
     return q;
 }
 
@@ -1966,10 +1968,7 @@ int launch_fused_pair(FusedArgs &args, int64_t chains, int sms, cudaStream_t str
     if (max_w > kPairMaxWarps) max_w = kPairMaxWarps;
     const Geometry geo = balance((chains + 15) / 16, sms, max_w);
     const int smem = kTableBytes + R * 64 + geo.warps_per_cta * per_warp;
-    int lg = 0;
-    while ((1 << lg) < R) lg++;
-    args.q.ru = 1u << (26 - lg);
-    args.q.rq = 1u << (lg + 6);
+    args.q.rmask = (uint32_t)(R - 1) << 6;
     int rc = set_smem(fused_pair_kernel<R>, smem);
     if (rc) return rc;
     fused_pair_kernel<R><<<geo.grid, geo.warps_per_cta * 32, smem, stream>>>(args);
