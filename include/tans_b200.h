@@ -248,6 +248,18 @@ int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_bytes,
                    int64_t cols, int64_t batch, int64_t col_splits,
                    int32_t *status, void *stream);
 
+/* Uncompressed e4m3 GEMV (no counterpart in the reference; the denominator
+ * of the decode-GEMV's amplification, as fp8_vecadd_raw is the fused add's):
+ *   y[b][r] = bf16(scale[r] * sum_c e4m3(w[r][c]) * x[b][c]), fp32 accumulate,
+ * w e4m3 [rows][cols] row-major (16-byte aligned), x bf16 [batch][cols],
+ * batch 1..8, y bf16 [batch][rows]; the same mma.sync f16 path and the same
+ * deterministic column-slice reduction as tans_b200_gemv (partials:
+ * caller-owned f32 [col_splits][batch][rows]).  rows % 16 == 0,
+ * cols % (64*col_splits) == 0. */
+int tans_b200_gemv_raw(const uint8_t *w, const float *scale, const uint16_t *x, uint16_t *y,
+                       float *partials, int64_t rows, int64_t cols, int64_t batch,
+                       int64_t col_splits, void *stream);
+
 /* Decode a GEMV-layout weight (tans_b200_gemv's stream format) to a dense
  * row-major bf16 [rows][cols] matrix of its e4m3 values (unscaled; exact).
  * For batches above 8, where the contraction belongs to a library bf16 GEMM

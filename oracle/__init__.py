@@ -13,6 +13,11 @@ Function map (reference file:line each one restates):
   encode                       csrc/tans_codec.cpp:22-60, 69-196
   decode                       csrc/tans_decode.cu:65-155
   vecadd_fused                 csrc/vecadd.cu:84-154, 156-243
+  quantize_freqs / build_spread / encode_front
+                               rans_vectoradd/tans_codec.py:24-27, 30-60, 90-143
+                               (numpy, so that a caller can encode with the
+                               reference's own compiled encoder without the
+                               product package)
 """
 from __future__ import annotations
 
@@ -170,6 +175,65 @@ def vecadd_fused(a, b, table, n_fp8_per_stream: int):
                                    _p(bc), bc.size, _p(bo), _p(bst), _p(bp), _p(bsm),
                                    _p(table), K, N, _p(out))
     return out, rc == 0
+
+
+# -------------------------------------------- encode front end (numpy)
+
+_L = 4096                            # tans_codec.py:24-25
+_SIGMA = (_L >> 1) + (_L >> 3) + 3   # tans_codec.py:26
+
+
+def quantize_freqs(probs) -> np.ndarray:
+    """tans_codec.py:30-46: round(p * L) (half to even), floor 1 for p > 0,
+    then move single units to/from the symbol with the largest rounding error
+    (first index on ties) until the sum is L."""
+    p = np.asarray(probs, dtype=np.float64)
+    f = np.round(p * _L).astype(np.int64)
+    f[(p > 0) & (f == 0)] = 1
+    while int(f.sum()) != _L:
+        err = p * _L - f
+        if f.sum() < _L:
+            err[p == 0] = -np.inf
+            f[int(np.argmax(err))] += 1
+        else:
+            err = -err
+            err[(p == 0) | (f <= 1)] = -np.inf
+            f[int(np.argmax(err))] -= 1
+    return f.astype(np.int32)
+
+
+def build_spread(freqs) -> np.ndarray:
+    """tans_codec.py:49-60: walk the slots with stride SIGMA (mod L), placing
+    symbol 0 f_0 times, then symbol 1, ..."""
+    spread = np.empty(_L, np.int32)
+    pos = 0
+    for sym, f in enumerate(np.asarray(freqs, dtype=np.int64)):
+        for _ in range(int(f)):
+            spread[pos] = sym
+            pos = (pos + _SIGMA) % _L
+    return spread
+
+
+def encode_front(fp8, exp_freqs, tile: int = 8):
+    """tans_codec.py:90-143 up to the slab encoder: the pair symbols
+    u8[K, N/2] (exp(2i) << 4 | exp(2i+1)), the packed sign/mantissa pairs
+    (sm(2i) | sm(2i+1) << 4) as [N/2/tile, K, tile] (tile > 0) or [N/2, K],
+    and the pair frequencies (outer product of the float32 nibble
+    probabilities) with their spread.  fp8: uint8 [K, N] e4m3 bytes."""
+    b = _np(fp8, np.uint8)
+    K, N = b.shape
+    exp = (b >> 3) & 15
+    sm = ((b >> 4) & 8) | (b & 7)
+    syms = ((exp[:, 0::2] << 4) | exp[:, 1::2]).astype(np.uint8)
+    pairs = (sm[:, 0::2] | (sm[:, 1::2] << 4)).astype(np.uint8)           # [K, N/2]
+    if tile > 0:
+        sm_out = np.ascontiguousarray(pairs.reshape(K, N // 2 // tile, tile).transpose(1, 0, 2))
+    else:
+        sm_out = np.ascontiguousarray(pairs.T)
+    pr = np.asarray(exp_freqs, dtype=np.float64).astype(np.float32)
+    pr = pr / pr.sum()
+    freqs = quantize_freqs((pr[:, None] * pr[None, :]).reshape(-1))
+    return syms, sm_out, freqs, build_spread(freqs)
 
 
 # ------------------------------------------------------------ reference _C

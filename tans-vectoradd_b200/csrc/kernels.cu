@@ -1176,6 +1176,90 @@ __device__ __forceinline__ void mma_16x8x16(float (&d)[4], uint32_t a0, uint32_t
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+// Uncompressed e4m3 GEMV (the decode-GEMV's denominator): the same sum with
+// the same mma.sync f16 path and the same column-slice reduction, W read as
+// plain e4m3 bytes [R][C].  A warp owns 16 rows of one column slice; per
+// 64-column chunk lane (g, t) loads 16 contiguous bytes of rows g and g + 8
+// (columns 16t .. 16t + 15).  Inside a chunk the MMA k index is permuted:
+// in step s, lane t's k = 2t, 2t+1 / 2t+8, 2t+9 are columns 16t + 4s + 0, 1 /
+// 2, 3, and the x (B) fragment follows the same permutation, so every
+// product w[r][c] * x[b][c] is summed exactly once.  Two chunks are in
+// flight per warp (4 KiB of W per warp).
+constexpr int kRawGemvWarps = 8;  // row groups (16 rows each) per CTA
+
+struct RawGemvArgs {
+    const uint8_t *w;       // e4m3 [R][C]
+    const uint16_t *x;      // bf16 [B][C]
+    float *part;            // f32 [KS][B][R]
+    int64_t R, C, B, KS;
+};
+
+__device__ __forceinline__ void raw_chunk(float (&acc)[4], uint4 wa, uint4 wb, const uint16_t *xp) {
+    const uint4 x0 = *reinterpret_cast<const uint4 *>(xp);      // halves 4s .. 4s + 3, s = 0, 1
+    const uint4 x1 = *reinterpret_cast<const uint4 *>(xp + 8);  // s = 2, 3
+    const uint32_t a[4] = {wa.x, wa.y, wa.z, wa.w}, b[4] = {wb.x, wb.y, wb.z, wb.w};
+    const uint32_t xv[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int s = 0; s < 4; s++)
+        mma_16x8x16(acc, cvt_f16x2_e4m3x2(a[s] & 0xFFFFu), cvt_f16x2_e4m3x2(b[s] & 0xFFFFu),
+                    cvt_f16x2_e4m3x2(a[s] >> 16), cvt_f16x2_e4m3x2(b[s] >> 16), xv[2 * s],
+                    xv[2 * s + 1]);
+}
+
+__global__ void __launch_bounds__(kRawGemvWarps * 32) gemv_raw_kernel(const RawGemvArgs p) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    const int64_t CS = p.C / p.KS;
+    const int k = blockIdx.y;
+    const int64_t pitch = CS + 8;  // halves
+    uint16_t *xs = reinterpret_cast<uint16_t *>(smem);
+    // x slice -> f16 in shared memory (rows >= B are zero)
+    for (int b = 0; b < kGemvMaxBatch; b++) {
+        const uint16_t *xr = p.x + b * p.C + k * CS;
+        for (int32_t c = threadIdx.x; c < (int32_t)CS; c += blockDim.x) {
+            const float v = b < p.B ? __uint_as_float((uint32_t)xr[c] << 16) : 0.f;
+            xs[b * pitch + c] = __half_as_ushort(__float2half_rn(v));
+        }
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int64_t r0 = ((int64_t)blockIdx.x * kRawGemvWarps + warp) * 16;
+    if (r0 >= p.R) return;
+    const uint8_t *w0 = p.w + (r0 + g) * p.C + k * CS + 16 * t;
+    const uint8_t *w1 = w0 + 8 * p.C;
+    const uint16_t *xp = xs + g * pitch + 16 * t;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int32_t nch = (int32_t)(CS / 64);
+    uint4 a0 = ld_stream_v4(w0), b0 = ld_stream_v4(w1), a1 = a0, b1 = b0;
+    if (nch > 1) {
+        a1 = ld_stream_v4(w0 + 64);
+        b1 = ld_stream_v4(w1 + 64);
+    }
+    for (int32_t j = 0; j < nch; j += 2) {
+        const uint4 ca0 = a0, cb0 = b0, ca1 = a1, cb1 = b1;
+        if (j + 2 < nch) {
+            a0 = ld_stream_v4(w0 + 64 * (j + 2));
+            b0 = ld_stream_v4(w1 + 64 * (j + 2));
+        }
+        if (j + 3 < nch) {
+            a1 = ld_stream_v4(w0 + 64 * (j + 3));
+            b1 = ld_stream_v4(w1 + 64 * (j + 3));
+        }
+        raw_chunk(acc, ca0, cb0, xp + 64 * j);
+        if (j + 1 < nch) raw_chunk(acc, ca1, cb1, xp + 64 * (j + 1));
+    }
+    // D fragment: rows g, g + 8; batch columns 2t, 2t + 1
+    float *pk = p.part + (int64_t)k * p.B * p.R;
+    if (2 * t < p.B) {
+        pk[(2 * t) * p.R + r0 + g] = acc[0];
+        pk[(2 * t) * p.R + r0 + g + 8] = acc[2];
+    }
+    if (2 * t + 1 < p.B) {
+        pk[(2 * t + 1) * p.R + r0 + g] = acc[1];
+        pk[(2 * t + 1) * p.R + r0 + g + 8] = acc[3];
+    }
+}
+
 // Natural-order e4m3 words of four pairs: lo = pairs 0,1 (bytes e0 e1 e0 e1),
 // hi = pairs 2,3.
 __device__ __forceinline__ void compose_pairs(uint32_t S, uint32_t M, const Opq &q, uint32_t &lo,
@@ -2398,6 +2482,41 @@ int launch_dense(const DenseArgs &args, int64_t chains, int sms, cudaStream_t st
     if (rc) return rc;
     gemv_dense_kernel<R><<<geo.grid, geo.warps_per_cta * 32, smem, st>>>(args);
     return launch_status("gemv_dense_kernel");
+}
+
+extern "C" int tans_b200_gemv_raw(const uint8_t *w, const float *scale, const uint16_t *x,
+                                  uint16_t *y, float *partials, int64_t rows, int64_t cols,
+                                  int64_t batch, int64_t col_splits, void *stream) {
+    tans_b200::clear_error();
+    if (rows <= 0 || rows % 16 != 0)
+        return fail(TANS_B200_ERR_INVALID, "gemv_raw: rows must be a positive multiple of 16");
+    if (col_splits < 1 || cols <= 0 || cols % (64 * col_splits) != 0)
+        return fail(TANS_B200_ERR_INVALID, "gemv_raw: cols must be a positive multiple of 64 * col_splits");
+    if (batch < 1 || batch > kGemvMaxBatch) return fail(TANS_B200_ERR_INVALID, "gemv_raw: batch must be 1..8");
+    if (!w || !scale || !x || !y || !partials) return fail(TANS_B200_ERR_INVALID, "gemv_raw: null pointer");
+    if (!aligned(w, 16) || !aligned(x, 2) || !aligned(y, 2) || !aligned(partials, 4) || !aligned(scale, 4))
+        return fail(TANS_B200_ERR_INVALID, "gemv_raw: w must be 16-byte aligned");
+    const int64_t cs = cols / col_splits;
+    const int64_t smem = kGemvMaxBatch * (cs + 8) * 2;
+    if (smem > kSmemMax)
+        return fail(TANS_B200_ERR_INVALID, "gemv_raw: a column slice of %lld does not fit in shared memory",
+                    (long long)cs);
+    int sms;
+    int rc = device_setup(&sms);
+    if (rc) return rc;
+    rc = set_smem(gemv_raw_kernel, (int)smem);
+    if (rc) return rc;
+    RawGemvArgs args{w, x, partials, rows, cols, batch, col_splits};
+    const dim3 grid((unsigned)((rows / 16 + kRawGemvWarps - 1) / kRawGemvWarps), (unsigned)col_splits);
+    cudaStream_t st = (cudaStream_t)stream;
+    gemv_raw_kernel<<<grid, kRawGemvWarps * 32, (int)smem, st>>>(args);
+    rc = launch_status("gemv_raw_kernel");
+    if (rc) return rc;
+    const int64_t n = rows * batch;
+    const int64_t blocks = (n + 255) / 256;
+    gemv_reduce_kernel<<<(unsigned)(blocks < 4 * sms ? blocks : 4 * sms), 256, 0, st>>>(
+        partials, scale, y, rows, batch, col_splits);
+    return launch_status("gemv_reduce_kernel");
 }
 
 extern "C" int tans_b200_gemv_weight_dense(const uint8_t *compressed, int64_t compressed_bytes,

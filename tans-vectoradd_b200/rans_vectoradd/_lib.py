@@ -49,6 +49,7 @@ def _load() -> ctypes.CDLL:
         "tans_b200_gemv_gather": (i32, [p, i64, p, p, p, p, p, p, p, p, i64, i64, i64, i64, p, p,
                                         p]),
         "tans_b200_gemv_weight_dense": (i32, [p, i64, p, p, p, p, p, p, i64, i64, i64, p, p]),
+        "tans_b200_gemv_raw": (i32, [p, p, p, p, p, i64, i64, i64, i64, p]),
         "tans_b200_scale_rows_bf16": (i32, [p, p, p, i64, i64, p]),
         "tans_b200_gemm_tc": (i32, [p, i64, p, p, p, p, p, p, p, p, i64, i64, i64, i64, p, p]),
         "tans_b200_fp8_vecadd_fused_range": (i32, [p, i64, p, p, p, p, p, i64, p, p, p, p, p, p,

@@ -272,6 +272,47 @@ def gemm_tc(weight: EncodedWeight, x: torch.Tensor, out: torch.Tensor | None = N
     return out
 
 
+def raw_col_splits(rows: int, cols: int, sms: int = 148) -> int:
+    """Column slices of the uncompressed GEMV: the fewest that divide the
+    64-column chunks and give at least four 128-row CTAs per SM."""
+    chunks = cols // 64
+    for d in range(1, chunks + 1):
+        if chunks % d == 0 and (rows + 127) // 128 * d >= 4 * sms:
+            return d
+    return chunks
+
+
+def gemv_raw(w8: torch.Tensor, scale: torch.Tensor, x: torch.Tensor,
+             out: torch.Tensor | None = None, partials: torch.Tensor | None = None,
+             col_splits: int | None = None) -> torch.Tensor:
+    """Uncompressed e4m3 GEMV, y = bf16(scale * (W8 @ x^T)) with fp32
+    accumulate (no reference counterpart): the same mma.sync path and column
+    reduction as gemv() with the weight read as plain e4m3 bytes, i.e. the
+    decode-GEMV's denominator.  w8: uint8 (e4m3 bits) [rows, cols] on CUDA."""
+    _req(w8.is_cuda and w8.dtype == torch.uint8 and w8.dim() == 2 and w8.is_contiguous(),
+         "w8 must be a contiguous CUDA uint8 [rows, cols] tensor of e4m3 bits")
+    _req(x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(),
+         "x must be a contiguous CUDA bfloat16 [batch, cols] tensor")
+    R, C = w8.shape
+    B = x.shape[0]
+    _req(x.shape[1] == C, f"x has {x.shape[1]} columns, the weight {C}")
+    _req(1 <= B <= 8, "batch must be 1..8")
+    dev = w8.device
+    _same_device(dev, scale, x)
+    KS = col_splits or raw_col_splits(R, C)
+    with torch.cuda.device(dev):
+        if out is None:
+            out = torch.empty((B, R), dtype=torch.bfloat16, device=dev)
+        if partials is None:
+            partials = torch.empty((KS, B, R), dtype=torch.float32, device=dev)
+        _req(partials.numel() >= KS * B * R and partials.dtype == torch.float32,
+             "partials must be f32 with col_splits * batch * rows elements")
+        sc = scale.float().contiguous()
+        check(LIB.tans_b200_gemv_raw(w8.data_ptr(), sc.data_ptr(), x.data_ptr(), out.data_ptr(),
+                                     partials.data_ptr(), R, C, B, KS, _stream(dev)))
+    return out
+
+
 def reference_gemv(w8: torch.Tensor, scale: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     """Decode-then-dense fp32 reference: bf16((W8.float() * s) @ x.float()^T)."""
     w = w8.view(torch.float8_e4m3fn).float() * scale.float()[:, None]

@@ -83,6 +83,31 @@ def test_gemv_down_projection_split(cuda):
     assert tans_gemv.rel_err(y1, ref) <= TOL
 
 
+@pytest.mark.gpu
+@pytest.mark.parametrize("R,C,B,KS", [(16, 64, 1, 1), (48, 128, 3, 2), (256, 1024, 8, 4),
+                                      (17408, 5120, 1, None), (5120, 17408, 8, None)])
+def test_gemv_raw_matches_fp32_reference(cuda, R, C, B, KS):
+    """The uncompressed e4m3 GEMV (the decode-GEMV's denominator): same
+    bound against the fp32 reference; deterministic across calls."""
+    w8, s = make(R, C, R + 3 * C)
+    x = torch.randn(B, C, generator=torch.Generator().manual_seed(5)).to(torch.bfloat16)
+    w8d, sd, xd = w8.to(cuda), s.to(cuda), x.to(cuda)
+    y1 = tans_gemv.gemv_raw(w8d, sd, xd, col_splits=KS)
+    y2 = tans_gemv.gemv_raw(w8d, sd, xd, col_splits=KS)
+    assert torch.equal(y1, y2)
+    assert tans_gemv.rel_err(y1, tans_gemv.reference_gemv(w8d, sd, xd)) <= TOL
+
+
+def test_gemv_raw_rejects_bad_shapes():
+    from rans_vectoradd._lib import LIB
+    assert LIB.tans_b200_gemv_raw(None, None, None, None, None, 24, 64, 1, 1, None) == 1
+    assert b"multiple of 16" in LIB.tans_b200_last_error()
+    assert LIB.tans_b200_gemv_raw(None, None, None, None, None, 16, 96, 1, 1, None) == 1
+    assert LIB.tans_b200_gemv_raw(None, None, None, None, None, 16, 64, 9, 1, None) == 1
+    assert LIB.tans_b200_gemv_raw(None, None, None, None, None, 16, 64, 1, 1, None) == 1
+    assert b"null pointer" in LIB.tans_b200_last_error()
+
+
 def test_gemv_rejects_bad_shapes():
     from rans_vectoradd._lib import LIB
     assert LIB.tans_b200_gemv(None, 0, None, None, None, None, None, None, None, None, None,

@@ -130,3 +130,21 @@ def test_fused_equals_raw_on_decoded_inputs(small):
     assert ok
     untiled = out.reshape(N // 16, K, 16).transpose(1, 0, 2).reshape(K, N)
     assert np.array_equal(untiled, oracle.vecadd_raw(a, b).reshape(K, N))
+
+
+@pytest.mark.parametrize("tile", [0, 8])
+def test_oracle_encode_front_matches_codec(tile):
+    """oracle.encode_front (numpy restatement of tans_codec.py:90-143 up to
+    the slab encoder) equals the golden-pinned codec front end, including a
+    profile with empty exponent bins."""
+    import numpy as np
+    import torch
+    from rans_vectoradd import QWEN3_14B_FP8_EXP, random_fp8_bytes, tans_codec
+    g = torch.Generator().manual_seed(11)
+    x = random_fp8_bytes(96 * 128, device="cpu", generator=g).view(96, 128)
+    for prof in (QWEN3_14B_FP8_EXP, [0.0] * 3 + [1.0] * 13):
+        syms, sm, freqs, spread = oracle.encode_front(x.numpy(), prof, tile=tile)
+        s2, sm2, _ = tans_codec.split_fp8(x, tile=tile)
+        pf = tans_codec.pair_freqs_from_exponents(torch.tensor(prof, dtype=torch.float64))
+        assert np.array_equal(syms, s2.numpy()) and np.array_equal(sm, sm2.numpy())
+        assert np.array_equal(freqs, pf) and np.array_equal(spread, tans_codec.build_spread(pf))
