@@ -68,6 +68,11 @@ def parse():
                     help="log2 fp8 elements (decode, encode)")
     ap.add_argument("--layers", type=int, default=40, help="layers of the GEMV stack")
     ap.add_argument("--batch", type=int, default=8, help="GEMV batch (1..8)")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="vecadd: headline keys only (no decode_cfg2 / gemv_cfg3 / stack_cfg4 / "
+                         "reference_gpu keys)")
+    ap.add_argument("--no-ref-gpu", action="store_true",
+                    help="do not time the reference's own kernels (oracle/_ref)")
     return ap.parse_args()
 
 
@@ -122,7 +127,7 @@ def make_workload(n: int, N: int, seed: int):
     # kernel argument order: comp, offsets, states, partial, sm
     a = [ex[0], ex[2], ex[1], ex[3], ex[4]]
     b = [ey[0], ey[2], ey[1], ey[3], ey[4]]
-    return x, y, a, b, tbl, K
+    return x, y, a, b, tbl, K, ex[6], ex[5]
 
 
 def make_workload_device(n: int, N: int, seed: int, dev):
@@ -151,7 +156,7 @@ def make_workload_device(n: int, N: int, seed: int, dev):
     tbl = tans_codec.build_decode_table(ex[6].numpy(), ex[5].numpy())
     a = [ex[0], ex[2], ex[1], ex[3], ex[4]]
     b = [ey[0], ey[2], ey[1], ey[3], ey[4]]
-    return x, y, a, b, tbl, K
+    return x, y, a, b, tbl, K, ex[6], ex[5]
 
 
 def alg_bytes(a, b, n):
@@ -264,39 +269,67 @@ def sum_over_ranks(v, ws, dev):
 
 # -------------------------------------------------------------- CPU legs
 
-def cpu_decode_add(a, b, tbl, N, n_total, budget_s=10.0):
-    """Oracle decode + add (port of the reference decoder and satfinite add,
-    OpenMP over streams) on a bounded sample of the workload's streams.
-    Returns (GB/s uncompressed-equivalent, threads, sample description)."""
+def _normal_fp8(n: int, gen: torch.Generator) -> torch.Tensor:
+    """The workload generator with torch alone (no product package): x ~
+    N(0, 1) scaled so max|x| maps to 448, cast to e4m3 bytes."""
+    v = torch.randn(n, generator=gen)
+    return (v * (448.0 / v.abs().max())).to(torch.float8_e4m3fn).view(torch.uint8)
+
+
+def reference_cpu_path(x, y, hist, N, k_s=1024, budget_s=10.0):
+    """The reference's CPU path on the first k_s streams of both inputs, on
+    every core of this process: its encode (the oracle's numpy restatement of
+    the tans_codec front end, tans_codec.py:90-143, feeding the reference's
+    own compiled tans_encode_interleaved, csrc/tans_codec.cpp:69-196, from
+    oracle/_ref), then decode + add (the oracle port of csrc/tans_decode.cu
+    and csrc/vecadd.cu; the reference has no CPU decoder).  About half the
+    budget goes to each half.  GB/s count 3 bytes per output element."""
     sys.path.insert(0, ROOT)
+    import numpy as np
     import oracle
-
-    K = a[2].numel()
-    k_s = min(K, 1024)  # 1024 streams x N bytes
-    # slice whole encoder blocks: offsets rebased, comp sliced by byte range
-    nb = (k_s + 127) // 128
-
-    def shard(t):
-        comp, off, st, part, sm = t
-        end = int(off[nb])
-        sm_s = sm.view(N // 16, K, 8)[:, :k_s].contiguous()
-        return tuple(v.cpu() for v in (comp[:end], off[:nb + 1], st[:k_s], part[:k_s], sm_s))
-
-    sa, sb = shard(a), shard(b)
-    elems = k_s * N
-    # every core this process may run on (torchrun sets OMP_NUM_THREADS=1)
+    ref = oracle.load_ref_ext()
     oracle.set_num_threads(len(os.sched_getaffinity(0)))
-    reps, t_used = 0, 0.0
-    t_start = time.perf_counter()
-    while t_used < budget_s and reps < 100000:
-        out, ok = oracle.vecadd_fused(sa, sb, tbl, N)
+    elems = k_s * N
+    xs, ys = x[:elems].view(k_s, N), y[:elems].view(k_s, N)
+
+    def enc(v):
+        syms, sm, f, sp = oracle.encode_front(v.numpy(), hist, tile=8)
+        if ref is not None:
+            comp, st, off, part = (t.numpy() for t in ref.tans_encode_interleaved(
+                torch.from_numpy(syms), torch.from_numpy(f), torch.from_numpy(sp)))
+        else:
+            comp, st, off, part = oracle.encode(syms, f, sp)
+        return (comp, off, st, part, sm), f, sp
+
+    reps_e, t0 = 0, time.perf_counter()
+    while True:
+        a, f, sp = enc(xs)
+        b, _, _ = enc(ys)
+        reps_e += 1
+        t_enc = time.perf_counter() - t0
+        if t_enc >= budget_s / 2:
+            break
+    tbl = oracle.build_decode_table(sp, f)
+    reps_d, t0 = 0, time.perf_counter()
+    while True:
+        out, ok = oracle.vecadd_fused(a, b, tbl, N)
         assert ok
-        reps += 1
-        t_used = time.perf_counter() - t_start
-    gbs = 3.0 * elems * reps / t_used / 1e9
-    return gbs, oracle.num_threads(), (f"{reps} pass(es) over {k_s} streams x {N} fp8 "
-                                       f"({elems} elements per input) of the workload, "
-                                       f"{t_used:.1f} s")
+        reps_d += 1
+        t_dec = time.perf_counter() - t0
+        if t_dec >= budget_s / 2:
+            break
+    same = bool(np.array_equal(out.reshape(N // 16, k_s, 16).transpose(1, 0, 2).reshape(-1),
+                               oracle.vecadd_raw(xs.numpy().reshape(-1), ys.numpy().reshape(-1))))
+    per_e, per_d = t_enc / reps_e, t_dec / reps_d
+    return {"decode_add_gbs": 3.0 * elems / per_d / 1e9,
+            "encode_decode_add_gbs": 3.0 * elems / (per_e + per_d) / 1e9,
+            "encode_input_gbs": 2.0 * elems / per_e / 1e9,
+            "encoder": "reference (oracle/_ref tans_encode_interleaved)" if ref is not None
+            else "oracle port (reference extension not built)",
+            "threads": oracle.num_threads(), "bit_exact_vs_raw_add": same,
+            "sample": (f"first {k_s} streams x {N} fp8 of each input ({elems} elements per "
+                       f"input): {reps_e} encode(s) of both inputs in {t_enc:.1f} s, "
+                       f"{reps_d} decode+add pass(es) in {t_dec:.1f} s")}
 
 
 def cpu_encode_rates(x, N, hist):
@@ -328,29 +361,79 @@ def cpu_encode_rates(x, N, hist):
 
 def run_reference_arm(args, ws, rank):
     """--impl reference: the reference's CPU implementation of the path on the
-    host cores.  The reference has no CPU decoder, so decode+add is the oracle
-    port of its decoder/adder; encode is timed with the reference's own
-    compiled encoder when oracle/_ref is present."""
+    host cores, on the same workload (seed 0 inputs, generated with torch
+    alone), each step a bounded sample (reference_cpu_path).  Nothing of the
+    product package is imported.  `value` is decode + add (the work the GPU
+    arm's e2e does from encoded host buffers); encode + decode + add is
+    reported beside it."""
     if rank != 0:
         return
-    n = 1 << args.elems_log2
+    n = vecadd_elements(args)
     N = args.n_fp8
-    x, y, a, b, tbl, K = make_workload(n, N, 0)
-    samples = []
+    gen = torch.Generator().manual_seed(0)
+    x, y = _normal_fp8(n, gen), _normal_fp8(n, gen)
+    hist = (torch.bincount(((x >> 3) & 15).long(), minlength=16) +
+            torch.bincount(((y >> 3) & 15).long(), minlength=16)).double().numpy()
+    K = n // N
+    runs = []
     for i in range(args.warmup + args.steps):
-        gbs, threads, desc = cpu_decode_add(a, b, tbl, N, n, budget_s=2.0)
+        r = reference_cpu_path(x, y, hist, N, budget_s=1.0)
         if i >= args.warmup:
-            samples.append(gbs)
-    v = statistics.median(samples)
+            runs.append(r)
+    v = statistics.median(r["decode_add_gbs"] for r in runs)
+    full = statistics.median(r["encode_decode_add_gbs"] for r in runs)
+    last = runs[-1]
     line = {"impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u8",
-            "data": "synthetic", "config": workload_config(args, K),
-            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": threads,
-                             "kind": "port", "sample": desc},
+            "data": "synthetic (N(0,1)*448/absmax e4m3, seed 0)", "config": workload_config(args, K),
+            "cpu_baseline": {"value": round(v, 3), "unit": "GB/s", "cores": last["threads"],
+                             "kind": "port", "sample": last["sample"],
+                             "encode_decode_add_gbs": round(full, 3),
+                             "encoder": last["encoder"],
+                             "bit_exact_vs_raw_add": last["bit_exact_vs_raw_add"]},
             "e2e": {"value": round(v, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     emit(line, args)
+
+
+def reference_gpu(da, db, dtbl, xd, yd, N, K, spread, freqs, out_ours, ms_fused, ms_raw,
+                  args, stream, barrier):
+    """The reference's own kernels (its unmodified sources compiled for
+    sm_100a into oracle/_ref, as in bench_vecadd.py:39-47, 84-99) on this
+    run's device data: fused decode+add, raw add and the standalone decode
+    (its [N/2][K] sign/mantissa layout, table rebuilt on the host each call
+    as the reference does); ratios = reference ms / ours."""
+    sys.path.insert(0, ROOT)
+    import oracle
+    import rans_vectoradd as rv
+    ref = oracle.load_ref_ext()
+    if ref is None:
+        return {"unavailable": "oracle/_ref (the reference built from source) is not present"}
+    fused = lambda: ref.fp8_vecadd_fused_tans(*da, *db, dtbl, N)  # noqa: E731
+    same_fused = bool(torch.equal(fused(), out_ours))
+    ms_f = timed(fused, args.steps, args.warmup, stream, barrier) / args.steps
+    ms_r = timed(lambda: ref.fp8_vecadd_raw(xd, yd), args.steps, args.warmup, stream,
+                 barrier) / args.steps
+    sm0 = da[4].view(N // 16, K, 8).permute(0, 2, 1).reshape(N // 2, K).contiguous()
+    # spread/freqs on the device: the reference builds its table on the host
+    # and places it on spread's device (csrc/tans_decode.cu:23-59)
+    sp, pf = spread.to(torch.int32).to(xd.device), freqs.to(torch.int32).to(xd.device)
+    dargs = (da[0], da[1], da[2], da[3], sm0, sp, pf)
+    ours_args = dargs
+    same_dec = bool(torch.equal(ref.gpu_tans_decode(*dargs, N), rv.gpu_tans_decode(*ours_args, N)))
+    dsteps = max(3, args.steps // 4)
+    ms_d = timed(lambda: ref.gpu_tans_decode(*dargs, N), dsteps, 2, stream, barrier) / dsteps
+    ms_do = timed(lambda: rv.gpu_tans_decode(*ours_args, N), dsteps, 2, stream, barrier) / dsteps
+    del sm0
+    return {"what": "the reference's unmodified kernels (oracle/_ref, built for sm_100a) on the "
+                    "same device tensors", "ms_fused": round(ms_f, 4), "ms_raw": round(ms_r, 4),
+            "ms_decode": round(ms_d, 4), "ms_decode_ours": round(ms_do, 4),
+            "x_ref_fused": round(ms_f / ms_fused, 3), "x_ref_raw": round(ms_r / ms_raw, 3),
+            "x_ref_decode": round(ms_d / ms_do, 3),
+            "reference_fused_over_its_raw": round(ms_r / ms_f, 4),
+            "fused_bit_exact_vs_reference_kernel": same_fused,
+            "decode_bit_exact_vs_reference_kernel": same_dec}
 
 
 def vecadd_elements(args) -> int:
@@ -404,13 +487,14 @@ def cfg2_input(n: int, N: int, seed: int, dev, chunk_log2: int = 28):
 
 def encode_cfg2(n: int, N: int, seed: int, dev):
     """cfg2 input encoded on the device (tile 0) with the public encoder.
-    Returns (comp, offsets, states, partial, sm, decode table, K, raw)."""
+    Returns (comp, offsets, states, partial, sm, decode table, K, raw, spread,
+    pair freqs)."""
     from rans_vectoradd import tans_codec
     raw, hist = cfg2_input(n, N, seed, dev)
     K = n // N
     comp, states, offsets, part, sm, pf, sp = tans_codec.encode(raw.view(K, N), hist, tile=0)
     table = tans_codec.build_decode_table(sp.numpy(), pf.numpy()).to(dev)
-    return comp, offsets, states, part, sm, table, K, raw
+    return comp, offsets, states, part, sm, table, K, raw, sp, pf
 
 
 def run_encode(args, dev, barrier):
@@ -454,13 +538,15 @@ def run_encode(args, dev, barrier):
     emit(line, args)
 
 
-def run_decode(args, dev, barrier):
-    """cfg2: standalone decode of 2^decode_log2 e4m3 bytes to [N][K] in HBM."""
+def decode_cfg2(args, dev, barrier, steps):
+    """cfg2: standalone decode of 2^decode_log2 e4m3 bytes to [N][K] in HBM,
+    checked by a byte round trip; the reference's own decode kernel
+    (oracle/_ref, csrc/tans_decode.cu:125-210) timed on the same tensors."""
     from rans_vectoradd import _C
     from rans_vectoradd._lib import LIB, check
     n = 1 << args.decode_log2
     N = args.n_fp8
-    comp, off, st, part, sm, tbl, K, raw = encode_cfg2(n, N, 0, dev)
+    comp, off, st, part, sm, tbl, K, raw, sp, pf = encode_cfg2(n, N, 0, dev)
     d = [t.to(dev) for t in (comp, off, st, part, sm, tbl)]
     out = torch.empty((N, K), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
@@ -472,14 +558,34 @@ def run_decode(args, dev, barrier):
                                    _C._status(dev).data_ptr(), stream.cuda_stream))
     step()
     ok = bool(torch.equal(out.t(), raw.view(K, N))) and _C.data_status(dev) == 0
-    ms = timed(step, args.steps, args.warmup, stream, barrier) / args.steps
+    ms = timed(step, steps, args.warmup, stream, barrier) / steps
     alg = sum(t.numel() * t.element_size() for t in (comp, off, st, part, sm)) + n
     peak, kind = measured_peak()
-    emit({"workload": "decode (cfg2)", "elements": n, "n_fp8_per_stream": N, "streams": K,
-          "ms": round(ms, 4), "output_gbs": round(n / (ms / 1e3) / 1e9, 2),
-          "hbm_frac_algorithmic": round(alg / (ms / 1e3) / 1e9 / peak, 4),
-          "algorithmic_bytes": alg, "bits_per_fp8": round((alg - n) * 8 / n, 4),
-          "bit_exact_round_trip": ok, "peak_source": kind}, args)
+    res = {"elements": n, "n_fp8_per_stream": N, "streams": K, "ms": round(ms, 4),
+           "output_gbs": round(n / (ms / 1e3) / 1e9, 2),
+           "hbm_frac_algorithmic": round(alg / (ms / 1e3) / 1e9 / peak, 4),
+           "algorithmic_bytes": alg, "bits_per_fp8": round((alg - n) * 8 / n, 4),
+           "bit_exact_round_trip": ok, "peak_source": kind, "kernel": "decode_kernel"}
+    sys.path.insert(0, ROOT)
+    import oracle
+    ref = oracle.load_ref_ext()
+    if ref is not None and not args.no_ref_gpu:
+        del out
+        # spread/freqs on the device (the reference puts its table on spread's device)
+        rargs = (d[0], d[1], d[2], d[3], d[4], sp.to(torch.int32).to(dev),
+                 pf.to(torch.int32).to(dev))
+        r = ref.gpu_tans_decode(*rargs, N)
+        same = bool(torch.equal(r.t(), raw.view(K, N)))
+        del r
+        rs = 3
+        ms_ref = timed(lambda: ref.gpu_tans_decode(*rargs, N), rs, 1, stream, barrier) / rs
+        res["reference_kernel"] = {"ms": round(ms_ref, 3), "x_ours": round(ms_ref / ms, 2),
+                                   "bit_exact_round_trip": same}
+    return res
+
+
+def run_decode(args, dev, barrier):
+    emit({"workload": "decode (cfg2)"} | decode_cfg2(args, dev, barrier, args.steps), args)
 
 
 def run_container(args, dev, barrier):
@@ -541,12 +647,15 @@ def make_gemv_weight(R, C, seed, dev, col_splits):
     return tans_gemv.encode_weight(w8, s, col_splits=col_splits).to(dev), w8, s
 
 
-def run_gemv(args, dev, barrier):
-    """cfg3: W [17408 x 5120] (and [5120 x 17408], 4 column slices), x bf16
-    batch 1 and 8; rel err vs decode-then-dense fp32; effective GB/s."""
+def gemv_cfg3(args, dev, barrier):
+    """cfg3: W [17408 x 5120] (and [5120 x 17408]), x bf16 batch 1 and 8; the
+    fused decode-GEMV against the decode-then-dense fp32 reference (rel err)
+    and against the uncompressed e4m3 GEMV on the same mma.sync path
+    (x_raw = raw time / fused time, the GEMV's amplification)."""
     from rans_vectoradd import tans_gemv
     peak, kind = measured_peak()
     stream = torch.cuda.current_stream(dev)
+    out = []
     for (R, C, KS, seed) in ((17408, 5120, None, 0), (5120, 17408, None, 1)):
         enc, w8, s = make_gemv_weight(R, C, seed, dev, KS)
         for B in (1, 8):
@@ -556,16 +665,37 @@ def run_gemv(args, dev, barrier):
             KS = enc.col_splits
             part = torch.empty((KS, B, R), dtype=torch.float32, device=dev) if KS > 1 else None
             tans_gemv.gemv(enc, x, y, part)
-            err = tans_gemv.rel_err(y, tans_gemv.reference_gemv(w8, s, x))
-            ms = timed(lambda: tans_gemv.gemv(enc, x, y, part), args.steps * 10, args.warmup,
-                       stream, barrier) / (args.steps * 10)
+            ref = tans_gemv.reference_gemv(w8, s, x)
+            err = tans_gemv.rel_err(y, ref)
+            reps = args.steps * 10
+            ms = timed(lambda: tans_gemv.gemv(enc, x, y, part), reps, args.warmup, stream,
+                       barrier) / reps
+            rks = tans_gemv.raw_col_splits(R, C)
+            yr = torch.empty_like(y)
+            pr = torch.empty((rks, B, R), dtype=torch.float32, device=dev)
+            tans_gemv.gemv_raw(w8, s, x, yr, pr, rks)
+            err_raw = tans_gemv.rel_err(yr, ref)
+            ms_raw = timed(lambda: tans_gemv.gemv_raw(w8, s, x, yr, pr, rks), reps, args.warmup,
+                           stream, barrier) / reps
             alg = enc.stream_bytes() + 4 * R + 2 * B * C + 2 * B * R
-            emit({"workload": "gemv (cfg3)", "rows": R, "cols": C, "batch": B, "col_splits": KS,
-                  "us": round(ms * 1e3, 2),
-                  "effective_gbs": round(R * C / (ms / 1e3) / 1e9, 2),
-                  "hbm_frac_algorithmic": round(alg / (ms / 1e3) / 1e9 / peak, 4),
-                  "rel_err": err, "bits_per_fp8": round(enc.stream_bytes() * 8 / (R * C), 4),
-                  "peak_source": kind}, args)
+            alg_raw = R * C + 4 * R + 2 * B * C + 2 * B * R
+            out.append({"rows": R, "cols": C, "batch": B, "col_splits": KS,
+                        "us": round(ms * 1e3, 2),
+                        "effective_gbs": round(R * C / (ms / 1e3) / 1e9, 2),
+                        "hbm_frac_algorithmic": round(alg / (ms / 1e3) / 1e9 / peak, 4),
+                        "rel_err": err, "bits_per_fp8": round(enc.stream_bytes() * 8 / (R * C), 4),
+                        "raw_us": round(ms_raw * 1e3, 2),
+                        "raw_hbm_frac": round(alg_raw / (ms_raw / 1e3) / 1e9 / peak, 4),
+                        "raw_rel_err": err_raw, "x_raw": round(ms_raw / ms, 4),
+                        "peak_source": kind})
+            del yr, pr
+        del enc, w8, s
+    return out
+
+
+def run_gemv(args, dev, barrier):
+    for r in gemv_cfg3(args, dev, barrier):
+        emit({"workload": "gemv (cfg3)"} | r, args)
 
 
 def run_gemm(args, dev, barrier):
@@ -616,10 +746,12 @@ def run_gemm(args, dev, barrier):
     emit(line, args)
 
 
-def run_stack(args, ws, rank, dev, barrier):
+def stack_cfg4(args, ws, rank, dev, barrier):
     """cfg4: `layers` x (up [17408 x 5120] + down [5120 x 17408]) e4m3 GEMVs,
-    rows sharded over the ranks, NCCL all-gather of each y; one step = one
-    forward through the stack at batch `batch`."""
+    rows sharded over the ranks, each y all-gathered (fused into the GEMV
+    epilogue at N > 1, NCCL all-gather as the comparison path); one step = one
+    forward through the stack at batch `batch`.  Returns the result dict on
+    rank 0 (None elsewhere)."""
     import torch.distributed as dist
     from rans_vectoradd import shard, tans_gemv
     H, F, B = 5120, 17408, args.batch
@@ -714,8 +846,9 @@ def run_stack(args, ws, rank, dev, barrier):
     local = sum(u.stream_bytes() + d.stream_bytes() for u, d in zip(ups, downs))
     alg = sum_over_ranks(local, ws, dev)
     peak, kind = measured_peak()
+    del ups, downs
     if rank == 0:
-        emit({"workload": "gemv stack (cfg4)", "n_gpus": ws, "layers": args.layers, "batch": B,
+        return {"n_gpus": ws, "layers": args.layers, "batch": B,
               "ms_per_forward": round(per, 4), "graph": True,
               "ms_per_forward_eager": round(ms_eager / args.steps, 4),
               "effective_gbs": round(wbytes / (per / 1e3) / 1e9, 2),
@@ -726,10 +859,92 @@ def run_stack(args, ws, rank, dev, barrier):
                              "buffer over NVLink (symmetric memory), flag wait in the next GEMV"
                              if ws > 1 else "none (one rank)"),
               "ms_per_forward_nccl_all_gather": round(ms_nccl / args.steps, 4) if ws > 1 else None,
-              "fused_bit_exact_vs_nccl": exact}, args)
+              "fused_bit_exact_vs_nccl": exact}
+    return None
+
+
+def run_stack(args, ws, rank, dev, barrier):
+    r = stack_cfg4(args, ws, rank, dev, barrier)
+    if r is not None:
+        emit({"workload": "gemv stack (cfg4)"} | r, args)
 
 
 # ------------------------------------------------------------------- main
+
+def run_sweep(args, n, N, x, y, raw_step, peak, stream, barrier, dev):
+    """Stream-length sweep (cfg1's 1K/4K/16K/64K pair-symbol and fp8 readings):
+    the same inputs re-encoded on the device at each length, plain format
+    and, for streams longer than --segment-pairs, split streams."""
+    import rans_vectoradd as rv
+    from rans_vectoradd import tans_codec
+    xd, yd = x.to(dev), y.to(dev)
+    hist = (torch.bincount(((xd >> 3) & 15).long(), minlength=16) +
+            torch.bincount(((yd >> 3) & 15).long(), minlength=16)).cpu().double()
+    raw = rv.fp8_vecadd_raw(xd, yd)
+    for n_fp8 in (2048, 8192, 32768, 131072, 1024, 4096, 16384, 65536):
+        if n_fp8 == N:
+            continue
+        K2 = n // n_fp8
+        for S in (0, args.segment_pairs):
+            if S and not (n_fp8 // 2 > S and (n_fp8 // 2) % S == 0 and K2 % 32 == 0):
+                continue
+            ex = tans_codec.encode(xd.view(K2, n_fp8), hist, tile=8, segment_pairs=S)
+            ey = tans_codec.encode(yd.view(K2, n_fp8), hist, tile=8, segment_pairs=S)
+            a2 = [ex[0], ex[2], ex[1], ex[3], ex[4]]
+            b2 = [ey[0], ey[2], ey[1], ey[3], ey[4]]
+            dt2 = tans_codec.build_decode_table(ex[6].numpy(), ex[5].numpy()).to(dev)
+            kw = {"segment_pairs": S} if S else {}
+            o = rv.fp8_vecadd_fused_tans(*a2, *b2, dt2, n_fp8, **kw)
+            ok = torch.equal(o.view(n_fp8 // 16, K2, 16).permute(1, 0, 2).reshape(-1), raw)
+            del o
+            ms = timed(lambda: rv.fp8_vecadd_fused_tans(*a2, *b2, dt2, n_fp8, **kw), args.steps,
+                       args.warmup, stream, barrier)
+            tot2, sb2 = alg_bytes(a2, b2, n)
+            ps = ms / args.steps
+            line = {"sweep": True, "n_fp8_per_stream": n_fp8, "pair_symbols": n_fp8 // 2,
+                    "streams": K2, "ms": round(ps, 4),
+                    "gbs_uncompressed_equiv": round(3.0 * n / (ps / 1e3) / 1e9, 2),
+                    "x_raw": round(raw_step / ps, 4), "bits_per_fp8": round(sb2 * 8 / (2 * n), 4),
+                    "hbm_frac_compressed": round(tot2 / (ps / 1e3) / 1e9 / peak, 4),
+                    "bit_exact_vs_raw": bool(ok)}
+            if S:
+                line["split_stream_segment_pairs"] = S
+                line["chains"] = K2 * (n_fp8 // 2 // S)
+            emit(line, args)
+            del a2, b2, ex, ey
+            torch.cuda.empty_cache()
+
+
+def all_ranks(v, ws, dev):
+    """Every rank's value of v (list, rank order)."""
+    if ws == 1:
+        return [v]
+    import torch.distributed as dist
+    t = torch.tensor([float(v)], dtype=torch.float64, device=dev)
+    out = [torch.empty_like(t) for _ in range(ws)]
+    dist.all_gather(out, t)
+    return [float(o.item()) for o in out]
+
+
+def graph_ms(fn, steps, warmup, stream, barrier, dev):
+    """The same launches captured once in a CUDA graph and replayed: device ms
+    per launch without the host launch path (Python, ctypes, driver)."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(steps):
+                fn()
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    ms = timed(graph.replay, 3, 1, stream, barrier) / 3 / steps
+    del graph
+    return ms
+
 
 def main():
     args = parse()
@@ -767,9 +982,9 @@ def main():
     n = vecadd_elements(args)
     t_setup = time.perf_counter()
     if args.working_set_gib > 0:
-        x, y, a, b, tbl, K = make_workload_device(n, N, rank, dev)
+        x, y, a, b, tbl, K, spread, freqs = make_workload_device(n, N, rank, dev)
     else:
-        x, y, a, b, tbl, K = make_workload(n, N, rank)
+        x, y, a, b, tbl, K, spread, freqs = make_workload(n, N, rank)
     setup_s = time.perf_counter() - t_setup
     total_alg, stream_bytes = alg_bytes(a, b, n)
     bits_per_fp8 = stream_bytes * 8 / (2 * n)
@@ -785,7 +1000,7 @@ def main():
     raw = rv.fp8_vecadd_raw(xd, yd)
     same = torch.equal(out.view(N // 16, K, 16).permute(1, 0, 2).reshape(-1), raw)
     assert _C.data_status(dev) == 0
-    del out, raw
+    del raw
 
     fused = lambda: rv.fp8_vecadd_fused_tans(*da, *db, dtbl, N)  # noqa: E731
     with Clocks(local) as clk:
@@ -793,7 +1008,12 @@ def main():
     clocks = clk.summary()
     ms_raw = timed(lambda: rv.fp8_vecadd_raw(xd, yd), args.steps, args.warmup, stream, barrier)
     ms_cpy = timed(lambda: rv.fp8_memcpy(xd), args.steps, args.warmup, stream, barrier)
+    ms_graph = graph_ms(fused, args.steps, 2, stream, barrier, dev)
 
+    # per-rank spread of the device metric: launch time and SM clock of every rank
+    per_rank_ms = all_ranks(ms_fused / args.steps, ws, dev)
+    per_rank_graph_ms = all_ranks(ms_graph, ws, dev)
+    per_rank_mhz = all_ranks((clocks or {}).get("sm_mhz") or 0.0, ws, dev)
     ms_fused_max = max_over_ranks(ms_fused, ws, dev)
     ms_raw_max = max_over_ranks(ms_raw, ws, dev)
     per_step = ms_fused_max / args.steps
@@ -802,6 +1022,12 @@ def main():
     t_launch = ms_fused / args.steps / 1e3
     achieved = total_alg / t_launch / 1e9
     peak, peak_kind = measured_peak()
+
+    refgpu = None
+    if rank == 0 and ws == 1 and not args.no_extras and not args.no_ref_gpu:
+        refgpu = reference_gpu(da, db, dtbl, xd, yd, N, K, spread, freqs, out,
+                               ms_fused / args.steps, ms_raw / args.steps, args, stream, barrier)
+    del out
 
     # ---- end to end through the public API: pinned host -> device -> host
     e2e = None
@@ -826,17 +1052,39 @@ def main():
                "bit_exact_vs_device_call": bool(torch.equal(
                    hout, rv.fp8_vecadd_fused_tans(*da, *db, dtbl, N).cpu())),
                "api": "rans_vectoradd._C.fp8_vecadd_fused_tans_host (tans_b200_fp8_vecadd_fused_host)"}
+        del ha, hb, hout
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
-        gbs, threads, desc = cpu_decode_add(a, b, tbl.cpu(), N, n)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-               "sample": desc}
+        hx, hy = x.cpu(), y.cpu()
+        hist = (torch.bincount(((hx >> 3) & 15).long(), minlength=16) +
+                torch.bincount(((hy >> 3) & 15).long(), minlength=16)).double().numpy()
+        r = reference_cpu_path(hx, hy, hist, N, budget_s=10.0)
+        cpu = {"value": round(r["decode_add_gbs"], 3), "unit": "GB/s", "cores": r["threads"],
+               "kind": "port", "sample": r["sample"],
+               "encode_decode_add_gbs": round(r["encode_decode_add_gbs"], 3),
+               "encoder": r["encoder"], "bit_exact_vs_raw_add": r["bit_exact_vs_raw_add"],
+               "note": "value: decode + add (oracle port; the reference has no CPU decoder); "
+                       "encode_decode_add: the reference's encode (its compiled encoder) "
+                       "then decode + add"}
         from rans_vectoradd.data import exponent_histogram
         xs, ys = x[:1 << 24].cpu(), y[:1 << 24].cpu()
         cpu["encode"] = cpu_encode_rates(xs, N, exponent_histogram(xs, ys).double())
 
     same_all = sum_over_ranks(1.0 if same else 0.0, ws, dev) == ws
+    del da, db, xd, yd
+    torch.cuda.empty_cache()
+
+    extras = {}
+    if not args.no_extras:
+        if rank == 0 and ws == 1:
+            extras["decode_cfg2"] = decode_cfg2(args, dev, barrier, args.steps)
+            torch.cuda.empty_cache()
+            extras["gemv_cfg3"] = gemv_cfg3(args, dev, barrier)
+            torch.cuda.empty_cache()
+        extras["stack_cfg4"] = stack_cfg4(args, ws, rank, dev, barrier)
+        torch.cuda.empty_cache()
+
     if rank == 0:
         traffic = profile_traffic(N, n)
         line = {
@@ -852,72 +1100,29 @@ def main():
             "bits_per_fp8": round(bits_per_fp8, 4),
             "algorithmic_bytes_per_step": int(total_alg),
             "hbm_frac_compressed": round(achieved / peak, 4),
+            "algorithmic_ceiling_x_raw": round(3.0 * n / total_alg, 4),
             "bit_exact_vs_raw": bool(same_all),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak,
                          "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": traffic, "peak_source": peak_kind,
-                         "kernel": "fused_split_kernel"},
+                         "kernel": "fused_pair_kernel"},
             "gpu_launches": args.steps,
+            "per_rank": {"fused_ms": [round(v, 4) for v in per_rank_ms],
+                         "fused_ms_graph_replay": [round(v, 4) for v in per_rank_graph_ms],
+                         "sm_mhz_median": per_rank_mhz,
+                         "min_median_max_ms": [round(min(per_rank_ms), 4),
+                                               round(statistics.median(per_rank_ms), 4),
+                                               round(max(per_rank_ms), 4)]},
             "clocks": clocks,
             "e2e": e2e,
             "cpu_baseline": cpu,
+            "reference_gpu": refgpu,
             "setup_s": round(setup_s, 2),
-        }
+        } | extras
         emit(line, args)
 
     if args.sweep and ws == 1:
-        sweep_hist = (torch.bincount(((xd >> 3) & 15).long(), minlength=16) +
-                      torch.bincount(((yd >> 3) & 15).long(), minlength=16)).cpu().double()
-        for n_fp8 in (2048, 8192, 32768, 131072, 1024, 4096, 16384, 65536):
-            if n_fp8 == N:
-                continue
-            del da, db
-            torch.cuda.empty_cache()
-            # the same inputs re-encoded on the device at this stream length
-            # (the device encoder's bytes equal the host encoder's)
-            from rans_vectoradd import tans_codec
-            K2 = n // n_fp8
-            ex = tans_codec.encode(xd.view(K2, n_fp8), sweep_hist, tile=8)
-            ey = tans_codec.encode(yd.view(K2, n_fp8), sweep_hist, tile=8)
-            a2 = [ex[0], ex[2], ex[1], ex[3], ex[4]]
-            b2 = [ey[0], ey[2], ey[1], ey[3], ey[4]]
-            da, db = a2, b2
-            dt2 = tans_codec.build_decode_table(ex[6].numpy(), ex[5].numpy()).to(dev)
-            ms = timed(lambda: rv.fp8_vecadd_fused_tans(*da, *db, dt2, n_fp8), args.steps,
-                       args.warmup, stream, barrier)
-            tot2, sb2 = alg_bytes(a2, b2, n)
-            ps = ms / args.steps
-            emit({"sweep": True, "n_fp8_per_stream": n_fp8, "pair_symbols": n_fp8 // 2,
-                  "streams": K2, "ms": round(ps, 4),
-                  "gbs_uncompressed_equiv": round(3.0 * n / (ps / 1e3) / 1e9, 2),
-                  "x_raw": round(raw_step / ps, 4), "bits_per_fp8": round(sb2 * 8 / (2 * n), 4),
-                  "hbm_frac_compressed": round(tot2 / (ps / 1e3) / 1e9 / peak, 4)}, args)
-            S = args.segment_pairs
-            if n_fp8 // 2 > S and (n_fp8 // 2) % S == 0 and K2 % 32 == 0:
-                # split-stream format: the same streams as n_fp8/2/S sub-streams each
-                del da, db, a2, b2
-                torch.cuda.empty_cache()
-                ex = tans_codec.encode(xd.view(K2, n_fp8), sweep_hist, tile=8, segment_pairs=S)
-                ey = tans_codec.encode(yd.view(K2, n_fp8), sweep_hist, tile=8, segment_pairs=S)
-                a2 = [ex[0], ex[2], ex[1], ex[3], ex[4]]
-                b2 = [ey[0], ey[2], ey[1], ey[3], ey[4]]
-                da, db = a2, b2
-                o = rv.fp8_vecadd_fused_tans(*da, *db, dt2, n_fp8, segment_pairs=S)
-                ok = torch.equal(o.view(n_fp8 // 16, K2, 16).permute(1, 0, 2).reshape(-1),
-                                 rv.fp8_vecadd_raw(xd, yd))
-                del o
-                ms = timed(lambda: rv.fp8_vecadd_fused_tans(*da, *db, dt2, n_fp8, segment_pairs=S),
-                           args.steps, args.warmup, stream, barrier)
-                tot2, sb2 = alg_bytes(a2, b2, n)
-                ps = ms / args.steps
-                emit({"sweep": True, "split_stream_segment_pairs": S, "n_fp8_per_stream": n_fp8,
-                      "pair_symbols": n_fp8 // 2, "streams": K2,
-                      "chains": K2 * (n_fp8 // 2 // S), "ms": round(ps, 4),
-                      "gbs_uncompressed_equiv": round(3.0 * n / (ps / 1e3) / 1e9, 2),
-                      "x_raw": round(raw_step / ps, 4),
-                      "bits_per_fp8": round(sb2 * 8 / (2 * n), 4),
-                      "hbm_frac_compressed": round(tot2 / (ps / 1e3) / 1e9 / peak, 4),
-                      "bit_exact_vs_raw": bool(ok)}, args)
+        run_sweep(args, n, N, x, y, raw_step, peak, stream, barrier, dev)
 
     if ws > 1:
         import torch.distributed as dist
