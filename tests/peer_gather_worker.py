@@ -61,7 +61,14 @@ def main():
             h = tans_gemv.gemv_gather(up, x, pg, 0, rank * fr)
             x = tans_gemv.gemv_gather(down, h, pg, 1, rank * hr)
             if record:
+                # A gathered buffer is ordered only against the next GEMV that
+                # reads it: a faster peer's next up-GEMV may already store
+                # into this rank's views[0].  Copy both buffers and hold every
+                # rank at a barrier before anyone issues the next layer.
+                torch.cuda.synchronize()
                 outs += [h.clone(), x.clone()]
+                torch.cuda.synchronize()
+                dist.barrier()
         return outs
 
     _C.data_status(dev)
