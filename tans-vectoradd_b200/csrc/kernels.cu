@@ -276,6 +276,7 @@ struct Opq {
     int32_t back;    // -128: one slab row down, in words
     int32_t back64;  // -64: one slab row down in the fused kernel's 64-unit rows
     uint32_t p26;    // 2^26: mul.hi.s32(v, p26) = v >> 6 (row of a 64-unit v)
+    uint32_t p25;    // 2^25: mul.hi.s32(v, p25) = v >> 7 (row of a 128-unit v)
     uint32_t rmask;  // (R - 1) * 64: ring row offset of a 64-unit v (set per launch)
 };
 
@@ -432,7 +433,6 @@ __device__ __forceinline__ void cp_async_wait() {
 constexpr int kRingLag = 2;
 constexpr int32_t kNoRow = -(1 << 30);  // row reported by lanes without a stream
 constexpr int kDecodeLag = 1;   // fill-group age read by the decode kernel
-constexpr int kGemvLag = 2;     // and by the GEMV kernel
 constexpr int kRingBurst = 12;  // rows filled when a group starts
 constexpr int kRingPerTile = 2; // rows filled per tile after that
 
@@ -542,6 +542,230 @@ __device__ __forceinline__ uint32_t ring_area(const uint8_t *smem, int warp, int
     return first + (uint32_t)(warp * chains) * bytes;
 }
 
+// ------------------------------------------- two-step chains and slab rings
+
+// Slab ring of the fused kernel.  Each half-warp (16 streams of one input)
+// keeps a ring of R slab rows of its 16 stream columns (64 bytes per row) in
+// shared memory; row r sits in ring row r mod R.  The warp fills it with
+// 16-byte cp.async copies: lane li of half h copies bytes 16 (li % 4) ..
+// of row fill - li / 4 of its half's block, so one instruction moves four
+// rows of both halves' rings.  A fill never overwrites a row that any lane of
+// the half may still read (rows above the slowest lane's next row minus R,
+// with one row of margin for a refill load still in flight).  After the copy
+// groups one fill old have landed (cp.async.wait_group 1, then __syncwarp so
+// that every lane sees the copies of the others), a tile may refill from the
+// ring if every row its lanes can reach is at or above that older fill
+// frontier; otherwise it waits for the newest group too, and if even that
+// does not cover it, it refills from global memory, which is always exact.
+constexpr int kPairFillRows = 4;  // rows per half filled by one copy instruction
+
+struct PairRing {
+    int32_t fill;    // next row to fill (< 0: every row is filled)
+    int32_t done0;   // lowest filled row including the newest group (INT_MIN: all rows)
+    int32_t done1;   // ... excluding it (complete once wait_group 1 returns)
+};
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool pred) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t"
+        "@p cp.async.cg.shared.global [%0], [%1], 16;\n\t}" ::"r"(dst),
+        "l"(src), "r"((uint32_t)pred)
+        : "memory");
+}
+
+// Copy the rows fill .. fill - 3 of a ring that lie above `lim` and at or
+// above row 0; returns the new fill row.  A ring row holds kUnit bytes (64:
+// 16 streams, 128: 32 streams) and is copied by kUnit / 16 lanes, 16 bytes
+// each, so the li-th lane of the ring's lanes copies piece li % (kUnit/16)
+// of row fill - li / (kUnit/16).  `src` is this lane's 16-byte piece of row 0
+// of the block (rows 512 bytes apart), `dst` its piece of ring row 0; the
+// ring row of row r is at (kUnit r) & mask (the ring is aligned to its size).
+template <int kUnit>
+__device__ __forceinline__ int32_t ring_fill16(int32_t fill, int32_t lim, bool on, int li,
+                                               const uint8_t *src, uint32_t dst, uint32_t mask) {
+    const int32_t r = fill - li / (kUnit / 16);
+    const bool go = on && r > lim && r >= 0;
+    cp_async16(dst | ((uint32_t)(r * kUnit) & mask), src + (int64_t)r * 512, go);
+    return on ? min(fill, max(fill - kPairFillRows, max(lim, -1))) : fill;
+}
+
+// Two tANS steps with one slab-exhaustion test.  Two steps consume at most 24
+// bits and the window w (bits cnt .. cnt + 31 of hi:lo) holds them all, so the
+// second step reads w << nb1; cnt < 32 before and < 56 after, so at most one
+// slab is exhausted and one refill (hi <- lo, lo <- next row) follows.  Here v
+// counts rows in units of 64 (row r: v = 64 r), matching 64-byte ring rows.
+// Shifts, adds and moves are multiplies by the opaque constants of Opq so
+// that they run on the FMA pipe; the funnel shifts and the slab test stay on
+// the ALU.
+#define TANS_STEP2_FIRST                                                                  \
+    asm("{\n\t.reg .u32 b, f;\n\t"                                                        \
+        "shf.l.wrap.b32 %0, %3, %4, %5;\n\t" /* w = top 32 bits of (hi:lo) << cnt */      \
+        "shf.l.wrap.b32 b, %0, 0, %2;\n\t"   /* bits1 = w >> (32 - nb1), 0 if nb1 = 0 */ \
+        "mul.hi.u32 f, %2, %6;\n\t"          /* e1 >> 16 */                               \
+        "mad.lo.u32 %1, b, %7, f;\n\t}"      /* entry of step 2 */                        \
+        : "=r"(w), "=r"(a1)                                                               \
+        : "r"(e1), "r"(ch.lo), "r"(ch.hi), "r"(ch.cnt), "r"(q.p16), "r"(q.step))
+
+#define TANS_STEP2_HEAD                                                            \
+    "shf.l.wrap.b32 w2, 0, %6, %5;\n\t" /* w << nb1 */                             \
+    "shf.l.wrap.b32 b, w2, 0, %7;\n\t"  /* bits2 */                                \
+    "mul.hi.u32 f, %7, %9;\n\t"                                                    \
+    "mad.lo.u32 %0, b, %10, f;\n\t"     /* next entry */                           \
+    "mad.lo.u32 c, %5, %8, %1;\n\t"     /* cnt + e1 + e2: bit 5 flips per slab */ \
+    "mad.lo.u32 c, %7, %8, c;\n\t"                                                 \
+    "xor.b32 t, c, %1;\n\t"                                                        \
+    "and.b32 t, t, 32;\n\t"                                                        \
+    "setp.ne.u32 pa, t, 0;\n\t"                                                    \
+    "mov.u32 %1, c;\n\t"
+
+// Refill from a ring of kUnit-byte rows (64: the fused kernel's half-warp
+// rings, v = 64 r; 128: a warp's 32 streams, v = 128 r): the ring row of row
+// r = v / kUnit is at (v & mask) | ring_lane, mask = (R - 1) * kUnit (the
+// ring is aligned to its size).
+template <int kUnit>
+__device__ __forceinline__ void chain_step2_ring(Chain &ch, const uint8_t *tb, uint32_t ring_lane,
+                                                 uint32_t mask, const Opq &q, uint32_t &e1,
+                                                 uint32_t &e2) {
+    e1 = *reinterpret_cast<const uint32_t *>(tb + ch.addr);
+    uint32_t w, a1;
+    TANS_STEP2_FIRST;
+    e2 = *reinterpret_cast<const uint32_t *>(tb + a1);
+    asm volatile(
+        "{\n\t.reg .u32 w2, b, f, c, t, u, sa;\n\t.reg .pred pa;\n\t" TANS_STEP2_HEAD
+        "and.b32 u, %4, %12;\n\t"
+        "or.b32 sa, u, %13;\n\t"
+        "@pa mad.lo.u32 %2, %3, %8, 0;\n\t"    /* hi <- lo */
+        "@pa ld.shared.u32 %3, [sa];\n\t"      /* lo <- next row of this stream */
+        "@pa mad.lo.s32 %4, %8, %11, %4;\n\t"  /* one row down */
+        "}"
+        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.v)
+        : "r"(e1), "r"(w), "r"(e2), "r"(q.one), "r"(q.p16), "r"(q.step),
+          "r"(kUnit == 64 ? q.back64 : q.back), "r"(mask), "r"(ring_lane));
+}
+
+// Refill from global memory (any row, any time); past the block's first row
+// nothing is loaded and lo keeps a stale word whose bits are never consumed.
+template <int kUnit>
+__device__ __forceinline__ void chain_step2_global(Chain &ch, const uint8_t *tb, const Opq &q,
+                                                   uint32_t &e1, uint32_t &e2) {
+    e1 = *reinterpret_cast<const uint32_t *>(tb + ch.addr);
+    uint32_t w, a1;
+    TANS_STEP2_FIRST;
+    e2 = *reinterpret_cast<const uint32_t *>(tb + a1);
+    asm volatile(
+        "{\n\t.reg .u32 w2, b, f, c, t;\n\t.reg .pred pa, pl;\n\t.reg .u64 ga;\n\t" TANS_STEP2_HEAD
+        "setp.ge.and.s32 pl, %4, 0, pa;\n\t"
+        "mul.wide.s32 ga, %4, %13;\n\t"   /* 512 / kUnit bytes per unit of v */
+        "add.u64 ga, ga, %12;\n\t"
+        "@pa mad.lo.u32 %2, %3, %8, 0;\n\t"    /* hi <- lo */
+        "@pl ld.global.nc.u32 %3, [ga];\n\t"   /* lo <- next row of this stream */
+        "@pa mad.lo.s32 %4, %8, %11, %4;\n\t"  /* one row down */
+        "}"
+        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.v)
+        : "r"(e1), "r"(w), "r"(e2), "r"(q.one), "r"(q.p16), "r"(q.step),
+          "r"(kUnit == 64 ? q.back64 : q.back), "l"(ch.src), "n"(512 / kUnit));
+}
+
+// NP pair steps (NP % 4 == 0), pair symbols packed four to a word.
+template <bool kRing, int NP>
+__device__ __forceinline__ void chain_tile(Chain &ch, const uint8_t *tb, uint32_t ring_lane,
+                                           const Opq &q, uint32_t (&S)[NP / 4]) {
+#pragma unroll
+    for (int j = 0; j < NP / 4; j++) {
+        uint32_t e0, e1, e2, e3;
+        if (kRing) {
+            chain_step2_ring<64>(ch, tb, ring_lane, q.rmask, q, e0, e1);
+            chain_step2_ring<64>(ch, tb, ring_lane, q.rmask, q, e2, e3);
+        } else {
+            chain_step2_global<64>(ch, tb, q, e0, e1);
+            chain_step2_global<64>(ch, tb, q, e2, e3);
+        }
+        S[j] = gather_syms(e0, e1, e2, e3);
+    }
+}
+
+// init_tans_ctx (csrc/tans_decode.cu:65-92) for 64-unit rows, with in-kernel
+// validation.  Returns the block's slab count G (0 if the metadata is
+// malformed) and in row0 the tensor row of the block's row 0 (-1 when the
+// block does not start on a 512-byte row of the buffer).
+__device__ __forceinline__ int32_t chain_init64(Chain &ch, const uint32_t *__restrict__ comp,
+                                                int64_t comp_bytes,
+                                                const int32_t *__restrict__ offsets,
+                                                const uint16_t *__restrict__ states,
+                                                const uint8_t *__restrict__ partial, int64_t sid,
+                                                uint32_t lane_off, int32_t *status, int32_t &row0) {
+    const int32_t G = chain_init(ch, comp, comp_bytes, offsets, states, partial, sid, lane_off, status);
+    const int64_t base = __ldg(offsets + sid / kBlk);
+    row0 = (G > 0 && base % 512 == 0) ? (int32_t)(base / 512) : -1;
+    ch.v = (G - 3) * 64;
+    return G;
+}
+
+// Row of a 64-unit v, on the FMA pipe (arithmetic: rows below 0 stay negative).
+__device__ __forceinline__ int32_t row_of(int32_t v, const Opq &q) {
+    int32_t r;
+    asm("mul.hi.s32 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(q.p26));
+    return r;
+}
+// Row of a 128-unit v.
+__device__ __forceinline__ int32_t row_of128(int32_t v, const Opq &q) {
+    int32_t r;
+    asm("mul.hi.s32 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(q.p25));
+    return r;
+}
+
+// Per-tile upkeep of one warp's ring of 128-byte rows (one chain per lane):
+// fill four more rows (never over a row the slowest live lane may still
+// read), then vote on whether every live lane's rows for the next 8 steps
+// (row .. row - 2) have landed; if not, wait for the newest fill and vote
+// again.  false: the tile refills from global memory.
+template <int R>
+__device__ __forceinline__ bool ring_tile128(PairRing &rg, int32_t row, bool live, bool on,
+                                             int lane, const uint8_t *src, uint32_t dst) {
+    const uint32_t full = 0xffffffffu;
+    const int32_t slow = __reduce_max_sync(full, live ? row : kNoRow);
+    const int32_t f = ring_fill16<128>(rg.fill, slow - R + 1, on, lane, src, dst,
+                                       (uint32_t)(R - 1) << 7);
+    cp_async_commit();
+    rg.done1 = rg.done0;
+    rg.done0 = f < 0 ? INT_MIN : (f < rg.fill ? f + 1 : rg.done0);
+    rg.fill = f;
+    cp_async_wait<1>();
+    __syncwarp();
+    if (__all_sync(full, !live || row - 2 >= rg.done1)) return true;
+    cp_async_wait<0>();
+    __syncwarp();
+    return __all_sync(full, !live || row - 2 >= rg.done0);
+}
+
+// Start a warp's ring for one group: row 0 of the warp's 32 stream columns is
+// taken from a live lane (all live lanes share the block); the ring serves
+// the group when that row is 16-byte aligned and the block has rows below
+// its top two, and then gets its first twelve rows at once.
+template <int R>
+__device__ __forceinline__ bool ring_start128(PairRing &rg, const Chain &ch, int32_t G, bool live,
+                                              int lane, uint32_t dst, const uint8_t *&src) {
+    const uint32_t full = 0xffffffffu;
+    const uint64_t row0 = reinterpret_cast<uint64_t>(ch.src) - 4u * (uint64_t)lane;
+    const uint32_t lv = __ballot_sync(full, live);
+    const int32_t Gw = __reduce_max_sync(full, live ? G : 0);
+    const uint64_t r = __shfl_sync(full, row0, lv ? __ffs(lv) - 1 : 0);
+    const bool on = lv != 0 && Gw >= 3 && (r & 15u) == 0;
+    src = reinterpret_cast<const uint8_t *>(r) + 16 * (lane & 7);  // unused when !on
+    rg.fill = Gw - 3;
+    rg.done0 = rg.done1 = Gw >= 3 ? Gw - 2 : INT_MIN;
+    if (on) {
+#pragma unroll
+        for (int i = 0; i < 3; i++)
+            rg.fill = ring_fill16<128>(rg.fill, -1, true, lane, src, dst, (uint32_t)(R - 1) << 7);
+        cp_async_commit();
+        cp_async_wait<0>();
+        rg.done0 = rg.done1 = rg.fill < 0 ? INT_MIN : rg.fill + 1;
+    }
+    __syncwarp();
+    return on;
+}
+
 // ---------------------------------------------------------------- decode
 
 struct DecodeArgs {
@@ -593,8 +817,8 @@ __global__ void __launch_bounds__(kDecodeMaxWarps * 32, 1) decode_kernel(const D
     const uint32_t sel2 = (qb & 1) ? 0x3715u : 0x6240u;
     const uint32_t lane_off = 4u * (lane % kCopies);
     const uint32_t mask = (uint32_t)(R - 1) << 7;
-    Ring rg;
-    rg.lane_base = ring_area<R>(smem, warp, 1) + 4u * lane;
+    const uint32_t ring = ring_area<R>(smem, warp, 1);
+    const uint32_t ring_lane = ring + 4u * lane, ring_dst = ring + 16u * (lane & 7);
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const int64_t n_groups = (p.K + 31) / 32;
     const int64_t P = p.seg_pairs, K = p.stride;
@@ -613,9 +837,9 @@ __global__ void __launch_bounds__(kDecodeMaxWarps * 32, 1) decode_kernel(const D
             G = chain_init(ch, p.comp, p.comp_bytes, p.offsets, p.states, p.partial, sid, lane_off,
                            p.status);
         const bool live = active && G > 0;
-        ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, G), live);
-        cp_async_commit();
-        cp_async_wait<0>();
+        PairRing rg;
+        const uint8_t *ring_src;
+        const bool on = ring_start128<R>(rg, ch, G, live, lane, ring_dst, ring_src);
         // Word path, for full warps when rows are 4-byte aligned: the
         // sign/mantissa bytes of 4 streams x 1 pair arrive as one word and are
         // transposed across the lane quad; the composed even/odd output words
@@ -649,17 +873,15 @@ __global__ void __launch_bounds__(kDecodeMaxWarps * 32, 1) decode_kernel(const D
                 w1n = ld_stream_u32(smw + k4);
             }
             if (t + 4 < full_tiles) prefetch_l2(smw + pf_ahead);
-            const int32_t need = ring_fill<R>(rg, ch, live);
-            cp_async_commit();
-            cp_async_wait<kDecodeLag>();
             uint32_t e[kTablePairs];
-            if (need >= rg.done[kDecodeLag]) {
+            if (ring_tile128<R>(rg, row_of128(ch.v, p.q), live, on, lane, ring_src, ring_dst)) {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++)
-                    e[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
+                for (int j = 0; j < kTablePairs; j += 2)
+                    chain_step2_ring<128>(ch, tb, ring_lane, mask, p.q, e[j], e[j + 1]);
             } else {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_global(ch, tb, p.q);
+                for (int j = 0; j < kTablePairs; j += 2)
+                    chain_step2_global<128>(ch, tb, p.q, e[j], e[j + 1]);
             }
             const uint32_t M0 = quad_transpose(w0, sel1, sel2);
             const uint32_t M1 = quad_transpose(w1, sel1, sel2);
@@ -695,17 +917,15 @@ __global__ void __launch_bounds__(kDecodeMaxWarps * 32, 1) decode_kernel(const D
         // Byte path: the rest of the stream (all of it for a partial warp or
         // unaligned rows), one pair at a time.
         for (int64_t i = (int64_t)full_tiles * kTablePairs; i < P; i += kTablePairs) {
-            const int32_t need = ring_fill<R>(rg, ch, live);
-            cp_async_commit();
-            cp_async_wait<kDecodeLag>();
             uint32_t s8[kTablePairs];
-            if (need >= rg.done[kDecodeLag]) {
+            if (ring_tile128<R>(rg, row_of128(ch.v, p.q), live, on, lane, ring_src, ring_dst)) {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++)
-                    s8[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
+                for (int j = 0; j < kTablePairs; j += 2)
+                    chain_step2_ring<128>(ch, tb, ring_lane, mask, p.q, s8[j], s8[j + 1]);
             } else {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++) s8[j] = chain_step_global(ch, tb, p.q);
+                for (int j = 0; j < kTablePairs; j += 2)
+                    chain_step2_global<128>(ch, tb, p.q, s8[j], s8[j + 1]);
             }
             if (active) {
 #pragma unroll
@@ -725,154 +945,6 @@ __global__ void __launch_bounds__(kDecodeMaxWarps * 32, 1) decode_kernel(const D
 }
 
 // ----------------------------------------------------------------- fused
-
-// Slab ring of the fused kernel.  Each half-warp (16 streams of one input)
-// keeps a ring of R slab rows of its 16 stream columns (64 bytes per row) in
-// shared memory; row r sits in ring row r mod R.  The warp fills it with
-// 16-byte cp.async copies: lane li of half h copies bytes 16 (li % 4) ..
-// of row fill - li / 4 of its half's block, so one instruction moves four
-// rows of both halves' rings.  A fill never overwrites a row that any lane of
-// the half may still read (rows above the slowest lane's next row minus R,
-// with one row of margin for a refill load still in flight).  After the copy
-// groups one fill old have landed (cp.async.wait_group 1, then __syncwarp so
-// that every lane sees the copies of the others), a tile may refill from the
-// ring if every row its lanes can reach is at or above that older fill
-// frontier; otherwise it waits for the newest group too, and if even that
-// does not cover it, it refills from global memory, which is always exact.
-constexpr int kPairFillRows = 4;  // rows per half filled by one copy instruction
-
-struct PairRing {
-    int32_t fill;    // next row to fill (< 0: every row is filled)
-    int32_t done0;   // lowest filled row including the newest group (INT_MIN: all rows)
-    int32_t done1;   // ... excluding it (complete once wait_group 1 returns)
-};
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool pred) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.u32 p, %2, 0;\n\t"
-        "@p cp.async.cg.shared.global [%0], [%1], 16;\n\t}" ::"r"(dst),
-        "l"(src), "r"((uint32_t)pred)
-        : "memory");
-}
-
-// Copy rows fill - li/4 (li = lane % 16) of this half that lie above `lim`
-// and at or above row 0; returns the new fill row.  `src` is this lane's
-// 16-byte piece of row 0 of its half's block (rows 512 bytes apart) and
-// `dst` its piece of ring row 0; ring row of row r at (64 r) & q.rmask.
-__device__ __forceinline__ int32_t ring_fill16(int32_t fill, int32_t lim, bool on, int li,
-                                               const uint8_t *src, uint32_t dst, const Opq &q) {
-    const int32_t r = fill - (li >> 2);
-    const bool go = on && r > lim && r >= 0;
-    cp_async16(dst | ((uint32_t)(r * 64) & q.rmask), src + (int64_t)r * 512, go);
-    return on ? min(fill, max(fill - kPairFillRows, max(lim, -1))) : fill;
-}
-
-// Two tANS steps with one slab-exhaustion test.  Two steps consume at most 24
-// bits and the window w (bits cnt .. cnt + 31 of hi:lo) holds them all, so the
-// second step reads w << nb1; cnt < 32 before and < 56 after, so at most one
-// slab is exhausted and one refill (hi <- lo, lo <- next row) follows.  Here v
-// counts rows in units of 64 (row r: v = 64 r), matching 64-byte ring rows.
-// Shifts, adds and moves are multiplies by the opaque constants of Opq so
-// that they run on the FMA pipe; the funnel shifts and the slab test stay on
-// the ALU.
-#define TANS_STEP2_FIRST                                                                  \
-    asm("{\n\t.reg .u32 b, f;\n\t"                                                        \
-        "shf.l.wrap.b32 %0, %3, %4, %5;\n\t" /* w = top 32 bits of (hi:lo) << cnt */      \
-        "shf.l.wrap.b32 b, %0, 0, %2;\n\t"   /* bits1 = w >> (32 - nb1), 0 if nb1 = 0 */ \
-        "mul.hi.u32 f, %2, %6;\n\t"          /* e1 >> 16 */                               \
-        "mad.lo.u32 %1, b, %7, f;\n\t}"      /* entry of step 2 */                        \
-        : "=r"(w), "=r"(a1)                                                               \
-        : "r"(e1), "r"(ch.lo), "r"(ch.hi), "r"(ch.cnt), "r"(q.p16), "r"(q.step))
-
-#define TANS_STEP2_HEAD                                                            \
-    "shf.l.wrap.b32 w2, 0, %6, %5;\n\t" /* w << nb1 */                             \
-    "shf.l.wrap.b32 b, w2, 0, %7;\n\t"  /* bits2 */                                \
-    "mul.hi.u32 f, %7, %9;\n\t"                                                    \
-    "mad.lo.u32 %0, b, %10, f;\n\t"     /* next entry */                           \
-    "mad.lo.u32 c, %5, %8, %1;\n\t"     /* cnt + e1 + e2: bit 5 flips per slab */ \
-    "mad.lo.u32 c, %7, %8, c;\n\t"                                                 \
-    "xor.b32 t, c, %1;\n\t"                                                        \
-    "and.b32 t, t, 32;\n\t"                                                        \
-    "setp.ne.u32 pa, t, 0;\n\t"                                                    \
-    "mov.u32 %1, c;\n\t"
-
-// Refill from this half-warp's ring: the ring row of row r = v / 64 is at
-// (v & (R - 1) * 64) | ring_lane (q.rmask; the ring is aligned to its size).
-__device__ __forceinline__ void chain_step2_ring(Chain &ch, const uint8_t *tb, uint32_t ring_lane,
-                                                 const Opq &q, uint32_t &e1, uint32_t &e2) {
-    e1 = *reinterpret_cast<const uint32_t *>(tb + ch.addr);
-    uint32_t w, a1;
-    TANS_STEP2_FIRST;
-    e2 = *reinterpret_cast<const uint32_t *>(tb + a1);
-    asm volatile(
-        "{\n\t.reg .u32 w2, b, f, c, t, u, sa;\n\t.reg .pred pa;\n\t" TANS_STEP2_HEAD
-        "and.b32 u, %4, %12;\n\t"
-        "or.b32 sa, u, %13;\n\t"
-        "@pa mad.lo.u32 %2, %3, %8, 0;\n\t"    /* hi <- lo */
-        "@pa ld.shared.u32 %3, [sa];\n\t"      /* lo <- next row of this stream */
-        "@pa mad.lo.s32 %4, %8, %11, %4;\n\t"  /* one row down */
-        "}"
-        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.v)
-        : "r"(e1), "r"(w), "r"(e2), "r"(q.one), "r"(q.p16), "r"(q.step), "r"(q.back64),
-          "r"(q.rmask), "r"(ring_lane));
-}
-
-// Refill from global memory (any row, any time); past the block's first row
-// nothing is loaded and lo keeps a stale word whose bits are never consumed.
-__device__ __forceinline__ void chain_step2_global(Chain &ch, const uint8_t *tb, const Opq &q,
-                                                   uint32_t &e1, uint32_t &e2) {
-    e1 = *reinterpret_cast<const uint32_t *>(tb + ch.addr);
-    uint32_t w, a1;
-    TANS_STEP2_FIRST;
-    e2 = *reinterpret_cast<const uint32_t *>(tb + a1);
-    asm volatile(
-        "{\n\t.reg .u32 w2, b, f, c, t;\n\t.reg .pred pa, pl;\n\t.reg .u64 ga;\n\t" TANS_STEP2_HEAD
-        "setp.ge.and.s32 pl, %4, 0, pa;\n\t"
-        "mul.wide.s32 ga, %4, 8;\n\t"
-        "add.u64 ga, ga, %12;\n\t"
-        "@pa mad.lo.u32 %2, %3, %8, 0;\n\t"    /* hi <- lo */
-        "@pl ld.global.nc.u32 %3, [ga];\n\t"   /* lo <- next row of this stream */
-        "@pa mad.lo.s32 %4, %8, %11, %4;\n\t"  /* one row down */
-        "}"
-        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.v)
-        : "r"(e1), "r"(w), "r"(e2), "r"(q.one), "r"(q.p16), "r"(q.step), "r"(q.back64),
-          "l"(ch.src));
-}
-
-// NP pair steps (NP % 4 == 0), pair symbols packed four to a word.
-template <bool kRing, int NP>
-__device__ __forceinline__ void chain_tile(Chain &ch, const uint8_t *tb, uint32_t ring_lane,
-                                           const Opq &q, uint32_t (&S)[NP / 4]) {
-#pragma unroll
-    for (int j = 0; j < NP / 4; j++) {
-        uint32_t e0, e1, e2, e3;
-        if (kRing) {
-            chain_step2_ring(ch, tb, ring_lane, q, e0, e1);
-            chain_step2_ring(ch, tb, ring_lane, q, e2, e3);
-        } else {
-            chain_step2_global(ch, tb, q, e0, e1);
-            chain_step2_global(ch, tb, q, e2, e3);
-        }
-        S[j] = gather_syms(e0, e1, e2, e3);
-    }
-}
-
-// init_tans_ctx (csrc/tans_decode.cu:65-92) for 64-unit rows, with in-kernel
-// validation.  Returns the block's slab count G (0 if the metadata is
-// malformed) and in row0 the tensor row of the block's row 0 (-1 when the
-// block does not start on a 512-byte row of the buffer).
-__device__ __forceinline__ int32_t chain_init64(Chain &ch, const uint32_t *__restrict__ comp,
-                                                int64_t comp_bytes,
-                                                const int32_t *__restrict__ offsets,
-                                                const uint16_t *__restrict__ states,
-                                                const uint8_t *__restrict__ partial, int64_t sid,
-                                                uint32_t lane_off, int32_t *status, int32_t &row0) {
-    const int32_t G = chain_init(ch, comp, comp_bytes, offsets, states, partial, sid, lane_off, status);
-    const int64_t base = __ldg(offsets + sid / kBlk);
-    row0 = (G > 0 && base % 512 == 0) ? (int32_t)(base / 512) : -1;
-    ch.v = (G - 3) * 64;
-    return G;
-}
 
 struct FusedArgs {
     const uint32_t *a_comp, *b_comp;
@@ -901,13 +973,6 @@ struct FusedArgs {
 // half-warp (see PairRing).
 constexpr int kPairMaxWarps = 28;
 
-// Row of a 64-unit v, on the FMA pipe (arithmetic: rows below 0 stay negative).
-__device__ __forceinline__ int32_t row_of(int32_t v, const Opq &q) {
-    int32_t r;
-    asm("mul.hi.s32 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(q.p26));
-    return r;
-}
-
 // Per-tile ring upkeep: fill up to four rows of each half's ring, then vote
 // on whether every lane's rows for this tile (down to row - 5: 16 steps read
 // at most 6 slabs) are in landed fills.
@@ -917,7 +982,7 @@ __device__ __forceinline__ bool ring_tile(PairRing &rg, int32_t row, bool live, 
     const uint32_t full = 0xffffffffu;
     const int32_t sa = __reduce_max_sync(full, (h == 0 && (kAll || live)) ? row : kNoRow);
     const int32_t sb = __reduce_max_sync(full, (h == 1 && (kAll || live)) ? row : kNoRow);
-    const int32_t f = ring_fill16(rg.fill, (h ? sb : sa) - R + 1, on, li, src, dst, q);
+    const int32_t f = ring_fill16<64>(rg.fill, (h ? sb : sa) - R + 1, on, li, src, dst, q.rmask);
     cp_async_commit();
     rg.done1 = rg.done0;
     rg.done0 = f < 0 ? INT_MIN : (f < rg.fill ? f + 1 : rg.done0);
@@ -1066,7 +1131,7 @@ __global__ void __launch_bounds__(kPairMaxWarps * 32, 1)
         if (on) {
             // the first rows: three fills of four, then wait for all of them
 #pragma unroll
-            for (int k = 0; k < 3; k++) rg.fill = ring_fill16(rg.fill, -1, true, li, fsrc, fdst, p.q);
+            for (int k = 0; k < 3; k++) rg.fill = ring_fill16<64>(rg.fill, -1, true, li, fsrc, fdst, p.q.rmask);
             cp_async_commit();
             cp_async_wait<0>();
             rg.done0 = rg.done1 = rg.fill < 0 ? INT_MIN : rg.fill + 1;
@@ -1178,18 +1243,21 @@ __device__ __forceinline__ void mma_16x8x16(float (&d)[4], uint32_t a0, uint32_t
 
 // Uncompressed e4m3 GEMV (the decode-GEMV's denominator): the same sum with
 // the same mma.sync f16 path and the same column-slice reduction, W read as
-// plain e4m3 bytes [R][C].  A warp owns 16 rows of one column slice; per
-// 64-column chunk lane (g, t) loads 16 contiguous bytes of rows g and g + 8
-// (columns 16t .. 16t + 15).  Inside a chunk the MMA k index is permuted:
-// in step s, lane t's k = 2t, 2t+1 / 2t+8, 2t+9 are columns 16t + 4s + 0, 1 /
-// 2, 3, and the x (B) fragment follows the same permutation, so every
-// product w[r][c] * x[b][c] is summed exactly once.  Two chunks are in
-// flight per warp (4 KiB of W per warp).
-constexpr int kRawGemvWarps = 8;  // row groups (16 rows each) per CTA
+// plain e4m3 bytes [R][C].  A warp owns 16 rows of one column slice at a
+// time; per 64-column chunk lane (g, t) loads 16 contiguous bytes of rows g
+// and g + 8 (columns 16t .. 16t + 15).  Inside a chunk the MMA k index is
+// permuted: in step s, lane t's k = 2t, 2t+1 / 2t+8, 2t+9 are columns
+// 16t + 4s + 0, 1 / 2, 3, and the x (B) fragment follows the same
+// permutation, so every product w[r][c] * x[b][c] is summed exactly once.
+// The grid is persistent (two CTAs per SM); each warp walks its row groups
+// chunk by chunk with four chunks (4 KiB of W) in flight, the first four
+// issued before x is staged.
+constexpr int kRawGemvWarps = 8;  // warps per CTA
+constexpr int kRawGemvDepth = 4;  // chunks in flight per warp
 
 struct RawGemvArgs {
     const uint8_t *w;       // e4m3 [R][C]
-    const uint16_t *x;      // bf16 [B][C]
+    const uint16_t *x;      // bf16 [B][C] (16-byte aligned)
     float *part;            // f32 [KS][B][R]
     int64_t R, C, B, KS;
 };
@@ -1206,57 +1274,93 @@ __device__ __forceinline__ void raw_chunk(float (&acc)[4], uint4 wa, uint4 wb, c
                     xv[2 * s + 1]);
 }
 
-__global__ void __launch_bounds__(kRawGemvWarps * 32) gemv_raw_kernel(const RawGemvArgs p) {
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t v) {
+    const __half2 h = __floats2half2_rn(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+__global__ void __launch_bounds__(kRawGemvWarps * 32, 2) gemv_raw_kernel(const RawGemvArgs p) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int64_t CS = p.C / p.KS;
     const int k = blockIdx.y;
-    const int64_t pitch = CS + 8;  // halves
+    const int64_t pitch = CS + 8;  // halves (rows stay 16-byte aligned)
     uint16_t *xs = reinterpret_cast<uint16_t *>(smem);
-    // x slice -> f16 in shared memory (rows >= B are zero)
-    for (int b = 0; b < kGemvMaxBatch; b++) {
-        const uint16_t *xr = p.x + b * p.C + k * CS;
-        for (int32_t c = threadIdx.x; c < (int32_t)CS; c += blockDim.x) {
-            const float v = b < p.B ? __uint_as_float((uint32_t)xr[c] << 16) : 0.f;
-            xs[b * pitch + c] = __half_as_ushort(__float2half_rn(v));
-        }
-    }
-    __syncthreads();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int64_t r0 = ((int64_t)blockIdx.x * kRawGemvWarps + warp) * 16;
-    if (r0 >= p.R) return;
-    const uint8_t *w0 = p.w + (r0 + g) * p.C + k * CS + 16 * t;
-    const uint8_t *w1 = w0 + 8 * p.C;
+    const int64_t groups = p.R / 16, gstride = (int64_t)gridDim.x * kRawGemvWarps;
+    const int64_t rg0 = (int64_t)blockIdx.x * kRawGemvWarps + warp;
+    const int32_t nch = (int32_t)(CS / 64);
+    const int32_t items = rg0 < groups ? (int32_t)((groups - rg0 + gstride - 1) / gstride) * nch : 0;
+    // W of row g (and g + 8), this lane's 16 bytes, column slice k, row group 0
+    const uint8_t *wk = p.w + (int64_t)g * p.C + k * CS + 16 * t;
+    const int64_t wrow8 = 8 * p.C, wgrp = 16 * p.C;
+    int64_t l_rg = rg0;
+    int32_t l_c = 0;
+    uint4 A[kRawGemvDepth], B[kRawGemvDepth];
+#pragma unroll
+    for (int u = 0; u < kRawGemvDepth; u++) {
+        A[u] = B[u] = make_uint4(0, 0, 0, 0);
+        if (u < items) {
+            const uint8_t *q = wk + l_rg * wgrp + 64 * l_c;
+            A[u] = ld_stream_v4(q);
+            B[u] = ld_stream_v4(q + wrow8);
+        }
+        if (++l_c == nch) {
+            l_c = 0;
+            l_rg += gstride;
+        }
+    }
+    // x slice -> f16 in shared memory, eight columns per 16-byte load (rows
+    // >= B are zero), while the first chunks of W are in flight
+    const int64_t c8 = CS / 8;
+    for (int64_t i = threadIdx.x; i < kGemvMaxBatch * c8; i += blockDim.x) {
+        const int64_t b = i / c8, c = (i - b * c8) * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (b < p.B) {
+            const uint4 r = *reinterpret_cast<const uint4 *>(p.x + b * p.C + k * CS + c);
+            v = make_uint4(bf16x2_to_f16x2(r.x), bf16x2_to_f16x2(r.y), bf16x2_to_f16x2(r.z),
+                           bf16x2_to_f16x2(r.w));
+        }
+        *reinterpret_cast<uint4 *>(xs + b * pitch + c) = v;
+    }
+    __syncthreads();
     const uint16_t *xp = xs + g * pitch + 16 * t;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    const int32_t nch = (int32_t)(CS / 64);
-    uint4 a0 = ld_stream_v4(w0), b0 = ld_stream_v4(w1), a1 = a0, b1 = b0;
-    if (nch > 1) {
-        a1 = ld_stream_v4(w0 + 64);
-        b1 = ld_stream_v4(w1 + 64);
-    }
-    for (int32_t j = 0; j < nch; j += 2) {
-        const uint4 ca0 = a0, cb0 = b0, ca1 = a1, cb1 = b1;
-        if (j + 2 < nch) {
-            a0 = ld_stream_v4(w0 + 64 * (j + 2));
-            b0 = ld_stream_v4(w1 + 64 * (j + 2));
-        }
-        if (j + 3 < nch) {
-            a1 = ld_stream_v4(w0 + 64 * (j + 3));
-            b1 = ld_stream_v4(w1 + 64 * (j + 3));
-        }
-        raw_chunk(acc, ca0, cb0, xp + 64 * j);
-        if (j + 1 < nch) raw_chunk(acc, ca1, cb1, xp + 64 * (j + 1));
-    }
-    // D fragment: rows g, g + 8; batch columns 2t, 2t + 1
+    int64_t c_rg = rg0;
+    int32_t c_c = 0;
     float *pk = p.part + (int64_t)k * p.B * p.R;
-    if (2 * t < p.B) {
-        pk[(2 * t) * p.R + r0 + g] = acc[0];
-        pk[(2 * t) * p.R + r0 + g + 8] = acc[2];
-    }
-    if (2 * t + 1 < p.B) {
-        pk[(2 * t + 1) * p.R + r0 + g] = acc[1];
-        pk[(2 * t + 1) * p.R + r0 + g + 8] = acc[3];
+    for (int32_t i = 0; i < items; i += kRawGemvDepth) {
+#pragma unroll
+        for (int u = 0; u < kRawGemvDepth; u++) {
+            if (i + u < items) {
+                const uint4 a = A[u], b = B[u];
+                if (i + u + kRawGemvDepth < items) {
+                    const uint8_t *q = wk + l_rg * wgrp + 64 * l_c;
+                    A[u] = ld_stream_v4(q);
+                    B[u] = ld_stream_v4(q + wrow8);
+                }
+                if (++l_c == nch) {
+                    l_c = 0;
+                    l_rg += gstride;
+                }
+                raw_chunk(acc, a, b, xp + 64 * c_c);
+                if (++c_c == nch) {
+                    // D fragment: rows g, g + 8; batch columns 2t, 2t + 1
+                    const int64_t r0 = c_rg * 16;
+                    if (2 * t < p.B) {
+                        pk[(2 * t) * p.R + r0 + g] = acc[0];
+                        pk[(2 * t) * p.R + r0 + g + 8] = acc[2];
+                    }
+                    if (2 * t + 1 < p.B) {
+                        pk[(2 * t + 1) * p.R + r0 + g] = acc[1];
+                        pk[(2 * t + 1) * p.R + r0 + g + 8] = acc[3];
+                    }
+                    acc[0] = acc[1] = acc[2] = acc[3] = 0.f;
+                    c_c = 0;
+                    c_rg += gstride;
+                }
+            }
+        }
     }
 }
 
@@ -1299,20 +1403,25 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
     const uint32_t lane_off = 4u * (lane % kCopies);
     const uint32_t mask = (uint32_t)(R - 1) << 7;
     const uint32_t xbytes = ((uint32_t)(kGemvMaxBatch * pitch * 2) + 127u) & ~127u;
-    Ring ra, rb;
+    // two rings per warp (chain a: rows g, chain b: rows g + 8), R rows of the
+    // warp's 32 stream columns (128 bytes per row) each
+    uint32_t ring_a, ring_b;
     {
         const uint32_t bytes = R * 128u;
         const uint32_t first =
             (smem_addr(smem) + kTableBytes + xbytes + bytes - 1) & ~(bytes - 1);
-        ra.lane_base = first + (uint32_t)(warp * 2) * bytes + 4u * lane;
-        rb.lane_base = ra.lane_base + bytes;
+        ring_a = first + (uint32_t)(warp * 2) * bytes;
+        ring_b = ring_a + bytes;
     }
+    const uint32_t lane_a = ring_a + 4u * lane, lane_b = ring_b + 4u * lane;
+    const uint32_t dst_a = ring_a + 16u * (lane & 7), dst_b = ring_b + 16u * (lane & 7);
     const int64_t K = p.R * 4 * p.KS;  // streams
     const int64_t N = CS / 4;          // fp8 per stream
     const int32_t n_tiles = (int32_t)(N / 16);  // CS / 64
     const int64_t groups = p.R / 16;
     const uint32_t *xw = reinterpret_cast<const uint32_t *>(xs) + g * (pitch / 2) + t;
     const int64_t tstep = K * 8, pf_ahead = 3 * tstep;  // sign/mantissa bytes per tile row
+    const uint32_t full = 0xffffffffu;
     for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; w < groups;
          w += (int64_t)gridDim.x * (blockDim.x >> 5)) {
         const int64_t sa_id = ((w * p.KS + k) * 2 + 0) * 32 + lane;
@@ -1323,14 +1432,37 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
         const int32_t gb = chain_init(cb, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
                                       sb_id, lane_off, p.status);
         const bool live = ga > 0 && gb > 0;
+        // row 0 of each chain's 32 stream columns, copied 16 bytes at a time
+        // when every lane is live and it is 16-byte aligned
+        const uintptr_t r0a = reinterpret_cast<uintptr_t>(ca.src) - 4u * lane;
+        const uintptr_t r0b = reinterpret_cast<uintptr_t>(cb.src) - 4u * lane;
+        const int32_t Ga = __reduce_max_sync(full, live ? ga : 0);
+        const int32_t Gb = __reduce_max_sync(full, live ? gb : 0);
+        const bool on = __all_sync(full, live && ((r0a | r0b) & 15u) == 0);
         if (!live) {
             chain_idle(ca, p.comp);
             chain_idle(cb, p.comp);
         }
-        ring_start<R>(ra, ca, __reduce_max_sync(0xffffffffu, live ? ga : 0), live);
-        ring_start<R>(rb, cb, __reduce_max_sync(0xffffffffu, live ? gb : 0), live);
-        cp_async_commit();
-        cp_async_wait<0>();
+        const uint8_t *src_a = reinterpret_cast<const uint8_t *>(r0a) + 16 * (lane & 7);
+        const uint8_t *src_b = reinterpret_cast<const uint8_t *>(r0b) + 16 * (lane & 7);
+        PairRing ra, rb;
+        ra.fill = Ga - 3;
+        rb.fill = Gb - 3;
+        ra.done0 = ra.done1 = Ga >= 3 ? Ga - 2 : INT_MIN;
+        rb.done0 = rb.done1 = Gb >= 3 ? Gb - 2 : INT_MIN;
+        if (on) {
+            // the first rows: three fills of four per chain, then wait for all
+#pragma unroll
+            for (int i = 0; i < 3; i++) {
+                ra.fill = ring_fill16<128>(ra.fill, -1, true, lane, src_a, dst_a, mask);
+                rb.fill = ring_fill16<128>(rb.fill, -1, true, lane, src_b, dst_b, mask);
+            }
+            cp_async_commit();
+            cp_async_wait<0>();
+            ra.done0 = ra.done1 = ra.fill < 0 ? INT_MIN : ra.fill + 1;
+            rb.done0 = rb.done1 = rb.fill < 0 ? INT_MIN : rb.fill + 1;
+        }
+        __syncwarp();
         float d[4] = {0.f, 0.f, 0.f, 0.f};
         uint2 sa_n = make_uint2(0, 0), sb_n = make_uint2(0, 0);
         // running pointers: this tile's sign/mantissa words and x fragments
@@ -1352,22 +1484,41 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
                 prefetch_l2(spa + pf_ahead);
                 prefetch_l2(spb + pf_ahead);
             }
-            const int32_t need_a = ring_fill<R>(ra, ca, live);
-            const int32_t need_b = ring_fill<R>(rb, cb, live);
+            // ring upkeep: four more rows per chain (never over a row the
+            // slowest lane may still read), then vote on this tile's rows
+            // (8 steps read at most 3 slabs: row .. row - 2)
+            const int32_t rowa = row_of128(ca.v, p.q), rowb = row_of128(cb.v, p.q);
+            const int32_t slow_a = __reduce_max_sync(full, live ? rowa : kNoRow);
+            const int32_t slow_b = __reduce_max_sync(full, live ? rowb : kNoRow);
+            const int32_t fa = ring_fill16<128>(ra.fill, slow_a - R + 1, on, lane, src_a, dst_a, mask);
+            const int32_t fb = ring_fill16<128>(rb.fill, slow_b - R + 1, on, lane, src_b, dst_b, mask);
             cp_async_commit();
-            cp_async_wait<kGemvLag>();
+            ra.done1 = ra.done0;
+            rb.done1 = rb.done0;
+            ra.done0 = fa < 0 ? INT_MIN : (fa < ra.fill ? fa + 1 : ra.done0);
+            rb.done0 = fb < 0 ? INT_MIN : (fb < rb.fill ? fb + 1 : rb.done0);
+            ra.fill = fa;
+            rb.fill = fb;
+            cp_async_wait<1>();
+            __syncwarp();
+            bool fast = __all_sync(full, !live || (rowa - 2 >= ra.done1 && rowb - 2 >= rb.done1));
+            if (!fast) {
+                cp_async_wait<0>();
+                __syncwarp();
+                fast = __all_sync(full, !live || (rowa - 2 >= ra.done0 && rowb - 2 >= rb.done0));
+            }
             uint32_t ea[kTablePairs], eb[kTablePairs];
-            if (need_a >= ra.done[kGemvLag] && need_b >= rb.done[kGemvLag]) {
+            if (fast) {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++) {
-                    ea[j] = chain_step_ring(ca, tb, ra.lane_base, mask, p.q);
-                    eb[j] = chain_step_ring(cb, tb, rb.lane_base, mask, p.q);
+                for (int j = 0; j < kTablePairs; j += 2) {
+                    chain_step2_ring<128>(ca, tb, lane_a, mask, p.q, ea[j], ea[j + 1]);
+                    chain_step2_ring<128>(cb, tb, lane_b, mask, p.q, eb[j], eb[j + 1]);
                 }
             } else {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++) {
-                    ea[j] = chain_step_global(ca, tb, p.q);
-                    eb[j] = chain_step_global(cb, tb, p.q);
+                for (int j = 0; j < kTablePairs; j += 2) {
+                    chain_step2_global<128>(ca, tb, p.q, ea[j], ea[j + 1]);
+                    chain_step2_global<128>(cb, tb, p.q, eb[j], eb[j + 1]);
                 }
             }
             uint32_t wa[4], wb[4];
@@ -2008,6 +2159,7 @@ Opq make_opq() {
     q.back = -kBlk;
     q.back64 = -64;
     q.p26 = 1u << 26;
+    q.p25 = 1u << 25;
     q.rmask = 0;
     return q;
 }
@@ -2494,8 +2646,8 @@ extern "C" int tans_b200_gemv_raw(const uint8_t *w, const float *scale, const ui
         return fail(TANS_B200_ERR_INVALID, "gemv_raw: cols must be a positive multiple of 64 * col_splits");
     if (batch < 1 || batch > kGemvMaxBatch) return fail(TANS_B200_ERR_INVALID, "gemv_raw: batch must be 1..8");
     if (!w || !scale || !x || !y || !partials) return fail(TANS_B200_ERR_INVALID, "gemv_raw: null pointer");
-    if (!aligned(w, 16) || !aligned(x, 2) || !aligned(y, 2) || !aligned(partials, 4) || !aligned(scale, 4))
-        return fail(TANS_B200_ERR_INVALID, "gemv_raw: w must be 16-byte aligned");
+    if (!aligned(w, 16) || !aligned(x, 16) || !aligned(y, 2) || !aligned(partials, 4) || !aligned(scale, 4))
+        return fail(TANS_B200_ERR_INVALID, "gemv_raw: w and x must be 16-byte aligned");
     const int64_t cs = cols / col_splits;
     const int64_t smem = kGemvMaxBatch * (cs + 8) * 2;
     if (smem > kSmemMax)
@@ -2507,7 +2659,11 @@ extern "C" int tans_b200_gemv_raw(const uint8_t *w, const float *scale, const ui
     rc = set_smem(gemv_raw_kernel, (int)smem);
     if (rc) return rc;
     RawGemvArgs args{w, x, partials, rows, cols, batch, col_splits};
-    const dim3 grid((unsigned)((rows / 16 + kRawGemvWarps - 1) / kRawGemvWarps), (unsigned)col_splits);
+    // persistent: two CTAs per SM over all column slices
+    int64_t gx = (rows / 16 + kRawGemvWarps - 1) / kRawGemvWarps;
+    const int64_t cap = (2 * (int64_t)sms + col_splits - 1) / col_splits;
+    if (gx > cap) gx = cap;
+    const dim3 grid((unsigned)gx, (unsigned)col_splits);
     cudaStream_t st = (cudaStream_t)stream;
     gemv_raw_kernel<<<grid, kRawGemvWarps * 32, (int)smem, st>>>(args);
     rc = launch_status("gemv_raw_kernel");
