@@ -1249,9 +1249,11 @@ __device__ __forceinline__ void mma_16x8x16(float (&d)[4], uint32_t a0, uint32_t
 // permuted: in step s, lane t's k = 2t, 2t+1 / 2t+8, 2t+9 are columns
 // 16t + 4s + 0, 1 / 2, 3, and the x (B) fragment follows the same
 // permutation, so every product w[r][c] * x[b][c] is summed exactly once.
-// The grid is persistent (two CTAs per SM); each warp walks its row groups
-// chunk by chunk with four chunks (4 KiB of W) in flight, the first four
-// issued before x is staged.
+// Each warp walks its row groups chunk by chunk with four chunks (4 KiB of
+// W) in flight, the first four issued before x is staged.  Every warp
+// instruction reads 64-byte pieces of 8 rows; that access pattern, not the
+// grid shape, bounds it near 3 TB/s (a sweep of column splits and grid caps
+// on [17408 x 5120] and [5120 x 17408] all landed at 31-33 us).
 constexpr int kRawGemvWarps = 8;  // warps per CTA
 constexpr int kRawGemvDepth = 4;  // chunks in flight per warp
 
@@ -1279,7 +1281,7 @@ __device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t v) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-__global__ void __launch_bounds__(kRawGemvWarps * 32, 2) gemv_raw_kernel(const RawGemvArgs p) {
+__global__ void __launch_bounds__(kRawGemvWarps * 32, 3) gemv_raw_kernel(const RawGemvArgs p) {
     extern __shared__ __align__(16) uint8_t smem[];
     const int64_t CS = p.C / p.KS;
     const int k = blockIdx.y;
@@ -2659,10 +2661,7 @@ extern "C" int tans_b200_gemv_raw(const uint8_t *w, const float *scale, const ui
     rc = set_smem(gemv_raw_kernel, (int)smem);
     if (rc) return rc;
     RawGemvArgs args{w, x, partials, rows, cols, batch, col_splits};
-    // persistent: two CTAs per SM over all column slices
-    int64_t gx = (rows / 16 + kRawGemvWarps - 1) / kRawGemvWarps;
-    const int64_t cap = (2 * (int64_t)sms + col_splits - 1) / col_splits;
-    if (gx > cap) gx = cap;
+    const int64_t gx = (rows / 16 + kRawGemvWarps - 1) / kRawGemvWarps;
     const dim3 grid((unsigned)gx, (unsigned)col_splits);
     cudaStream_t st = (cudaStream_t)stream;
     gemv_raw_kernel<<<grid, kRawGemvWarps * 32, (int)smem, st>>>(args);

@@ -274,10 +274,11 @@ def gemm_tc(weight: EncodedWeight, x: torch.Tensor, out: torch.Tensor | None = N
 
 def raw_col_splits(rows: int, cols: int, sms: int = 148) -> int:
     """Column slices of the uncompressed GEMV: the fewest that divide the
-    64-column chunks and give at least four 128-row CTAs per SM."""
+    64-column chunks and give about 4.5 CTAs (128 rows each) per SM (best of
+    a sweep over slices and grid shapes on the cfg3 matrices)."""
     chunks = cols // 64
     for d in range(1, chunks + 1):
-        if chunks % d == 0 and (rows + 127) // 128 * d >= 4 * sms:
+        if chunks % d == 0 and (rows + 127) // 128 * d * 2 >= 9 * sms:
             return d
     return chunks
 
@@ -293,6 +294,8 @@ def gemv_raw(w8: torch.Tensor, scale: torch.Tensor, x: torch.Tensor,
          "w8 must be a contiguous CUDA uint8 [rows, cols] tensor of e4m3 bits")
     _req(x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(),
          "x must be a contiguous CUDA bfloat16 [batch, cols] tensor")
+    if x.data_ptr() % 16:
+        x = x.clone()  # 16-byte aligned copy for the vector loads
     R, C = w8.shape
     B = x.shape[0]
     _req(x.shape[1] == C, f"x has {x.shape[1]} columns, the weight {C}")
