@@ -871,7 +871,7 @@ def run_stack(args, ws, rank, dev, barrier):
 
 # ------------------------------------------------------------------- main
 
-def run_sweep(args, n, N, x, y, raw_step, peak, stream, barrier, dev):
+def run_sweep(args, n, N, x, y, raw_step, peak, stream, barrier, dev, emit_lines=True):
     """Stream-length sweep (cfg1's 1K/4K/16K/64K pair-symbol and fp8 readings):
     the same inputs re-encoded on the device at each length, plain format
     and, for streams longer than --segment-pairs, split streams."""
@@ -881,6 +881,7 @@ def run_sweep(args, n, N, x, y, raw_step, peak, stream, barrier, dev):
     hist = (torch.bincount(((xd >> 3) & 15).long(), minlength=16) +
             torch.bincount(((yd >> 3) & 15).long(), minlength=16)).cpu().double()
     raw = rv.fp8_vecadd_raw(xd, yd)
+    lines = []
     for n_fp8 in (2048, 8192, 32768, 131072, 1024, 4096, 16384, 65536):
         if n_fp8 == N:
             continue
@@ -910,9 +911,36 @@ def run_sweep(args, n, N, x, y, raw_step, peak, stream, barrier, dev):
             if S:
                 line["split_stream_segment_pairs"] = S
                 line["chains"] = K2 * (n_fp8 // 2 // S)
-            emit(line, args)
+            lines.append(line)
+            if emit_lines:
+                emit(line, args)
             del a2, b2, ex, ey
             torch.cuda.empty_cache()
+    del xd, yd, raw
+    torch.cuda.empty_cache()
+    return lines
+
+
+def host_copy_ceiling(h2d_bytes, d2h_bytes, steps, stream, barrier, dev, ws):
+    """The PCIe ceiling under the e2e number: the same byte counts copied
+    pinned host -> device and device -> host concurrently (two streams, no
+    kernel), on every rank at the same time; GB/s of the e2e metric (3 bytes
+    per output element) that copies alone would allow, max time over ranks."""
+    hin = torch.empty(h2d_bytes, dtype=torch.uint8).pin_memory()
+    hout = torch.empty(d2h_bytes, dtype=torch.uint8).pin_memory()
+    din = torch.empty(h2d_bytes, dtype=torch.uint8, device=dev)
+    dout = torch.empty(d2h_bytes, dtype=torch.uint8, device=dev)
+    s2 = torch.cuda.Stream(dev)
+
+    def step():
+        s2.wait_stream(stream)
+        din.copy_(hin, non_blocking=True)
+        with torch.cuda.stream(s2):
+            hout.copy_(dout, non_blocking=True)
+        stream.wait_stream(s2)
+    ms = max_over_ranks(timed(step, steps, 2, stream, barrier) / steps, ws, dev)
+    del hin, hout, din, dout
+    return ms
 
 
 def all_ranks(v, ws, dev):
@@ -1053,6 +1081,11 @@ def main():
                    hout, rv.fp8_vecadd_fused_tans(*da, *db, dtbl, N).cpu())),
                "api": "rans_vectoradd._C.fp8_vecadd_fused_tans_host (tans_b200_fp8_vecadd_fused_host)"}
         del ha, hb, hout
+        ms_copy = host_copy_ceiling(int(h2d), int(n), e_steps, stream, barrier, dev, ws)
+        e2e["host_copy_ceiling"] = {
+            "gbs": round(3.0 * n * ws / (ms_copy / 1e3) / 1e9, 3), "ms_per_step": round(ms_copy, 4),
+            "frac": round((ms_copy / 1e3) / (ms_e2e / e_steps / 1e3), 4),
+            "what": "the step's H2D and D2H bytes copied concurrently on all ranks, no kernel"}
 
     cpu = None
     if rank == 0 and ws == 1 and not args.no_cpu:
@@ -1084,6 +1117,13 @@ def main():
             torch.cuda.empty_cache()
         extras["stack_cfg4"] = stack_cfg4(args, ws, rank, dev, barrier)
         torch.cuda.empty_cache()
+        if rank == 0 and ws == 1 and not args.sweep:
+            # cfg1's stream-length sweep (fewer steps per length)
+            sw = argparse.Namespace(**vars(args))
+            sw.steps = max(3, args.steps // 4)
+            sw.warmup = 2
+            extras["sweep"] = run_sweep(sw, n, N, x, y, raw_step, peak, stream, barrier, dev,
+                                        emit_lines=False)
 
     if rank == 0:
         traffic = profile_traffic(N, n)

@@ -1019,10 +1019,7 @@ __device__ __forceinline__ void pair_group(const FusedArgs &p, Chain &ch, PairRi
             mo_n = ld_stream_v2(so);
             mx_n = ld_stream_v2(sx);
         }
-        if ((kAll || live) && t + 3 < n16) {
-            prefetch_l2(so + 4 * t8);
-            prefetch_l2(sx + 4 * t8);
-        }
+        // (no L2 prefetch further ahead: it cost 6 % on cfg1)
         uint32_t S[4];
         if (ring_tile<R, kAll>(rg, row_of(ch.v, p.q), live, on, h, li, fsrc, fdst, p.q))
             chain_tile<true, 16>(ch, tb, ring_lane, p.q, S);
