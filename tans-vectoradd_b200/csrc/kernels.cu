@@ -1419,7 +1419,7 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
     const int32_t n_tiles = (int32_t)(N / 16);  // CS / 64
     const int64_t groups = p.R / 16;
     const uint32_t *xw = reinterpret_cast<const uint32_t *>(xs) + g * (pitch / 2) + t;
-    const int64_t tstep = K * 8, pf_ahead = 3 * tstep;  // sign/mantissa bytes per tile row
+    const int64_t tstep = K * 8;  // sign/mantissa bytes per tile row
     const uint32_t full = 0xffffffffu;
     for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; w < groups;
          w += (int64_t)gridDim.x * (blockDim.x >> 5)) {
@@ -1478,10 +1478,6 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
             if (live && tt + 1 < n_tiles) {
                 sa_n = ld_stream_v2(spa);
                 sb_n = ld_stream_v2(spb);
-            }
-            if (live && tt + 4 < n_tiles) {
-                prefetch_l2(spa + pf_ahead);
-                prefetch_l2(spb + pf_ahead);
             }
             // ring upkeep: four more rows per chain (never over a row the
             // slowest lane may still read), then vote on this tile's rows
