@@ -48,6 +48,7 @@
 
 #include <climits>
 #include <mutex>
+#include <utility>
 
 namespace tans_b200 {
 int fail(int code, const char *fmt, ...);
@@ -91,6 +92,15 @@ __device__ __forceinline__ uint2 ld_stream_v2(const void *p) {
 __device__ __forceinline__ void prefetch_l2(const void *p) {
     asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
+
+// Programmatic dependent launch (the GEMV chain: GEMV -> reduce or publish ->
+// next GEMV).  A kernel lets the next one in its stream start as soon as all
+// of its own CTAs are running, so the next kernel's prologue (table load)
+// overlaps its tail; the next kernel waits for this one to complete, with
+// its memory visible, before it reads anything this one writes.  Every
+// global write of these kernels comes after their wait.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t ld_stream_u32(const void *p) {
     uint32_t v;
@@ -1377,12 +1387,16 @@ constexpr int kGemvMaxWarps = 20;
 template <int R>
 __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvArgs p) {
     extern __shared__ __align__(16) uint8_t smem[];
+    pdl_trigger();
+    // the table is this weight's own (not written by the kernel before this
+    // one): load it while that kernel may still run, then wait for it
+    load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
+    pdl_wait();
     if (p.wait_n > 0) {  // x is gathered by the peers' epilogues: wait for all of them
         if (threadIdx.x == 0 && !peer_wait(p.wait_flags, *p.wait_seq, p.wait_n) && p.status)
             atomicOr(p.status, TANS_B200_DATA_TIMEOUT);
         __syncthreads();
     }
-    load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
     const int64_t CS = p.C / p.KS;
     const int k = blockIdx.y;
     const int64_t pitch = CS + 8;  // halves
@@ -1563,6 +1577,8 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
 // y[b][r] = bf16(scale[r] * sum_k part[k][b][r]) for column-sliced GEMVs.
 __global__ void gemv_reduce_kernel(const float *__restrict__ part, const float *__restrict__ scale,
                                    uint16_t *__restrict__ y, int64_t R, int64_t B, int64_t KS) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t n = R * B;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -1592,6 +1608,8 @@ struct PublishArgs {
 };
 
 __global__ void gemv_publish_kernel(const PublishArgs p) {
+    pdl_trigger();
+    pdl_wait();
     const int64_t half = p.R / 2, n = half * p.B, plane = p.R * p.B;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
@@ -2111,6 +2129,27 @@ int launch_status(const char *what) {
 
 bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+// Launch with programmatic stream serialisation (see pdl_trigger): the kernel
+// may start once the previous kernel in the stream has all its CTAs running
+// (at once, if that kernel does not trigger early).
+template <typename... P, typename... A>
+int launch_pdl(void (*kernel)(P...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+               const char *name, A &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<A>(args)...);
+    if (e != cudaSuccess) return fail(TANS_B200_ERR_CUDA, "%s launch: %s", name, cudaGetErrorString(e));
+    return TANS_B200_OK;
+}
+
 constexpr int kSmemMax = 227 * 1024;
 
 // Ring depth by stream length: lanes of a warp drift apart by roughly
@@ -2507,14 +2546,14 @@ static int launch_gemv_kernel(const GemvArgs &args, int sms, cudaStream_t st) {
     gx = (groups + wpc * rounds - 1) / (wpc * rounds);
     const int smem = (int)(fixed + wpc * per_warp);
     const dim3 grid((unsigned)gx, (unsigned)col_splits);
+    const dim3 block((unsigned)wpc * 32);
     switch (rr) {
-        case 16: rc = set_smem(gemv_kernel<16>, smem); if (!rc) gemv_kernel<16><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
-        case 32: rc = set_smem(gemv_kernel<32>, smem); if (!rc) gemv_kernel<32><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
-        case 64: rc = set_smem(gemv_kernel<64>, smem); if (!rc) gemv_kernel<64><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
-        default: rc = set_smem(gemv_kernel<128>, smem); if (!rc) gemv_kernel<128><<<grid, (unsigned)wpc * 32, smem, st>>>(args); break;
+        case 16: rc = set_smem(gemv_kernel<16>, smem); if (!rc) rc = launch_pdl(gemv_kernel<16>, grid, block, smem, st, "gemv_kernel", args); break;
+        case 32: rc = set_smem(gemv_kernel<32>, smem); if (!rc) rc = launch_pdl(gemv_kernel<32>, grid, block, smem, st, "gemv_kernel", args); break;
+        case 64: rc = set_smem(gemv_kernel<64>, smem); if (!rc) rc = launch_pdl(gemv_kernel<64>, grid, block, smem, st, "gemv_kernel", args); break;
+        default: rc = set_smem(gemv_kernel<128>, smem); if (!rc) rc = launch_pdl(gemv_kernel<128>, grid, block, smem, st, "gemv_kernel", args); break;
     }
-    if (rc) return rc;
-    return launch_status("gemv_kernel");
+    return rc;
 }
 
 extern "C" int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_bytes,
@@ -2550,9 +2589,9 @@ extern "C" int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_byte
     const int64_t n = rows * batch;
     const int threads = 256;
     const int64_t blocks = (n + threads - 1) / threads;
-    gemv_reduce_kernel<<<(unsigned)(blocks < 4 * sms ? blocks : 4 * sms), threads, 0, st>>>(
-        partials, scale, y, rows, batch, col_splits);
-    return launch_status("gemv_reduce_kernel");
+    return launch_pdl(gemv_reduce_kernel, dim3((unsigned)(blocks < 4 * sms ? blocks : 4 * sms)),
+                      dim3(threads), 0, st, "gemv_reduce_kernel", (const float *)partials, scale,
+                      (uint16_t *)y, rows, batch, col_splits);
 }
 
 extern "C" int tans_b200_gemv_gather(const uint8_t *compressed, int64_t compressed_bytes,
@@ -2598,8 +2637,8 @@ extern "C" int tans_b200_gemv_gather(const uint8_t *compressed, int64_t compress
     const int64_t n = rows / 2 * batch;
     const int threads = 256;
     const int64_t blocks = (n + threads - 1) / threads;
-    gemv_publish_kernel<<<(unsigned)(blocks < 2 * sms ? blocks : 2 * sms), threads, 0, st>>>(pa);
-    return launch_status("gemv_publish_kernel");
+    return launch_pdl(gemv_publish_kernel, dim3((unsigned)(blocks < 2 * sms ? blocks : 2 * sms)),
+                      dim3(threads), 0, st, "gemv_publish_kernel", pa);
 }
 
 // y[m][r] = bf16(acc[m][r] * scale[r]): the prefill epilogue after the
