@@ -701,10 +701,10 @@ def run_gemv(args, dev, barrier):
 def run_gemm(args, dev, barrier):
     """Prefill-size batches on the cfg3 weight [17408 x 5120]: the dense
     bf16 decode of the encoded weight (GB/s of e4m3 output), tans_gemv.gemm
-    (the dispatching entry), both of its large-batch forms — gemm_tc (decode
-    into shared memory + tcgen05 MMA) and gemm_dense (dense decode + library
-    bf16 GEMM with fp32 output + per-row scale) — and the GEMM alone on a
-    pre-decoded weight; rel err vs the decode-then-dense fp32 reference."""
+    (the dispatching entry: gemm_tc_kernel, W decoded into shared memory +
+    tcgen05 MMA, above 8 tokens), and for comparison gemm_dense (dense decode
+    + library bf16 GEMM with fp32 output + per-row scale) and that library
+    GEMM alone on a pre-decoded weight; rel err vs the fp32 reference."""
     from rans_vectoradd import tans_gemv
     stream = torch.cuda.current_stream(dev)
     R, C = 17408, 5120
@@ -728,21 +728,15 @@ def run_gemm(args, dev, barrier):
                          barrier) / args.steps
         ms_mm = timed(lambda: torch.mm(x, w.t(), out_dtype=torch.float32), args.steps,
                       args.warmup, stream, barrier) / args.steps
-        y_tc = tans_gemv.gemm_tc(enc, x)
-        err_tc = tans_gemv.rel_err(y_tc, tans_gemv.reference_gemv(w8, s, x))
-        ms_tc = timed(lambda: tans_gemv.gemm_tc(enc, x, y_tc), args.steps, args.warmup, stream,
-                      barrier) / args.steps
         fl = 2.0 * B * R * C
         line["batches"].append({"batch": B, "us": round(ms * 1e3, 1),
                                 "tflops": round(fl / (ms / 1e3) / 1e12, 1),
-                                "path": "tc_fused" if 8 < B <= tans_gemv.TC_MAX_BATCH else "dense",
-                                "dense_path_us": round(ms_dense * 1e3, 1),
-                                "gemm_only_us": round(ms_mm * 1e3, 1),
-                                "gemm_only_tflops": round(fl / (ms_mm / 1e3) / 1e12, 1),
+                                "path": "gemm_tc_kernel" if B > 8 else "gemv_kernel",
                                 "rel_err": err,
-                                "tc_fused_us": round(ms_tc * 1e3, 1),
-                                "tc_fused_tflops": round(fl / (ms_tc / 1e3) / 1e12, 1),
-                                "tc_fused_rel_err": err_tc})
+                                "dense_path_us": round(ms_dense * 1e3, 1),
+                                "dense_path_tflops": round(fl / (ms_dense / 1e3) / 1e12, 1),
+                                "gemm_only_us": round(ms_mm * 1e3, 1),
+                                "gemm_only_tflops": round(fl / (ms_mm / 1e3) / 1e12, 1)})
     emit(line, args)
 
 

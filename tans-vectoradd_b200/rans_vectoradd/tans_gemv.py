@@ -212,25 +212,20 @@ def dense_weight(weight: EncodedWeight, out: torch.Tensor | None = None) -> torc
 # 256-token tile, so beyond one tile the dense decode + library GEMM is
 # faster (on B200, [17408 x 5120]: 116 us vs 139 us at 256 tokens, 229 us vs
 # 158 us at 512).
-TC_MAX_BATCH = 256
-
-
-def gemm(weight: EncodedWeight, x: torch.Tensor, w_dense: torch.Tensor | None = None
-         ) -> torch.Tensor:
-    """y [batch, rows] bf16 = scale * W @ x^T for any batch: the fused GEMV
-    kernel up to batch 8; the fused decode + tensor-core kernel (`gemm_tc`)
-    up to TC_MAX_BATCH tokens when rows % 128 == 0; above that, or when a
-    decoded copy is passed in `w_dense`, the weight is decoded to dense bf16
-    (`dense_weight`) and contracted by a library bf16 GEMM with fp32 output,
-    scaled per row of W, then rounded once."""
+def gemm(weight: EncodedWeight, x: torch.Tensor) -> torch.Tensor:
+    """y [batch, rows] bf16 = scale * W @ x^T for any batch, on this
+    library's own kernels only: the fused GEMV kernel up to 8 tokens; above
+    that the fused decode + tensor-core kernel (`gemm_tc`, every token count)
+    when rows % 128 == 0, else the GEMV kernel over 8-token slices of x.  The
+    dense form (`gemm_dense`: dense bf16 decode + a library GEMM) is a
+    separate entry point and is never chosen here."""
     _req(x.is_cuda and x.dtype == torch.bfloat16 and x.dim() == 2 and x.is_contiguous(),
          "x must be a contiguous CUDA bfloat16 [batch, cols] tensor")
     if x.shape[0] <= 8:
         return gemv(weight, x)
-    if (w_dense is None and x.shape[0] <= TC_MAX_BATCH and weight.rows % 128 == 0
-            and x.data_ptr() % 16 == 0):
-        return gemm_tc(weight, x)
-    return gemm_dense(weight, x, w_dense)
+    if weight.rows % 128 == 0:
+        return gemm_tc(weight, x if x.data_ptr() % 16 == 0 else x.clone())
+    return torch.cat([gemv(weight, x[i:i + 8]) for i in range(0, x.shape[0], 8)])
 
 
 def gemm_dense(weight: EncodedWeight, x: torch.Tensor, w_dense: torch.Tensor | None = None
