@@ -420,12 +420,6 @@ __device__ __forceinline__ void cp_async4(uint32_t dst, const void *src, bool pr
         "l"(src), "r"((uint32_t)pred)
         : "memory");
 }
-// 8-byte copy; zero-fills the destination when !pred.
-__device__ __forceinline__ void cp_async8(uint32_t dst, const void *src, bool pred) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src),
-                 "r"(pred ? 8u : 0u)
-                 : "memory");
-}
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait() {
@@ -1767,9 +1761,11 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_dense_kernel(const Den
 // written out.  A CTA owns 128 rows of W and walks the columns in 64-column
 // chunks through a ring of `stages` shared-memory stages, with the work split
 // by warp role:
-//   - 16 decode warps (8 row groups x 2 chains, one tANS chain per lane):
-//     per chunk each decodes one 8-pair tile of its streams straight into the
-//     stage's bf16 A tile (K-major, 128-byte swizzle), then arrives on the
+//   - 16 decode warps (8 row groups x 2 chains, one tANS chain per lane, two
+//     steps per slab test, slab rows through a per-warp ring of 128-byte rows
+//     filled by 16-byte copies, sign/mantissa words loaded two chunks ahead
+//     into registers): per chunk each decodes one 8-pair tile of its streams
+//     straight into the stage's bf16 A tile (K-major, 128-byte swizzle), then arrives on the
 //     stage's a_full barrier.  A warp waits only for the stage to be empty
 //     (the MMAs that last read it have completed), so warps drift up to
 //     `stages` chunks apart instead of meeting at a block barrier per chunk;
@@ -1778,12 +1774,32 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) gemv_dense_kernel(const Den
 //     the stage's B tile, waits for a_full and x_full, issues four
 //     tcgen05.mma (M = 128, N = tokens, K = 16, bf16 in, fp32 accumulate in
 //     tensor memory) and commits them to the stage's `empty` barrier.
-// After the last chunk warps 0-3 read the accumulator rows back
-// (tcgen05.ld), scale, round once to bf16 and store.  Every mbarrier wait is
+// After the last chunk the 16 decode warps read the accumulator back
+// (tcgen05.ld; warp w reads lanes 32 (w % 4).. and every fourth 8-column
+// group), scale, round once to bf16 and store.  Every mbarrier wait is
 // bounded and gives up early once another warp has given up; a wait that
 // runs out ORs TANS_B200_DATA_TIMEOUT into the status word, the CTA
 // waits (bounded) for its own tensor copies still in flight, skips its
 // epilogue and frees its tensor memory.
+//
+// CTA pairs (CL = 2, batches above one tile): the decode, not the MMA,
+// bounds this kernel, so every decoded row must serve as many tokens as the
+// tensor memory holds.  Two CTAs of a cluster decode row blocks 2b and 2b + 1
+// exactly as above, each into its own stage, and the pair is one 2-SM MMA
+// (tcgen05 cta_group::2, M = 256): the first CTA's MMA thread issues it, the
+// hardware reads A rows 0-127 from the first CTA's stage and rows 128-255
+// from the second's, and x rows (the N dimension) half from each.  Per K
+// step two MMAs of mma_n tokens (<= 256 each) fill 2 * mma_n accumulator
+// columns in both CTAs' tensor memory, so one decode of W serves up to 512
+// tokens and no decoded tile is copied between the CTAs.  The second CTA's
+// MMA-warp lane loads its x rows and, once its decode warps and copies have
+// finished a chunk, arrives on the first CTA's `pair_full` barrier; the
+// first CTA's MMA thread, once the pair's MMAs of a stage are done, arrives
+// on the second CTA's `free` barrier, which its decode warps and x loads
+// wait on.  A CTA that gives up raises its partner's failure flag; cluster
+// barriers after the set-up, after the main loops and before the tensor
+// memory is freed keep either CTA from leaving while the other may still
+// read or write its shared or tensor memory.
 
 constexpr int kTcWarps = 16;                     // decode warps
 constexpr int kTcThreads = (kTcWarps + 1) * 32;  // + the MMA warp
@@ -1792,14 +1808,9 @@ constexpr int kTcMaxStages = 4;
 constexpr int kTcATile = 128 * 128;   // 128 rows x 64 bf16
 constexpr uint32_t kTcWaitLimit = 1u << 16;  // polls per wait
 constexpr uint32_t kTcPollNs = 10000;        // suspend-time hint per poll (ns): bound ~0.66 s
-constexpr int kTcLag = 3;    // cp.async groups (ring rows + sign/mantissa) in flight under the decode
-constexpr int kTcSmAhead = 3;  // chunks whose sign/mantissa words are requested ahead
-constexpr int kTcSmSlots = 4;  // their per-warp queue slots (32 lanes x 8 bytes each)
-static_assert(kTcSmAhead >= kTcLag && kTcSmSlots > kTcSmAhead, "sign/mantissa queue too short");
-static_assert((kTcSmSlots & (kTcSmSlots - 1)) == 0, "queue slots: a power of two");
 
 struct TcArgs {
-    CUtensorMap xmap;         // x [M][C] bf16: box 64 columns x nt rows, 128-byte swizzle
+    CUtensorMap xmap;         // x [M][C] bf16: box 64 columns x brows / halves rows, 128-byte swizzle
     const uint32_t *comp;
     int64_t comp_bytes;
     const int32_t *offsets;
@@ -1810,7 +1821,9 @@ struct TcArgs {
     const float *scale;       // [R]
     uint16_t *y;              // bf16 [M][R]
     int64_t R, C, KS, M;
-    int32_t nt;               // tokens per CTA (multiple of 16, <= 256)
+    int32_t brows;            // x rows (tokens) per B stage of this CTA
+    int32_t mma_n;            // tokens per MMA (multiple of 16, <= 256)
+    int32_t halves;           // MMAs per K step (accumulators of mma_n columns)
     int32_t stages;           // shared-memory stages (2..kTcMaxStages)
     int32_t *status;
     Opq q;
@@ -1834,15 +1847,26 @@ __device__ __forceinline__ uint32_t tc_swz(uint32_t row, uint32_t k) {
 // Each poll lets the hardware suspend the thread for up to kTcPollNs until
 // the phase completes, so waiting warps take no issue slots from the
 // decoding ones; the whole wait is bounded by kTcWaitLimit polls.
+// With kCluster the wait acquires at cluster scope (arrivals released by
+// other CTAs of the cluster).
+template <bool kCluster = false>
 __device__ __forceinline__ bool tc_wait(uint32_t mbar, uint32_t parity, const volatile int32_t *failed) {
     for (uint32_t i = 0; i < kTcWaitLimit; i++) {
         uint32_t done;
-        asm volatile(
-            "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2, %3;\n\t"
-            "selp.b32 %0, 1, 0, P1;\n\t}"
-            : "=r"(done)
-            : "r"(mbar), "r"(parity), "n"(kTcPollNs)
-            : "memory");
+        if constexpr (kCluster)
+            asm volatile(
+                "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P1, [%1], "
+                "%2;\n\tselp.b32 %0, 1, 0, P1;\n\t}"
+                : "=r"(done)
+                : "r"(mbar), "r"(parity)
+                : "memory");
+        else
+            asm volatile(
+                "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2, %3;\n\t"
+                "selp.b32 %0, 1, 0, P1;\n\t}"
+                : "=r"(done)
+                : "r"(mbar), "r"(parity), "n"(kTcPollNs)
+                : "memory");
         if (done) return true;
         if ((i & 15u) == 15u && failed && *failed) return false;
     }
@@ -1854,14 +1878,31 @@ __device__ __forceinline__ void tc_arrive(uint32_t mbar) {
                  : "memory");
 }
 
-// x chunk c (columns 64c..64c+63 of tokens m0..m0+nt-1) -> B tile at `dst`,
-// completing `bytes` on mbarrier `bar`.
-__device__ __forceinline__ void tc_load_x(const CUtensorMap *map, uint32_t dst, uint32_t bar,
-                                          int32_t c, int32_t m0, uint32_t bytes) {
-    asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(
-                     bar),
-                 "r"(bytes)
-                 : "memory");
+// Thread-block cluster helpers: this CTA's rank, the shared::cluster address
+// of a shared-memory address in CTA `rank`, a releasing arrive on a cluster
+// mbarrier, and a full cluster barrier (every thread of every CTA).
+__device__ __forceinline__ uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cluster_addr(uint32_t saddr, uint32_t rank) {
+    uint32_t d;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(saddr), "r"(rank));
+    return d;
+}
+__device__ __forceinline__ void tc_arrive_cluster(uint32_t mbar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(mbar) : "memory");
+}
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
+                     : "memory");
+}
+
+// One box of x (columns 64c..64c+63, tokens row..) -> shared memory at
+// `dst`, completing its bytes on mbarrier `bar` (armed by the caller).
+__device__ __forceinline__ void tc_copy_x(const CUtensorMap *map, uint32_t dst, uint32_t bar, int32_t c,
+                                          int32_t m0) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, "
         "{%2, %3}], [%4];" ::"r"(dst),
@@ -1869,36 +1910,70 @@ __device__ __forceinline__ void tc_load_x(const CUtensorMap *map, uint32_t dst, 
         : "memory");
 }
 
-template <int R>
+// Block-wide (CL = 1) or cluster-wide barrier between the main loops and the
+// epilogue, ordered after the tensor-core work of every thread.
+template <int CL>
+__device__ __forceinline__ void tc_fence_sync() {
+    if constexpr (CL > 1)
+        cluster_sync();
+    else
+        __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;");
+}
+
+template <int R, int CL>
 __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_constant__ TcArgs p) {
+    static_assert(CL == 1 || CL == 2, "one CTA or a CTA pair per MMA");
     extern __shared__ __align__(16) uint8_t smem[];
-    __shared__ __align__(8) uint64_t a_full[kTcMaxStages], x_full[kTcMaxStages], empty[kTcMaxStages];
+    __shared__ __align__(8) uint64_t a_full[kTcMaxStages], x_full[kTcMaxStages], empty[kTcMaxStages],
+        pair_full[kTcMaxStages], free_[kTcMaxStages];
     __shared__ uint32_t tmem_base_s;
     __shared__ int32_t failed_s;
     volatile int32_t *failed = &failed_s;
-    load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int S = p.stages;
+    // layout: A stages (1024-byte aligned for the swizzle), B stages, the
+    // decode warps' slab rings (each aligned to its size), the decode table
     const uint32_t base_sa = smem_addr(smem);
-    const uint32_t smq_sa = ring_area<R>(smem, kTcWarps, 1);                   // sign/mantissa queues
-    const uint32_t a_sa = (smq_sa + kTcWarps * kTcSmSlots * 256u + 1023u) & ~1023u;  // A stages
-    const uint32_t b_bytes = (uint32_t)p.nt * 128u;
-    const uint32_t b_sa = a_sa + (uint32_t)S * kTcATile;                      // B stages
+    const uint32_t a_sa = (base_sa + 1023u) & ~1023u;
+    const uint32_t b_bytes = (uint32_t)p.brows * 128u;
+    const uint32_t b_sa = a_sa + (uint32_t)S * kTcATile;
+    constexpr uint32_t ring_bytes = R * 128u;
+    const uint32_t ring0 = (b_sa + (uint32_t)S * b_bytes + ring_bytes - 1u) & ~(ring_bytes - 1u);
+    const uint32_t tbl_sa = ring0 + kTcWarps * ring_bytes;
+    load_table(reinterpret_cast<uint32_t *>(smem + (tbl_sa - base_sa)), p.table, p.status);
     const uint32_t af0 = smem_addr(&a_full[0]), xf0 = smem_addr(&x_full[0]), em0 = smem_addr(&empty[0]);
-    const uint32_t ncols = p.nt <= 32 ? 32u : (p.nt <= 64 ? 64u : (p.nt <= 128 ? 128u : 256u));
-    if (warp == 0) {
-        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
-                         smem_addr(&tmem_base_s)), "r"(ncols));
-        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
-    }
+    const uint32_t pr0 = smem_addr(&pair_full[0]), fr0 = smem_addr(&free_[0]);
+    const uint32_t acc_cols = (uint32_t)(p.halves * p.mma_n);
+    const uint32_t ncols = acc_cols <= 32 ? 32u
+                                          : (acc_cols <= 64 ? 64u
+                                                            : (acc_cols <= 128 ? 128u
+                                                                               : (acc_cols <= 256 ? 256u : 512u)));
+    const uint32_t rank = CL > 1 ? cluster_rank() : 0u;
+    const uint32_t peer = rank ^ 1u;
     if (threadIdx.x == 32 * kTcWarps) {
         for (int s = 0; s < S; s++) {
             asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(af0 + 8u * s), "r"(kTcWarps));
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(xf0 + 8u * s));
             asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(em0 + 8u * s));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(pr0 + 8u * s));
+            asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(fr0 + 8u * s));
         }
         asm volatile("fence.mbarrier_init.release.cluster;");
         failed_s = 0;
+    }
+    if constexpr (CL > 1) cluster_sync();  // the partner's barriers exist before anything arrives on them
+    if (warp == 0) {
+        if constexpr (CL > 1) {
+            // one allocation for the pair: the same columns in both CTAs' tensor memory
+            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_addr(&tmem_base_s)), "r"(ncols));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+        } else {
+            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                             smem_addr(&tmem_base_s)), "r"(ncols));
+            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+        }
     }
     asm volatile("tcgen05.fence::before_thread_sync;");
     __syncthreads();
@@ -1906,52 +1981,97 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
     const uint32_t tmem = tmem_base_s;
     const int64_t CS = p.C / p.KS, K = p.R * 4 * p.KS;
     const int32_t tps = (int32_t)(CS / 64), nchunks = (int32_t)(p.C / 64);
-    const int32_t m0 = (int32_t)blockIdx.y * p.nt;
+    const int32_t m0 = (int32_t)blockIdx.y * p.halves * p.mma_n;  // first token of this tile
+    // a give-up is seen by both CTAs of a pair
+    auto give_up = [&]() {
+        *failed = 1;
+        if constexpr (CL > 1)
+            asm volatile("st.relaxed.cluster.shared::cluster.b32 [%0], 1;" ::"r"(
+                             cluster_addr(smem_addr(&failed_s), peer))
+                         : "memory");
+    };
+    // x rows of chunk c -> B stage s: one box of all tokens (CL = 1), or per
+    // MMA half h this CTA's mma_n / 2 tokens (m0 + h mma_n + rank mma_n / 2 ..)
+    auto load_x = [&](int32_t c, int s) {
+        const uint32_t dst = b_sa + (uint32_t)s * b_bytes, bar = xf0 + 8u * (uint32_t)s;
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(b_bytes)
+                     : "memory");
+        if constexpr (CL > 1) {
+            const int32_t hb = p.mma_n / 2;
+            for (int h = 0; h < p.halves; h++)
+                tc_copy_x(&p.xmap, dst + (uint32_t)(h * hb) * 128u, bar, c, m0 + h * p.mma_n + (int32_t)rank * hb);
+        } else {
+            tc_copy_x(&p.xmap, dst, bar, c, m0);
+        }
+    };
 
-    if (warp == kTcWarps) {
-        // ------------------------------------------------ MMA warp (lane 0)
+    if (warp == kTcWarps && (CL == 1 || rank == 0)) {
+        // ------------------------------------- MMA warp (lane 0): one CTA, or the pair's leader
         if (lane == 0) {
-            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.nt >> 3) << 17) |
-                                   ((uint32_t)(128 >> 4) << 24);
+            const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(p.mma_n >> 3) << 17) |
+                                   ((uint32_t)((128 * CL) >> 4) << 24);
             bool ok = true;
             int32_t loaded = 0, consumed = 0, issued = 0;  // x chunks issued / waited for; MMA chunks
-            for (; loaded < (nchunks < S ? nchunks : S); loaded++)
-                tc_load_x(&p.xmap, b_sa + (uint32_t)loaded * b_bytes, xf0 + 8u * loaded, loaded, m0,
-                          b_bytes);
+            for (; loaded < (nchunks < S ? nchunks : S); loaded++) load_x(loaded, loaded);
             int s = 0, ps = 0;          // stage of chunk c and of chunk c - 1
             uint32_t ph = 0, pph = 0;   // their phase parities
             for (int32_t c = 0; c < nchunks && ok; c++) {
-                if (!tc_wait(af0 + 8u * s, ph, failed) || !tc_wait(xf0 + 8u * s, ph, failed)) {
-                    ok = false;
-                    break;
-                }
-                consumed = c + 1;
-                asm volatile("tcgen05.fence::after_thread_sync;");
-                const uint32_t as = a_sa + (uint32_t)s * kTcATile, bs = b_sa + (uint32_t)s * b_bytes;
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    const uint64_t ad = tc_smem_desc(as + 32u * j), bd = tc_smem_desc(bs + 32u * j);
-                    asm volatile(
-                        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-                        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(
-                            tmem),
-                        "l"(ad), "l"(bd), "r"(idesc), "r"((uint32_t)(c > 0 || j > 0)), "r"(0u), "r"(0u),
-                        "r"(0u), "r"(0u));
-                }
-                asm volatile(
-                    "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                        em0 + 8u * s)
-                    : "memory");
-                issued = c + 1;
-                // refill the stage of chunk c-1 (its MMAs were issued one chunk ago)
+                // first release the stage of chunk c - 1 once its MMAs are done
+                // (the partner's decode warps and x copies wait for this), and
+                // refill its x
                 if (c >= 1 && loaded < nchunks) {
                     if (!tc_wait(em0 + 8u * ps, pph, failed)) {
                         ok = false;
                         break;
                     }
-                    tc_load_x(&p.xmap, b_sa + (uint32_t)ps * b_bytes, xf0 + 8u * ps, loaded, m0, b_bytes);
+                    if constexpr (CL > 1) tc_arrive_cluster(cluster_addr(fr0 + 8u * ps, peer));
+                    load_x(loaded, ps);
                     loaded++;
                 }
+                if (!tc_wait(af0 + 8u * s, ph, failed) || !tc_wait(xf0 + 8u * s, ph, failed)) {
+                    ok = false;
+                    break;
+                }
+                if constexpr (CL > 1) {  // the partner's A rows and x rows of chunk c
+                    if (!tc_wait<true>(pr0 + 8u * s, ph, failed)) {
+                        ok = false;
+                        break;
+                    }
+                }
+                consumed = c + 1;
+                asm volatile("tcgen05.fence::after_thread_sync;");
+                const uint32_t as = a_sa + (uint32_t)s * kTcATile, bs = b_sa + (uint32_t)s * b_bytes;
+                for (int h = 0; h < p.halves; h++) {  // MMA half h -> accumulator columns h * mma_n
+#pragma unroll
+                    for (int j = 0; j < 4; j++) {
+                        const uint64_t ad = tc_smem_desc(as + 32u * j),
+                                       bd = tc_smem_desc(bs + (uint32_t)(h * p.mma_n / CL) * 128u + 32u * j);
+                        const uint32_t acc = (uint32_t)(c > 0 || j > 0), d = tmem + (uint32_t)(h * p.mma_n);
+                        if constexpr (CL > 1)
+                            asm volatile(
+                                "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                                "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, "
+                                "%5}, p;\n\t}" ::"r"(d),
+                                "l"(ad), "l"(bd), "r"(idesc), "r"(acc), "r"(0u));
+                        else
+                            asm volatile(
+                                "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                                "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}" ::"r"(
+                                    d),
+                                "l"(ad), "l"(bd), "r"(idesc), "r"(acc), "r"(0u));
+                    }
+                }
+                if constexpr (CL > 1)
+                    asm volatile(
+                        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                            em0 + 8u * s)
+                        : "memory");
+                else
+                    asm volatile(
+                        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                            em0 + 8u * s)
+                        : "memory");
+                issued = c + 1;
                 ps = s;
                 pph = ph;
                 if (++s == S) {
@@ -1965,7 +2085,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 if (!tc_wait(em0 + 8u * (cl % S), (uint32_t)((cl / S) & 1), failed)) ok = false;
             }
             if (!ok) {
-                *failed = 1;
+                give_up();
                 // copies and MMAs still in flight finish before the CTA frees
                 // its tensor memory and exits
                 for (int32_t c = consumed; c < loaded; c++)
@@ -1975,69 +2095,108 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             }
         }
         __syncwarp();
+    } else if (warp == kTcWarps) {
+        // ------------------------------------- the pair's second CTA: x rows + readiness (lane 0)
+        if constexpr (CL > 1) {
+            if (lane == 0) {
+                bool ok = true;
+                int32_t loaded = 0, consumed = 0;
+                const uint32_t lead_pr0 = cluster_addr(pr0, 0u);
+                int s = 0;
+                uint32_t ph = 0;
+                for (int32_t c = 0; c < nchunks && ok; c++) {
+                    // the stage is free once the leader's MMAs of chunk c - S are done
+                    if (c >= S && !tc_wait<true>(fr0 + 8u * s, ph ^ 1u, failed)) {
+                        ok = false;
+                        break;
+                    }
+                    load_x(c, s);
+                    loaded = c + 1;
+                    if (!tc_wait(af0 + 8u * s, ph, failed) || !tc_wait(xf0 + 8u * s, ph, failed)) {
+                        ok = false;
+                        break;
+                    }
+                    consumed = c + 1;
+                    tc_arrive_cluster(lead_pr0 + 8u * s);
+                    if (++s == S) {
+                        s = 0;
+                        ph ^= 1u;
+                    }
+                }
+                if (!ok) {
+                    give_up();
+                    for (int32_t c = consumed; c < loaded; c++)
+                        tc_wait(xf0 + 8u * (c % S), (uint32_t)((c / S) & 1), nullptr);
+                }
+            }
+            __syncwarp();
+        }
     } else {
         // ----------------------------------------------------- decode warps
-        const uint8_t *tb = smem;
+        // one chain per lane (two tANS steps per slab test), a ring of R
+        // 128-byte slab rows per warp filled 16 bytes a copy, the
+        // sign/mantissa words of the next two chunks in registers
+        const uint8_t *tb = smem + (tbl_sa - base_sa);
         const uint32_t lane_off = 4u * (lane % kCopies);
         const uint32_t mask = (uint32_t)(R - 1) << 7;
-        RingT<kTcLag> rg;
-        rg.lane_base = ring_area<R>(smem, warp, 1) + 4u * lane;
+        const uint32_t ring = ring0 + (uint32_t)warp * ring_bytes;
+        const uint32_t ring_lane = ring + 4u * lane, ring_dst = ring + 16u * (lane & 7);
         uint8_t *a_ptr = smem + (a_sa - base_sa);
         const int g = lane >> 2, t4 = lane & 3;
         const int rgrp = warp >> 1, chain = warp & 1;
         const int64_t wg = (int64_t)blockIdx.x * 8 + rgrp;          // global 16-row group
         const uint32_t row = (uint32_t)(16 * rgrp + g + 8 * chain);  // row within the tile
-        // this lane's sign/mantissa queue: chunk c's 8 bytes in slot c % kTcSmSlots
-        const uint32_t smq = smq_sa + (uint32_t)warp * (kTcSmSlots * 256u) + 8u * lane;
+        const int64_t tstep = K * 8;  // sign/mantissa bytes per chunk row
         Chain ch;
         chain_idle(ch, p.comp);
-        bool live = false, ok = true;
+        PairRing rg{};
+        bool live = false, on = false, ok = true;
+        const uint8_t *ring_src = nullptr;
         const uint8_t *sp = p.sm;
+        uint2 m_n0 = make_uint2(0u, 0u), m_n1 = make_uint2(0u, 0u);
         int32_t kslice = 0, tt = 0;  // slice of chunk c and chunk within it
         int s = 0;                   // stage of chunk c
         uint32_t ph = 0;             // (c / S) & 1
         for (int32_t c = 0; c < nchunks; c++) {
-            if (tt == 0) {  // this slice's streams, its first rows and sign/mantissa words
+            if (tt == 0) {  // this slice's streams, their first rows and sign/mantissa words
                 const int64_t sid = ((wg * p.KS + kslice) * 2 + chain) * 32 + lane;
                 const int32_t G = chain_init(ch, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
                                              sid, lane_off, p.status);
                 live = G > 0;
                 if (!live) chain_idle(ch, p.comp);
-                cp_async_wait<0>();
-                ring_start<R>(rg, ch, __reduce_max_sync(0xffffffffu, live ? G : 0), live);
+                on = ring_start128<R>(rg, ch, G, live, lane, ring_dst, ring_src);
                 sp = p.sm + sid * 8;
-#pragma unroll
-                for (int d = 0; d < kTcSmAhead; d++)
-                    cp_async8(smq + ((uint32_t)(c + d) & (kTcSmSlots - 1)) * 256u, sp + (int64_t)d * K * 8,
-                              live && d < tps);
-                cp_async_commit();
-                cp_async_wait<0>();
+                if (live) {
+                    m_n0 = ld_stream_v2(sp);
+                    if (tps > 1) m_n1 = ld_stream_v2(sp + tstep);
+                }
             }
-            // one group per chunk: ring rows and the sign/mantissa words of
-            // chunk c + kTcSmAhead.  A chunk is short next to a DRAM round
-            // trip, so the decode reads groups kTcLag chunks old
-            const int32_t need = ring_fill<R>(rg, ch, live);
-            cp_async8(smq + ((uint32_t)(c + kTcSmAhead) & (kTcSmSlots - 1)) * 256u,
-                      sp + (int64_t)(tt + kTcSmAhead) * K * 8, live && tt + kTcSmAhead < tps);
-            cp_async_commit();
-            cp_async_wait<kTcLag>();
-            uint2 m;
-            asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];"
-                         : "=r"(m.x), "=r"(m.y)
-                         : "r"(smq + ((uint32_t)c & (kTcSmSlots - 1)) * 256u));
+            const uint2 m = m_n0;
+            m_n0 = m_n1;
+            if (live && tt + 2 < tps) m_n1 = ld_stream_v2(sp + (int64_t)(tt + 2) * tstep);
             uint32_t e[kTablePairs];
-            if (need >= rg.done[kTcLag]) {
+            if (ring_tile128<R>(rg, row_of128(ch.v, p.q), live, on, lane, ring_src, ring_dst)) {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_ring(ch, tb, rg.lane_base, mask, p.q);
+                for (int j = 0; j < kTablePairs; j += 2)
+                    chain_step2_ring<128>(ch, tb, ring_lane, mask, p.q, e[j], e[j + 1]);
             } else {
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j++) e[j] = chain_step_global(ch, tb, p.q);
+                for (int j = 0; j < kTablePairs; j += 2) chain_step2_global<128>(ch, tb, p.q, e[j], e[j + 1]);
             }
             uint32_t wd[4];
             compose_pairs(gather_syms(e[0], e[1], e[2], e[3]), m.x, p.q, wd[0], wd[1]);
             compose_pairs(gather_syms(e[4], e[5], e[6], e[7]), m.y, p.q, wd[2], wd[3]);
             // the stage is free once the MMAs of chunk c - S have completed
-            if (c >= S && ok && !tc_wait(em0 + 8u * s, ph ^ 1u, failed)) ok = false;
+            // (the leader's, relayed to the pair's second CTA); a wait that
+            // gives up is published before this warp arrives
+            if (c >= S && ok) {
+                const bool got = (CL > 1 && rank == 1) ? tc_wait<true>(fr0 + 8u * s, ph ^ 1u, failed)
+                                                       : tc_wait(em0 + 8u * s, ph ^ 1u, failed);
+                if (!got) {
+                    ok = false;
+                    give_up();
+                }
+            }
             uint8_t *at = a_ptr + s * kTcATile;
 #pragma unroll
             for (int j = 0; j < 4; j++) {  // 16-column sub-chunk j: columns 2t, 2t+1 | 8+2t, 9+2t
@@ -2046,6 +2205,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 *reinterpret_cast<uint32_t *>(at + tc_swz(row, 16 * j + 2 * t4)) = lo;
                 *reinterpret_cast<uint32_t *>(at + tc_swz(row, 16 * j + 8 + 2 * t4)) = hi;
             }
+            // the MMAs read the tile through the async proxy
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
             __syncwarp();
             if (lane == 0) tc_arrive(af0 + 8u * s);
@@ -2059,36 +2219,43 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
             }
         }
         cp_async_wait<0>();
-        if (!ok) *failed = 1;
     }
-    __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;");
+    tc_fence_sync<CL>();  // the leader's MMAs are done before either CTA reads its accumulator
     const bool good = *failed == 0;
-    if (warp < 4 && good) {
-        const int64_t r = (int64_t)blockIdx.x * 128 + 32 * warp + lane;
+    if (warp < kTcWarps && good) {
+        // warp w: tensor-memory lanes 32 (w % 4).. (rows of this CTA's
+        // block), 8-column groups w / 4, w / 4 + 4, ... (token m0 + column)
+        const int quarter = warp & 3;
+        const int64_t r = (int64_t)blockIdx.x * 128 + 32 * quarter + lane;
         const float sc = p.scale[r];
-        for (int col = 0; col < p.nt; col += 8) {
+        for (int col = 8 * (warp >> 2); col < (int)acc_cols; col += 32) {
             uint32_t v[8];
             asm volatile(
                 "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]),
                   "=r"(v[6]), "=r"(v[7])
-                : "r"(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)col));
+                : "r"(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)col));
             asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
-            for (int i = 0; i < 8; i++) {
-                const int64_t mm = (int64_t)m0 + col + i;
+            for (int k = 0; k < 8; k++) {
+                const int64_t mm = (int64_t)m0 + col + k;
                 if (mm < p.M)
-                    p.y[mm * p.R + r] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]) * sc));
+                    p.y[mm * p.R + r] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[k]) * sc));
             }
         }
     }
     if (!good && threadIdx.x == 0 && p.status) atomicOr(p.status, TANS_B200_DATA_TIMEOUT);
     asm volatile("tcgen05.fence::before_thread_sync;");
-    __syncthreads();
+    if constexpr (CL > 1)
+        cluster_sync();  // both CTAs have read their accumulators before the pair frees them
+    else
+        __syncthreads();
     if (warp == 0) {
         asm volatile("tcgen05.fence::after_thread_sync;");
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+        if constexpr (CL > 1)
+            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
+        else
+            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(ncols));
     }
 }
 
@@ -2783,15 +2950,37 @@ extern "C" int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_b
     int sms;
     int rc = device_setup(&sms);
     if (rc) return rc;
-    // tokens per CTA: all of them up to 256 (multiple of 16), else 256-token tiles
-    int nt = (int)((m + 15) / 16 * 16);
-    if (nt > kTcMaxTokens) nt = kTcMaxTokens;
-    const int64_t ty = (m + nt - 1) / nt;
-    // ring rows: 32 where two stages still fit beside them, else 16
-    const int per_stage = kTcATile + nt * 128;
-    const int rr = nt <= 128 ? 32 : 16;
-    const int fixed = kTableBytes + rr * 128 + kTcWarps * rr * 128 + kTcWarps * kTcSmSlots * 256 + 1024;
-    int stages = (kSmemMax - 1024 - fixed) / per_stage;  // 1 KiB left for static shared memory
+    // Up to 256 tokens: one CTA per 128-row block holds them all (multiple of
+    // 16).  Above that, when the row-block count is even, CTA pairs over two
+    // row blocks (2-SM MMA, M = 256) with tiles of up to 512 tokens: two MMAs
+    // of mma_n tokens per K step (the smallest multiple of 16 that spreads M
+    // evenly over the tiles), each CTA holding half of every MMA's x rows.
+    // Otherwise 256-token tiles, each decoding W again.
+    const int cl = (m > kTcMaxTokens && (rows / 128) % 2 == 0) ? 2 : 1;
+    int brows, mma_n, halves, box_rows;
+    int64_t ty;
+    if (cl == 2) {
+        ty = (m + 2 * kTcMaxTokens - 1) / (2 * kTcMaxTokens);
+        halves = 2;
+        mma_n = (int)(((m + 2 * ty - 1) / (2 * ty) + 15) / 16 * 16);
+        box_rows = mma_n / 2;
+        brows = mma_n;  // two halves of mma_n / 2 rows
+    } else {
+        mma_n = (int)((m + 15) / 16 * 16);
+        if (mma_n > kTcMaxTokens) mma_n = kTcMaxTokens;
+        ty = (m + mma_n - 1) / mma_n;
+        halves = 1;
+        box_rows = brows = mma_n;
+    }
+    // ring rows by slice length (at most 32), 16 where 32 would leave fewer
+    // than two stages; fixed bytes: 1 KiB to align the stages, the rings'
+    // own alignment past that, the rings and the table
+    const int per_stage = kTcATile + brows * 128;
+    auto fixed_bytes = [](int r) { return 1024 + (r * 128 > 1024 ? r * 128 - 1024 : 0) + kTcWarps * r * 128 + kTableBytes; };
+    int rr = ring_rows(cols / col_splits / 8) > 16 ? 32 : 16;
+    if (rr == 32 && (kSmemMax - 256 - fixed_bytes(32)) / per_stage < 2) rr = 16;
+    const int fixed = fixed_bytes(rr);
+    int stages = (kSmemMax - 256 - fixed) / per_stage;  // 256 bytes left for static shared memory
     if (stages > kTcMaxStages) stages = kTcMaxStages;
     if (stages < 2) return fail(TANS_B200_ERR_INVALID, "gemm_tc: shared memory");
     const int smem = fixed + stages * per_stage;
@@ -2800,11 +2989,11 @@ extern "C" int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_b
     if (rc) return rc;
     TcArgs args{};
     // x [m][cols] bf16: dimension 0 = columns (contiguous), dimension 1 = tokens;
-    // one box = 64 columns (128 bytes, the swizzle span) x nt tokens; tokens
-    // past m read as zeros
+    // one box = 64 columns (128 bytes, the swizzle span) x box_rows tokens;
+    // tokens past m read as zeros
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)m};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    const cuuint32_t box[2] = {64, (cuuint32_t)nt};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     CUresult cr = encode(&args.xmap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t *>(x), dims,
                          strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -2823,19 +3012,41 @@ extern "C" int tans_b200_gemm_tc(const uint8_t *compressed, int64_t compressed_b
     args.C = cols;
     args.KS = col_splits;
     args.M = m;
-    args.nt = nt;
+    args.brows = brows;
+    args.mma_n = mma_n;
+    args.halves = halves;
     args.stages = stages;
     args.status = status;
     args.q = make_opq();
     const dim3 grid((unsigned)(rows / 128), (unsigned)ty);
-    if (rr == 32) {
-        rc = set_smem(gemm_tc_kernel<32>, smem);
+    if (cl == 2) {
+        // CTA pairs along x (row blocks 2b, 2b + 1)
+        if (rr != 16) return fail(TANS_B200_ERR_INVALID, "gemm_tc: pair layout");
+        rc = set_smem(gemm_tc_kernel<16, 2>, smem);
         if (rc) return rc;
-        gemm_tc_kernel<32><<<grid, kTcThreads, smem, (cudaStream_t)stream>>>(args);
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = grid;
+        cfg.blockDim = dim3(kTcThreads);
+        cfg.dynamicSmemBytes = (size_t)smem;
+        cfg.stream = (cudaStream_t)stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 2;
+        attr[0].val.clusterDim.y = 1;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        const cudaError_t e = cudaLaunchKernelEx(&cfg, gemm_tc_kernel<16, 2>, args);
+        if (e != cudaSuccess)
+            return fail(TANS_B200_ERR_CUDA, "gemm_tc_kernel launch: %s", cudaGetErrorString(e));
+    } else if (rr == 32) {
+        rc = set_smem(gemm_tc_kernel<32, 1>, smem);
+        if (rc) return rc;
+        gemm_tc_kernel<32, 1><<<grid, kTcThreads, smem, (cudaStream_t)stream>>>(args);
     } else {
-        rc = set_smem(gemm_tc_kernel<16>, smem);
+        rc = set_smem(gemm_tc_kernel<16, 1>, smem);
         if (rc) return rc;
-        gemm_tc_kernel<16><<<grid, kTcThreads, smem, (cudaStream_t)stream>>>(args);
+        gemm_tc_kernel<16, 1><<<grid, kTcThreads, smem, (cudaStream_t)stream>>>(args);
     }
     return launch_status("gemm_tc_kernel");
 }

@@ -168,10 +168,13 @@ def test_gemm_large_batch_matches_reference(cuda, monkeypatch, R, C, B):
 @pytest.mark.gpu
 @pytest.mark.parametrize("R,C,B,KS", [(128, 512, 16, 1), (256, 1024, 40, 1), (1024, 5120, 64, 5),
                                       (512, 4352, 300, 4), (17408, 5120, 256, None),
-                                      (128, 512, 1, 1), (384, 2048, 5, 2)])
+                                      (128, 512, 1, 1), (384, 2048, 5, 2), (384, 2048, 600, 2),
+                                      (256, 1024, 1000, 1), (17408, 5120, 2048, None)])
 def test_gemm_tc_matches_reference(cuda, R, C, B, KS):
     """Decode into shared memory + tcgen05 MMA: rel err within the GEMV bound,
-    tokens beyond one 256-token tile and ragged token counts included."""
+    tokens beyond one 256-token tile and ragged token counts included; above
+    256 tokens cluster pairs share each decoded tile (even row-block counts)
+    or 256-token tiles decode W again (384 rows: three row blocks)."""
     from rans_vectoradd import _C
     w8, s = make(R, C, R + 7 * C)
     enc = tans_gemv.encode_weight(w8.to(cuda), s.to(cuda), col_splits=KS)
