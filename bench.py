@@ -94,6 +94,16 @@ def measured_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+def measured_bf16_sustained():
+    """cuBLAS bf16 TFLOP/s sustained under the power cap (MEASURED_PEAKS.json),
+    the denominator for kernels timed inside longer runs; None if absent."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return float(json.load(f)["bf16_tflops_sustained"])
+    except Exception:
+        return None
+
+
 def profile_traffic(n_fp8: int, n_elems: int):
     """Per-launch DRAM bytes (read + write) of the fused kernel from the
     committed ncu capture (profiles/fused_kernel_traffic.json), scaled by
@@ -713,7 +723,9 @@ def run_gemm(args, dev, barrier):
     exact = bool(torch.equal(w, w8.view(torch.float8_e4m3fn).to(torch.bfloat16)))
     ms_dec = timed(lambda: tans_gemv.dense_weight(enc, w), args.steps * 4, args.warmup, stream,
                    barrier) / (args.steps * 4)
+    peak = measured_bf16_sustained()
     line = {"workload": "gemm (cfg3 weight, prefill batches)", "rows": R, "cols": C,
+            "bf16_tflops_sustained_measured": peak,
             "dense_decode_us": round(ms_dec * 1e3, 2),
             "dense_decode_gbs_e4m3": round(R * C / (ms_dec / 1e3) / 1e9, 1),
             "dense_exact": exact, "batches": []}
@@ -731,7 +743,10 @@ def run_gemm(args, dev, barrier):
         fl = 2.0 * B * R * C
         line["batches"].append({"batch": B, "us": round(ms * 1e3, 1),
                                 "tflops": round(fl / (ms / 1e3) / 1e12, 1),
-                                "path": "gemm_tc_kernel" if B > 8 else "gemv_kernel",
+                                "frac_of_sustained_bf16": (round(fl / (ms / 1e3) / 1e12 / peak, 3)
+                                                           if peak else None),
+                                "path": ("gemm_tc_kernel (CTA pairs, 2-SM MMA)" if B > 256
+                                         else "gemm_tc_kernel" if B > 8 else "gemv_kernel"),
                                 "rel_err": err,
                                 "dense_path_us": round(ms_dense * 1e3, 1),
                                 "dense_path_tflops": round(fl / (ms_dense / 1e3) / 1e12, 1),
