@@ -880,6 +880,41 @@ def run_stack(args, ws, rank, dev, barrier):
 
 # ------------------------------------------------------------------- main
 
+def table_log11_extra(args, x, y, N, raw_step, stream, barrier, dev):
+    """table_log 11, a labelled extra (the reference fixes L = 4096,
+    tans_codec.py:24-25): the headline inputs encoded on the device with a
+    2048-entry table, the fused add timed like the headline (fewer steps),
+    bit-exact against the uncompressed add, and its compressed size against
+    the L = 4096 encoding."""
+    import rans_vectoradd as rv
+    from rans_vectoradd import tans_codec
+    xd, yd = x.to(dev), y.to(dev)
+    n = xd.numel()
+    K = n // N
+    hist = (torch.bincount(((xd >> 3) & 15).long(), minlength=16) +
+            torch.bincount(((yd >> 3) & 15).long(), minlength=16)).cpu().double()
+    ex = tans_codec.encode(xd.view(K, N), hist, tile=8, table_log=11)
+    ey = tans_codec.encode(yd.view(K, N), hist, tile=8, table_log=11)
+    tbl = tans_codec.build_decode_table(ex[6].numpy(), ex[5].numpy()).to(dev)
+    a = [ex[0], ex[2], ex[1], ex[3], ex[4]]
+    b = [ey[0], ey[2], ey[1], ey[3], ey[4]]
+    out = rv.fp8_vecadd_fused_tans(*a, *b, tbl, N)
+    exact = bool(torch.equal(out.view(N // 16, K, 16).permute(1, 0, 2).reshape(-1),
+                             rv.fp8_vecadd_raw(xd, yd)))
+    del out
+    steps = max(3, args.steps // 4)
+    ms = timed(lambda: rv.fp8_vecadd_fused_tans(*a, *b, tbl, N), steps, 2, stream,
+               barrier) / steps
+    stream_bytes = sum(t.numel() * t.element_size() for t in a + b)
+    return {"table_log": 11, "table_entries": 2048, "n_fp8_per_stream": N,
+            "fused_ms": round(ms, 4), "gbs": round(3.0 * n / (ms / 1e3) / 1e9, 3),
+            "x_raw": round(raw_step / ms, 4),
+            "bits_per_fp8": round(stream_bytes * 8 / (2 * n), 4),
+            "bit_exact_vs_raw_add": exact,
+            "note": "labelled extra: L = 2048 build (libtans_b200_l11.so); the headline and "
+                    "parity path stay at the reference's L = 4096"}
+
+
 def run_sweep(args, n, N, x, y, raw_step, peak, stream, barrier, dev, emit_lines=True):
     """Stream-length sweep (cfg1's 1K/4K/16K/64K pair-symbol and fp8 readings):
     the same inputs re-encoded on the device at each length, plain format
@@ -1126,6 +1161,10 @@ def main():
             torch.cuda.empty_cache()
         extras["stack_cfg4"] = stack_cfg4(args, ws, rank, dev, barrier)
         torch.cuda.empty_cache()
+        if rank == 0 and ws == 1:
+            extras["table_log_11"] = table_log11_extra(args, x, y, N, raw_step, stream, barrier,
+                                                       dev)
+            torch.cuda.empty_cache()
         if rank == 0 and ws == 1 and not args.sweep:
             # cfg1's stream-length sweep (fewer steps per length)
             sw = argparse.Namespace(**vars(args))

@@ -38,15 +38,23 @@ extern "C" {
  * the decode entry points take (a device int32, may be NULL).  Malformed
  * metadata never makes a kernel read out of bounds; it is reported here. */
 #define TANS_B200_DATA_BAD_OFFSETS 1 /* block offsets not monotone/in range */
-#define TANS_B200_DATA_BAD_STATE 2   /* initial state outside [4096, 8192)  */
+#define TANS_B200_DATA_BAD_STATE 2   /* initial state outside [L, 2L)       */
 #define TANS_B200_DATA_BAD_TABLE 4   /* spread/freqs/table entry malformed  */
 #define TANS_B200_DATA_TIMEOUT 8     /* a bounded in-kernel wait ran out    */
 
-#define TANS_B200_TABLE_SIZE 4096   /* L = M, tans_codec.py:24-25 */
+/* Table size L = M (tans_codec.py:24-25).  4096 is the reference's and the
+ * parity build; the library is also built with -DTANS_B200_TABLE_SIZE=2048
+ * (table_log 11, libtans_b200_l11.so) as a labelled extra. */
+#ifndef TANS_B200_TABLE_SIZE
+#define TANS_B200_TABLE_SIZE 4096
+#endif
 #define TANS_B200_BLOCK_STREAMS 128 /* tans_codec.py:27          */
 
 /* Message for the last failed call on this thread ("" if none). */
 const char *tans_b200_last_error(void);
+/* L of this build (4096, or 2048 for the table_log 11 build).  The
+ * reference fixes L = 4096 (tans_codec.py:24-25); no counterpart. */
+int tans_b200_table_size(void);
 /* Library version string. */
 const char *tans_b200_version(void);
 

@@ -64,6 +64,11 @@ def lib() -> ctypes.CDLL:
         L.oracle_decode.argtypes = [p, i64, p, p, p, p, p, i64, i64, p]
         L.oracle_vecadd_fused.restype = ctypes.c_int
         L.oracle_vecadd_fused.argtypes = [p, i64, p, p, p, p, p, i64, p, p, p, p, p, i64, i64, p]
+        L.oracle_decode_l.restype = ctypes.c_int
+        L.oracle_decode_l.argtypes = [p, i64, p, p, p, p, p, i64, i64, p, i64]
+        L.oracle_vecadd_fused_l.restype = ctypes.c_int
+        L.oracle_vecadd_fused_l.argtypes = [p, i64, p, p, p, p, p, i64, p, p, p, p, p, i64, i64, p,
+                                            i64]
         L.oracle_num_threads.restype = ctypes.c_int
         L.oracle_set_num_threads.restype = None
         L.oracle_set_num_threads.argtypes = [ctypes.c_int]
@@ -156,8 +161,9 @@ def decode(comp, offsets, states, partial, sm, table, n_fp8_per_stream: int):
     K = states.size
     N = int(n_fp8_per_stream)
     out = np.empty((N, K), np.uint8)
-    rc = lib().oracle_decode(_p(comp), comp.size, _p(offsets), _p(states), _p(partial), _p(sm),
-                             _p(table), K, N, _p(out))
+    # the table's size is L: 4096 (the reference's), or 2048 for the table_log 11 extra
+    rc = lib().oracle_decode_l(_p(comp), comp.size, _p(offsets), _p(states), _p(partial), _p(sm),
+                               _p(table), K, N, _p(out), table.size)
     return out, rc == 0
 
 
@@ -171,9 +177,9 @@ def vecadd_fused(a, b, table, n_fp8_per_stream: int):
     K = ast.size
     N = int(n_fp8_per_stream)
     out = np.empty(N * K, np.uint8)
-    rc = lib().oracle_vecadd_fused(_p(ac), ac.size, _p(ao), _p(ast), _p(ap), _p(asm),
-                                   _p(bc), bc.size, _p(bo), _p(bst), _p(bp), _p(bsm),
-                                   _p(table), K, N, _p(out))
+    rc = lib().oracle_vecadd_fused_l(_p(ac), ac.size, _p(ao), _p(ast), _p(ap), _p(asm),
+                                     _p(bc), bc.size, _p(bo), _p(bst), _p(bp), _p(bsm),
+                                     _p(table), K, N, _p(out), table.size)
     return out, rc == 0
 
 

@@ -248,6 +248,7 @@ done:
 
 typedef struct {
     uint32_t x, hi, lo, cnt;
+    uint32_t L;   /* table size: 4096 (the reference's), 2048 for table_log 11 */
     int64_t slab; /* next slab index to load, or < 0 */
     const uint8_t *blk;
 } chain_t;
@@ -260,14 +261,15 @@ static uint32_t load_slab(const chain_t *c, int64_t slab, int64_t t) {
 
 /* tans_decode.cu:65-92 (init_tans_ctx).  Returns -1 on malformed metadata. */
 static int chain_init(chain_t *c, const uint8_t *comp, int64_t comp_bytes, const int32_t *offsets,
-                      const uint16_t *states, const uint8_t *partial, int64_t sid) {
+                      const uint16_t *states, const uint8_t *partial, int64_t sid, uint32_t L) {
     int64_t b = sid / ORACLE_BLOCK, t = sid % ORACLE_BLOCK;
     int64_t base = offsets[b], next = offsets[b + 1], g;
     if (base < 0 || next < base || next > comp_bytes || (next - base) % (ORACLE_BLOCK * 4) != 0)
         return -1;
     g = (next - base) / (ORACLE_BLOCK * 4);
     if (g < 1) return -1;
-    if (states[sid] < ORACLE_L || states[sid] >= 2 * ORACLE_L) return -1;
+    if (states[sid] < L || states[sid] >= 2 * L) return -1;
+    c->L = L;
     c->blk = comp + base;
     c->x = states[sid];
     c->hi = load_slab(c, g - 1, t);
@@ -279,7 +281,7 @@ static int chain_init(chain_t *c, const uint8_t *comp, int64_t comp_bytes, const
 
 /* tans_decode.cu:94-123 (tans_step).  Returns the pair symbol. */
 static uint8_t chain_step(chain_t *c, const int32_t *table, int64_t t) {
-    uint32_t e = (uint32_t)table[c->x - ORACLE_L];
+    uint32_t e = (uint32_t)table[c->x - c->L];
     uint32_t nb = (e >> 8) & 15u, base = (e >> 16) & 0xFFFFu;
     uint32_t window = c->cnt == 0 ? c->hi : (c->hi << c->cnt) | (c->lo >> (32u - c->cnt));
     uint32_t bits = nb == 0 ? 0u : window >> (32u - nb);
@@ -296,15 +298,16 @@ static uint8_t chain_step(chain_t *c, const int32_t *table, int64_t t) {
 
 /* tans_decode.cu:125-155: out[N][K], sm[N/2][K].  Returns 0, or -1 if any
  * stream's metadata is malformed (that stream's output is zeroed). */
-int oracle_decode(const uint8_t *comp, int64_t comp_bytes, const int32_t *offsets,
-                  const uint16_t *states, const uint8_t *partial, const uint8_t *sm,
-                  const int32_t *table, int64_t K, int64_t N, uint8_t *out) {
+int oracle_decode_l(const uint8_t *comp, int64_t comp_bytes, const int32_t *offsets,
+                    const uint16_t *states, const uint8_t *partial, const uint8_t *sm,
+                    const int32_t *table, int64_t K, int64_t N, uint8_t *out, int64_t L) {
     int bad = 0;
+    if (L != ORACLE_L && L != ORACLE_L / 2) return -1;
 #pragma omp parallel for schedule(static) reduction(| : bad)
     for (int64_t k = 0; k < K; k++) {
         chain_t c;
         int64_t t = k % ORACLE_BLOCK;
-        if (chain_init(&c, comp, comp_bytes, offsets, states, partial, k) != 0) {
+        if (chain_init(&c, comp, comp_bytes, offsets, states, partial, k, (uint32_t)L) != 0) {
             for (int64_t j = 0; j < N; j++) out[j * K + k] = 0;
             bad = 1;
             continue;
@@ -319,23 +322,34 @@ int oracle_decode(const uint8_t *comp, int64_t comp_bytes, const int32_t *offset
     return bad ? -1 : 0;
 }
 
+/* The reference's table size (tans_codec.py:24-25). */
+int oracle_decode(const uint8_t *comp, int64_t comp_bytes, const int32_t *offsets,
+                  const uint16_t *states, const uint8_t *partial, const uint8_t *sm,
+                  const int32_t *table, int64_t K, int64_t N, uint8_t *out) {
+    return oracle_decode_l(comp, comp_bytes, offsets, states, partial, sm, table, K, N, out,
+                           ORACLE_L);
+}
+
 /* vecadd.cu:156-243: both inputs decoded with one table, composed, added;
- * sm tiled [N/16][K][8], out tiled [N/16][K][16].  Returns 0 or -1. */
-int oracle_vecadd_fused(const uint8_t *a_comp, int64_t a_bytes, const int32_t *a_off,
-                        const uint16_t *a_st, const uint8_t *a_part, const uint8_t *a_sm,
-                        const uint8_t *b_comp, int64_t b_bytes, const int32_t *b_off,
-                        const uint16_t *b_st, const uint8_t *b_part, const uint8_t *b_sm,
-                        const int32_t *table, int64_t K, int64_t N, uint8_t *out) {
-    uint8_t *tab = (uint8_t *)malloc(65536);
+ * sm tiled [N/16][K][8], out tiled [N/16][K][16].  Returns 0 or -1.  L is
+ * the table size (4096, or 2048 for the table_log 11 extra). */
+int oracle_vecadd_fused_l(const uint8_t *a_comp, int64_t a_bytes, const int32_t *a_off,
+                          const uint16_t *a_st, const uint8_t *a_part, const uint8_t *a_sm,
+                          const uint8_t *b_comp, int64_t b_bytes, const int32_t *b_off,
+                          const uint16_t *b_st, const uint8_t *b_part, const uint8_t *b_sm,
+                          const int32_t *table, int64_t K, int64_t N, uint8_t *out, int64_t L) {
+    uint8_t *tab;
     int bad = 0;
+    if (L != ORACLE_L && L != ORACLE_L / 2) return -1;
+    tab = (uint8_t *)malloc(65536);
     int64_t n_tiles = N / 16;
     oracle_fp8_add_table(tab);
 #pragma omp parallel for schedule(static) reduction(| : bad)
     for (int64_t k = 0; k < K; k++) {
         chain_t ca, cb;
         int64_t t = k % ORACLE_BLOCK;
-        if (chain_init(&ca, a_comp, a_bytes, a_off, a_st, a_part, k) != 0 ||
-            chain_init(&cb, b_comp, b_bytes, b_off, b_st, b_part, k) != 0) {
+        if (chain_init(&ca, a_comp, a_bytes, a_off, a_st, a_part, k, (uint32_t)L) != 0 ||
+            chain_init(&cb, b_comp, b_bytes, b_off, b_st, b_part, k, (uint32_t)L) != 0) {
             for (int64_t j = 0; j < n_tiles; j++) memset(out + (j * K + k) * 16, 0, 16);
             bad = 1;
             continue;
@@ -353,6 +367,15 @@ int oracle_vecadd_fused(const uint8_t *a_comp, int64_t a_bytes, const int32_t *a
     }
     free(tab);
     return bad ? -1 : 0;
+}
+
+int oracle_vecadd_fused(const uint8_t *a_comp, int64_t a_bytes, const int32_t *a_off,
+                        const uint16_t *a_st, const uint8_t *a_part, const uint8_t *a_sm,
+                        const uint8_t *b_comp, int64_t b_bytes, const int32_t *b_off,
+                        const uint16_t *b_st, const uint8_t *b_part, const uint8_t *b_sm,
+                        const int32_t *table, int64_t K, int64_t N, uint8_t *out) {
+    return oracle_vecadd_fused_l(a_comp, a_bytes, a_off, a_st, a_part, a_sm, b_comp, b_bytes, b_off,
+                                 b_st, b_part, b_sm, table, K, N, out, ORACLE_L);
 }
 
 int oracle_num_threads(void) {

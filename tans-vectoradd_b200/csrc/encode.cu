@@ -150,7 +150,7 @@ struct Emitter {
     uint32_t *out;
     __device__ __forceinline__ void step(const EncTables &t, uint32_t s) {
         const uint32_t w = t.info[kInfoCopies * s];
-        const uint32_t k = (uint32_t)((int32_t)x + info_delta(w)) >> 13;
+        const uint32_t k = (uint32_t)((int32_t)x + info_delta(w)) >> (tans_b200::kTableLog + 1);
         const uint32_t v = x & ((1u << k) - 1u);
         const uint32_t hi = __funnelshift_l(v, 0u, fill);  // bits that spill past 32
         lo |= v << fill;
@@ -315,7 +315,8 @@ __global__ void __launch_bounds__(kBlk, 8) enc_stage_kernel(const EncArgs a) {
                     s = (((row[2 * i] >> 3) & 15u) << 4) | ((row[2 * i + 1] >> 3) & 15u);
                 else
                     s = row[i];
-                if (info_delta(t.info[kInfoCopies * s]) == (tans_b200::kEncoderBadBits << 13))
+                if (info_delta(t.info[kInfoCopies * s]) ==
+                    (tans_b200::kEncoderBadBits << (tans_b200::kTableLog + 1)))
                     atomicMin(&h->bad_symbol, (int)s);
             }
         }

@@ -63,6 +63,8 @@ extern "C" const char *tans_b200_last_error(void) { return g_last_error.c_str();
 
 extern "C" const char *tans_b200_version(void) { return "tans_b200 0.1 (sm_100a)"; }
 
+extern "C" int tans_b200_table_size(void) { return (int)kL; }
+
 // ------------------------------------------------------------ decode table
 
 extern "C" int tans_b200_build_decode_table_host(const int32_t *spread, const int32_t *freqs,
@@ -79,8 +81,8 @@ extern "C" int tans_b200_build_decode_table_host(const int32_t *spread, const in
         if (xp <= 0 || xp >= 2 * (int64_t)kL)
             return fail(TANS_B200_ERR_INVALID, "build_decode_table: inconsistent freqs for symbol %d",
                         s);
-        // nb = shifts that lift xp into [L, 2L): 12 - floor(log2 xp)
-        int nb = 12 - (31 - __builtin_clz(static_cast<uint32_t>(xp)));
+        // nb = shifts that lift xp into [L, 2L): log2 L - floor(log2 xp)
+        int nb = tans_b200::kTableLog - (31 - __builtin_clz(static_cast<uint32_t>(xp)));
         if (nb < 0)
             return fail(TANS_B200_ERR_INVALID, "build_decode_table: symbol %d over-subscribed", s);
         uint32_t base = static_cast<uint32_t>(xp) << nb;
@@ -99,7 +101,7 @@ struct tans_b200_encoded {
     std::vector<uint32_t> next_state;  // flat: cum[s] + r -> L + slot
     std::vector<uint32_t> cum;         // per-symbol start in next_state
     std::vector<uint32_t> freq;
-    std::vector<uint32_t> k1;          // 12 - floor(log2 f)
+    std::vector<uint32_t> k1;          // log2 L - floor(log2 f)
     std::vector<uint32_t> thresh;      // f << k1
     std::vector<uint64_t> bits;        // total bits per stream
     std::vector<uint16_t> final_state;
@@ -189,7 +191,7 @@ extern "C" int tans_b200_encode(const uint8_t *symbols, int64_t K, int64_t N,
         uint32_t f = static_cast<uint32_t>(freqs[s]);
         e->freq[s] = f;
         uint32_t hf = f ? 31u - __builtin_clz(f) : 0u;
-        e->k1[s] = f ? 12u - std::min(hf, 12u) : 0u;
+        e->k1[s] = f ? (uint32_t)tans_b200::kTableLog - std::min(hf, (uint32_t)tans_b200::kTableLog) : 0u;
         e->thresh[s] = f ? (f << e->k1[s]) : 0u;
     }
     if (sum != kL) {
@@ -335,12 +337,13 @@ int tans_b200::encoder_tables(const int32_t *freqs, int64_t n_syms, const int32_
     for (int s = 0; s < 256; s++) {
         const uint32_t f = s < n_syms ? static_cast<uint32_t>(freqs[s]) : 0u;
         if (f == 0) {
-            t->delta[s] = kEncoderBadBits << 13;
+            t->delta[s] = kEncoderBadBits << (kTableLog + 1);
             t->base[s] = 0;
             continue;
         }
-        const uint32_t k1 = 12u - std::min(31u - static_cast<uint32_t>(__builtin_clz(f)), 12u);
-        t->delta[s] = static_cast<int32_t>(k1 << 13) - static_cast<int32_t>(f << k1);
+        const uint32_t lg = (uint32_t)kTableLog;
+        const uint32_t k1 = lg - std::min(31u - static_cast<uint32_t>(__builtin_clz(f)), lg);
+        t->delta[s] = static_cast<int32_t>(k1 << (kTableLog + 1)) - static_cast<int32_t>(f << k1);
         t->base[s] = static_cast<int32_t>(cum[s]) - static_cast<int32_t>(f);
     }
     return TANS_B200_OK;

@@ -39,6 +39,7 @@
 //    an optional device status word.
 
 #include "../../include/tans_b200.h"
+#include "internal.h"
 
 #include <cuda.h>  // CUtensorMap and its enums (the encoder is resolved at run time)
 #include <cuda_bf16.h>
@@ -50,10 +51,6 @@
 #include <mutex>
 #include <utility>
 
-namespace tans_b200 {
-int fail(int code, const char *fmt, ...);
-void clear_error();
-}  // namespace tans_b200
 using tans_b200::fail;
 
 namespace {
@@ -235,7 +232,7 @@ __global__ void __launch_bounds__(1024) build_table_kernel(const int32_t *__rest
         const int64_t xp = (int64_t)fr[s] + rank;
         uint32_t entry = 0;
         if (xp > 0 && xp < 2 * kL) {
-            const int nb = 12 - (31 - __clz((uint32_t)xp));
+            const int nb = tans_b200::kTableLog - (31 - __clz((uint32_t)xp));
             if (nb >= 0) entry = (uint32_t)s | ((uint32_t)nb << 8) | (((uint32_t)xp << nb) << 16);
         }
         if (entry == 0 && status) atomicOr(status, TANS_B200_DATA_BAD_TABLE);

@@ -27,7 +27,7 @@ import os
 
 import torch
 
-from ._lib import LIB, check
+from ._lib import LIB, check, lib_for_table
 
 _L = 4096
 _BLOCK = 128
@@ -94,6 +94,15 @@ def _segments(n_fp8_per_stream: int, segment_pairs: int) -> int:
     return P // segment_pairs
 
 
+def _lib_for(n_entries: int, what: str):
+    """The library for a table of n_entries: the reference's L = 4096 build,
+    or the table_log 11 build (2048 entries, a labelled extra).  Other sizes
+    get the reference's check message."""
+    if n_entries not in (_L, _L // 2):
+        raise RuntimeError(f"{what} must have {_L} entries")
+    return lib_for_table(n_entries)
+
+
 def _streams_per_block_from_env() -> int:
     value = os.environ.get("TANS_STREAMS_PER_BLOCK")
     if not value:
@@ -123,7 +132,7 @@ def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: tor
          "input must be a contiguous CUDA uint8 [K, n] tensor")
     _req(freqs.dtype == torch.int32, "freqs must be int32")
     _req(spread.dtype == torch.int32, "spread must be int32")
-    _req(spread.numel() == _L, f"spread must have {_L} entries")
+    lib = _lib_for(spread.numel(), "spread")
     fr = freqs.detach().to("cpu").contiguous()
     sp = spread.detach().to("cpu").contiguous()
     K, n = inp.shape
@@ -136,7 +145,7 @@ def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: tor
     nblocks = (chains + _BLOCK - 1) // _BLOCK
     with torch.cuda.device(dev):
         wsb = ctypes.c_int64()
-        check(LIB.tans_b200_encode_device_workspace_bytes(K, n, kind, S, ctypes.byref(wsb)))
+        check(lib.tans_b200_encode_device_workspace_bytes(K, n, kind, S, ctypes.byref(wsb)), lib)
         ws = torch.empty(wsb.value, dtype=torch.uint8, device=dev)
         states = torch.empty(chains, dtype=torch.uint16, device=dev)
         partial = torch.empty(chains, dtype=torch.uint8, device=dev)
@@ -146,10 +155,10 @@ def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: tor
             shape = (P // tile, K, tile) if tile > 0 and P % tile == 0 else (P, K)
             sm = torch.empty(shape, dtype=torch.uint8, device=dev)
         st = _stream(dev)
-        check(LIB.tans_b200_encode_device_plan(
+        check(lib.tans_b200_encode_device_plan(
             inp.data_ptr(), kind, K, n, tile, S, fr.data_ptr(), fr.numel(), sp.data_ptr(),
             sm.data_ptr() if sm is not None else None, states.data_ptr(), partial.data_ptr(),
-            offsets.data_ptr(), ws.data_ptr(), st))
+            offsets.data_ptr(), ws.data_ptr(), st), lib)
         hdr = ws[:16].cpu()
         err, bad = (int(v) for v in hdr[:8].view(torch.int32))
         total = int(hdr[8:].view(torch.int64)[0])
@@ -158,8 +167,8 @@ def encode_device(inp: torch.Tensor, kind: int, freqs: torch.Tensor, spread: tor
         if err & _lib.ENC_TOO_LARGE:
             raise RuntimeError("encode: compressed size exceeds the int32 offsets of the format")
         comp = torch.empty(total, dtype=torch.uint8, device=dev)
-        check(LIB.tans_b200_encode_device_emit(kind, K, n, S, offsets.data_ptr(),
-                                               ws.data_ptr(), comp.data_ptr(), st))
+        check(lib.tans_b200_encode_device_emit(kind, K, n, S, offsets.data_ptr(),
+                                               ws.data_ptr(), comp.data_ptr(), st), lib)
     return comp, states, offsets, partial, sm
 
 
@@ -180,22 +189,22 @@ def tans_encode_interleaved(symbols: torch.Tensor, freqs: torch.Tensor, spread: 
     _req(symbols.is_contiguous() and not symbols.is_cuda, "symbols must be contiguous CPU")
     _req(freqs.is_contiguous() and not freqs.is_cuda, "freqs must be contiguous CPU")
     _req(spread.is_contiguous() and not spread.is_cuda, "spread must be contiguous CPU")
-    _req(spread.numel() == _L, f"spread must have {_L} entries")
+    lib = _lib_for(spread.numel(), "spread")
     K, N = symbols.shape
     h = ctypes.c_void_p()
-    check(LIB.tans_b200_encode(symbols.data_ptr(), K, N, freqs.data_ptr(), freqs.numel(),
-                               spread.data_ptr(), 0, ctypes.byref(h)))
+    check(lib.tans_b200_encode(symbols.data_ptr(), K, N, freqs.data_ptr(), freqs.numel(),
+                               spread.data_ptr(), 0, ctypes.byref(h)), lib)
     try:
         nbytes, nblocks = ctypes.c_int64(), ctypes.c_int64()
-        check(LIB.tans_b200_encoded_sizes(h, ctypes.byref(nbytes), ctypes.byref(nblocks)))
+        check(lib.tans_b200_encoded_sizes(h, ctypes.byref(nbytes), ctypes.byref(nblocks)), lib)
         comp = torch.empty(nbytes.value, dtype=torch.uint8)
         states = torch.empty(K, dtype=torch.uint16)
         offsets = torch.empty(nblocks.value + 1, dtype=torch.int32)
         partial = torch.empty(K, dtype=torch.uint8)
-        check(LIB.tans_b200_encoded_export(h, comp.data_ptr(), states.data_ptr(),
-                                           offsets.data_ptr(), partial.data_ptr()))
+        check(lib.tans_b200_encoded_export(h, comp.data_ptr(), states.data_ptr(),
+                                           offsets.data_ptr(), partial.data_ptr()), lib)
     finally:
-        LIB.tans_b200_encoded_free(h)
+        lib.tans_b200_encoded_free(h)
     return comp, states, offsets, partial
 
 
@@ -203,27 +212,29 @@ def tans_encode_interleaved(symbols: torch.Tensor, freqs: torch.Tensor, spread: 
 
 def build_decode_table_device(spread: torch.Tensor, freqs: torch.Tensor,
                               device: torch.device | None = None) -> torch.Tensor:
-    """Reference-format decode table int32[4096] on `device` (default: the
-    device of spread).  Built by a kernel from CUDA inputs, on the host from
-    CPU inputs (then copied)."""
+    """Reference-format decode table int32[L] on `device` (default: the
+    device of spread), L = spread.numel() (4096; 2048 for table_log 11).
+    Built by a kernel from CUDA inputs, on the host from CPU inputs (then
+    copied)."""
     _req(spread.dtype == torch.int32, "spread must be int32")
-    _req(spread.numel() == _L, f"spread must have {_L} entries")
+    lib = _lib_for(spread.numel(), "spread")
+    L = spread.numel()
     _req(freqs.dtype == torch.int32, "freqs must be int32")
     dev = device if device is not None else spread.device
     if spread.is_cuda and freqs.is_cuda and spread.device == dev and freqs.device == dev:
         _req(0 < freqs.numel() <= 256, "decode table alphabet must be 1..256 symbols")
         spread_c, freqs_c = spread.contiguous(), freqs.contiguous()
         with torch.cuda.device(dev):
-            table = torch.empty(_L, dtype=torch.int32, device=dev)
-            check(LIB.tans_b200_build_decode_table(spread_c.data_ptr(), freqs_c.data_ptr(),
+            table = torch.empty(L, dtype=torch.int32, device=dev)
+            check(lib.tans_b200_build_decode_table(spread_c.data_ptr(), freqs_c.data_ptr(),
                                                    freqs_c.numel(), table.data_ptr(),
-                                                   _status(dev).data_ptr(), _stream(dev)))
+                                                   _status(dev).data_ptr(), _stream(dev)), lib)
         return table
     sp = spread.detach().cpu().contiguous()
     fr = freqs.detach().cpu().contiguous()
-    table = torch.empty(_L, dtype=torch.int32)
-    check(LIB.tans_b200_build_decode_table_host(sp.data_ptr(), fr.data_ptr(), fr.numel(),
-                                                table.data_ptr()))
+    table = torch.empty(L, dtype=torch.int32)
+    check(lib.tans_b200_build_decode_table_host(sp.data_ptr(), fr.data_ptr(), fr.numel(),
+                                                table.data_ptr()), lib)
     return table.to(dev)
 
 
@@ -260,6 +271,7 @@ def gpu_tans_decode(compressed: torch.Tensor, offsets: torch.Tensor, states: tor
     _req(sign_mantissa.numel() == (N // 2) * K, "sign_mantissa has the wrong shape")
     dev = compressed.device
     _same_device(dev, offsets, states, partial_cnts, sign_mantissa)
+    lib = _lib_for(spread.numel(), "spread")
     with torch.cuda.device(dev):
         table = build_decode_table_device(spread, freqs, dev)
         out = torch.empty((N, K), dtype=torch.uint8, device=dev)
@@ -267,9 +279,9 @@ def gpu_tans_decode(compressed: torch.Tensor, offsets: torch.Tensor, states: tor
                 partial_cnts.data_ptr(), sign_mantissa.data_ptr(), table.data_ptr(),
                 out.data_ptr(), K, N)
         if S:
-            check(LIB.tans_b200_decode_split(*args, S, _status(dev).data_ptr(), _stream(dev)))
+            check(lib.tans_b200_decode_split(*args, S, _status(dev).data_ptr(), _stream(dev)), lib)
         else:
-            check(LIB.tans_b200_decode(*args, _status(dev).data_ptr(), _stream(dev)))
+            check(lib.tans_b200_decode(*args, _status(dev).data_ptr(), _stream(dev)), lib)
     _post_check(dev)
     return out
 
@@ -331,7 +343,7 @@ def fp8_vecadd_fused_tans(a_comp: torch.Tensor, a_offsets: torch.Tensor,
          "partial-count tensors must match state tensors")
     _req(a_comp.numel() % 4 == 0 and b_comp.numel() % 4 == 0,
          "compressed tensors must have byte lengths divisible by 4")
-    _req(decode_tbl.numel() == _L, f"decode_tbl must have {_L} entries")
+    lib = _lib_for(decode_tbl.numel(), "decode_tbl")
     N = int(n_fp8_per_stream)
     _req(N % (2 * _TILE_PAIRS) == 0, f"n_fp8_per_stream must be divisible by {2 * _TILE_PAIRS}")
     S = int(segment_pairs)
@@ -356,10 +368,10 @@ def fp8_vecadd_fused_tans(a_comp: torch.Tensor, a_offsets: torch.Tensor,
                 b_comp.data_ptr(), b_comp.numel(), b_offsets.data_ptr(), b_states.data_ptr(),
                 b_partial.data_ptr(), b_sm.data_ptr(), decode_tbl.data_ptr(), out.data_ptr(), K, N)
         if S:
-            check(LIB.tans_b200_fp8_vecadd_fused_split(*args, S, _status(dev).data_ptr(),
-                                                        _stream(dev)))
+            check(lib.tans_b200_fp8_vecadd_fused_split(*args, S, _status(dev).data_ptr(),
+                                                        _stream(dev)), lib)
         else:
-            check(LIB.tans_b200_fp8_vecadd_fused(*args, _status(dev).data_ptr(), _stream(dev)))
+            check(lib.tans_b200_fp8_vecadd_fused(*args, _status(dev).data_ptr(), _stream(dev)), lib)
     _post_check(dev)
     return out
 
@@ -389,8 +401,9 @@ def fp8_vecadd_fused_tans_host(a_comp: torch.Tensor, a_offsets: torch.Tensor,
         _req(not t.is_cuda and t.is_contiguous(), "host inputs must be contiguous CPU tensors")
     _req(a_states.dtype == torch.uint16 and b_states.dtype == torch.uint16, "states must be uint16")
     _req(a_offsets.dtype == torch.int32 and b_offsets.dtype == torch.int32, "offsets must be int32")
-    _req(decode_tbl.dtype == torch.int32 and decode_tbl.numel() == _L,
+    _req(decode_tbl.dtype == torch.int32 and decode_tbl.numel() in (_L, _L // 2),
          f"decode_tbl must be {_L} int32 entries")
+    lib = _lib_for(decode_tbl.numel(), "decode_tbl")
     N = int(n_fp8_per_stream)
     _req(N % (2 * _TILE_PAIRS) == 0, f"n_fp8_per_stream must be divisible by {2 * _TILE_PAIRS}")
     K = a_states.numel()
@@ -409,20 +422,21 @@ def fp8_vecadd_fused_tans_host(a_comp: torch.Tensor, a_offsets: torch.Tensor,
          out.dtype == torch.uint8, "out must be a contiguous CPU uint8 tensor of K*N bytes")
     with torch.cuda.device(dev):
         need = ctypes.c_int64()
-        check(LIB.tans_b200_fp8_vecadd_fused_host_workspace_bytes(
-            K, N, a_comp.numel(), b_comp.numel(), ctypes.byref(need)))
+        check(lib.tans_b200_fp8_vecadd_fused_host_workspace_bytes(
+            K, N, a_comp.numel(), b_comp.numel(), ctypes.byref(need)), lib)
         key = (dev.index, need.value)
         ws = _host_ws.get(key)
         if ws is None:
             _host_ws.clear()
             ws = torch.empty(need.value, dtype=torch.uint8, device=dev)
             _host_ws[key] = ws
-        check(LIB.tans_b200_fp8_vecadd_fused_host(
+        check(lib.tans_b200_fp8_vecadd_fused_host(
             a_comp.data_ptr(), a_comp.numel(), a_offsets.data_ptr(), a_states.data_ptr(),
             a_partial.data_ptr(), a_sm.data_ptr(),
             b_comp.data_ptr(), b_comp.numel(), b_offsets.data_ptr(), b_states.data_ptr(),
             b_partial.data_ptr(), b_sm.data_ptr(), decode_tbl.data_ptr(), out.data_ptr(), K, N,
-            int(chunk_streams), ws.data_ptr(), ws.numel(), _status(dev).data_ptr(), _stream(dev)))
+            int(chunk_streams), ws.data_ptr(), ws.numel(), _status(dev).data_ptr(), _stream(dev)),
+            lib)
     return out
 
 

@@ -10,6 +10,12 @@ nibble stored uncompressed (sm(2i) | sm(2i+1) << 4 per pair).  The heavy
 lifting (nibble split, tiling, slab encode) runs in C++ with OpenMP inside
 libtans_b200; table construction is vectorised numpy here.
 
+Table size: L = 4096 (table_log 12) is the reference's and the parity path.
+`encode(..., table_log=11)` is a labelled extra with a 2048-entry table
+(pair frequencies quantised to 2048, the same spread rule with its own
+stride); every op infers L from the spread / decode-table size and runs the
+library build for it.
+
 Wire format: each stream is a sequence of uint32 slabs filled LSB-first;
 the final partial slab stays LSB-aligned and `partial_cnts` gives its bit
 count; 128-stream blocks pad every stream to the block's slab count G_b with
@@ -27,6 +33,13 @@ L = 4096
 M = L
 SIGMA = (L >> 1) + (L >> 3) + 3  # hash-walk stride (odd, so it visits every slot)
 BLOCK_STREAMS = 128
+TABLE_LOGS = (12, 11)  # 12: the reference's L; 11: the labelled extra
+
+
+def _table_size(n: int) -> int:
+    if n not in [1 << t for t in TABLE_LOGS]:
+        raise AssertionError(f"freqs must sum to {L}")
+    return n
 
 
 def quantize_freqs(probs: np.ndarray, target: int = M) -> np.ndarray:
@@ -55,54 +68,59 @@ def quantize_freqs(probs: np.ndarray, target: int = M) -> np.ndarray:
 
 def build_spread(freqs: np.ndarray) -> np.ndarray:
     """Slot -> symbol map: the j-th placed symbol (symbols in order, symbol s
-    repeated f_s times) goes to slot (j * SIGMA) mod L."""
+    repeated f_s times) goes to slot (j * SIGMA) mod L, L = sum of freqs
+    (4096; 2048 for table_log 11, stride (L >> 1) + (L >> 3) + 3 likewise)."""
     f = np.asarray(freqs, dtype=np.int64)
-    if int(f.sum()) != L:
-        raise AssertionError(f"freqs must sum to {L}")
+    Lt = _table_size(int(f.sum()))
+    sigma = (Lt >> 1) + (Lt >> 3) + 3
     if (f < 0).any():
         # quantize_freqs can drive a zero-probability symbol to -1 when it has
         # to remove units (as the reference's does); the reference's spread
         # then trips its slot assertion
         raise AssertionError("freqs must be non-negative")
-    spread = np.full(L, -1, dtype=np.int32)
-    spread[(np.arange(L, dtype=np.int64) * SIGMA) % L] = np.repeat(
+    spread = np.full(Lt, -1, dtype=np.int32)
+    spread[(np.arange(Lt, dtype=np.int64) * sigma) % Lt] = np.repeat(
         np.arange(f.size, dtype=np.int32), f)
     return spread
 
 
 def build_decode_table(spread: np.ndarray, freqs: np.ndarray) -> torch.Tensor:
-    """[L] int32 decode table, entry = sym | nb << 8 | base << 16.
+    """[L] int32 decode table, entry = sym | nb << 8 | base << 16 (L =
+    spread size: 4096, or 2048 for table_log 11).
 
     For slot j holding symbol s with rank r among the slots of s (ascending
     slot order): x' = f_s + r, nb lifts x' into [L, 2L), base = x' << nb.  A
     decoder at state x = L + j reads nb bits and moves to base | bits."""
     sp = np.asarray(spread, dtype=np.int64)
     fr = np.asarray(freqs, dtype=np.int64)
-    if sp.size != L or sp.min() < 0 or sp.max() >= fr.size:
+    Lt = sp.size
+    if Lt not in [1 << t for t in TABLE_LOGS] or sp.min() < 0 or sp.max() >= fr.size:
         raise AssertionError("spread does not match freqs")
     counts = np.bincount(sp, minlength=fr.size)
     first = np.concatenate(([0], np.cumsum(counts)[:-1]))
     order = np.argsort(sp, kind="stable")
-    rank = np.empty(L, dtype=np.int64)
-    rank[order] = np.arange(L, dtype=np.int64) - np.repeat(first, counts)
+    rank = np.empty(Lt, dtype=np.int64)
+    rank[order] = np.arange(Lt, dtype=np.int64) - np.repeat(first, counts)
     xp = fr[sp] + rank
     if (xp <= 0).any():
         raise AssertionError("spread does not match freqs")
-    nb = 12 - (np.frexp(xp.astype(np.float64))[1] - 1)
+    nb = (Lt.bit_length() - 1) - (np.frexp(xp.astype(np.float64))[1] - 1)
     base = xp << nb
-    if not ((base >= L) & (base < 2 * L)).all():
+    if not ((base >= Lt) & (base < 2 * Lt)).all():
         raise AssertionError("spread does not match freqs")
     table = ((sp & 0xFF) | (nb << 8) | (base << 16)).astype(np.uint32)
     return torch.from_numpy(table.view(np.int32))
 
 
-def pair_freqs_from_exponents(exp_freqs) -> np.ndarray:
+def pair_freqs_from_exponents(exp_freqs, table_log: int = 12) -> np.ndarray:
     """Pair-symbol frequencies from 16 exponent weights: the outer product of
     the normalised nibble probabilities (float32, as the reference computes
-    them), quantised to sum to M."""
+    them), quantised to sum to M = 2^table_log (4096 in the reference)."""
+    if table_log not in TABLE_LOGS:
+        raise AssertionError(f"table_log must be one of {TABLE_LOGS}")
     probs = torch.as_tensor(exp_freqs).float().numpy()
     probs = probs / probs.sum()
-    return quantize_freqs((probs[:, None] * probs[None, :]).flatten(), target=M)
+    return quantize_freqs((probs[:, None] * probs[None, :]).flatten(), target=1 << table_log)
 
 
 def split_fp8(fp8_bytes: torch.Tensor, tile: int = 0, want_hist: bool = False):
@@ -128,6 +146,7 @@ def encode(
     exp_freqs: torch.Tensor,
     tile: int = 0,
     segment_pairs: int = 0,
+    table_log: int = 12,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor,
            torch.Tensor, torch.Tensor, torch.Tensor]:
     """tANS encode FP8 bytes [K, N] (pair alphabet).
@@ -148,6 +167,10 @@ def encode(
     pair-symbol matrix rearranged that way; sm_packed keeps the unsplit
     layout.  Long streams then decode as N/2/S times as many chains
     (gpu_tans_decode / fp8_vecadd_fused_tans with segment_pairs=S).
+
+    table_log = 11 (a labelled extra; the reference has only 12): pair
+    frequencies sum to 2048 and spread has 2048 entries; the decode ops
+    recognise that size and use the 2048-entry library build.
     """
     assert fp8_bytes.dim() == 2 and fp8_bytes.dtype == torch.uint8
     K, N = fp8_bytes.shape
@@ -158,7 +181,7 @@ def encode(
     if segment_pairs:
         assert segment_pairs > 0 and (N // 2) % segment_pairs == 0, \
             f"segment_pairs={segment_pairs} must divide n_pairs={N // 2}"
-    pair_freqs = pair_freqs_from_exponents(exp_freqs)
+    pair_freqs = pair_freqs_from_exponents(exp_freqs, table_log)
     spread = build_spread(pair_freqs)
     pair_freqs_t = torch.from_numpy(pair_freqs)
     spread_t = torch.from_numpy(spread)
