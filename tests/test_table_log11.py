@@ -89,13 +89,14 @@ def test_l11_gpu_decode_and_fused_add(K, N):
     assert torch.equal(a[6], b[6]) and a[6].numel() == 2048
     tbl = tans_codec.build_decode_table(a[6].numpy(), a[5].numpy()).to(dev)
     _C.data_status(dev)
-    fused = _C.fp8_vecadd_fused_tans(*[t.to(dev) for t in a[:5]], *[t.to(dev) for t in b[:5]],
-                                     tbl, N)
+    def parts(e):  # encode's (comp, states, offsets, partial, sm) in the ops' order
+        return [e[i].to(dev) for i in (0, 2, 1, 3, 4)]
+    fused = _C.fp8_vecadd_fused_tans(*parts(a), *parts(b), tbl, N)
     raw = _C.fp8_vecadd_raw(x.T.contiguous().view(-1).to(dev), y.T.contiguous().view(-1).to(dev))
     want = raw.view(N // 16, 16, K).permute(0, 2, 1).reshape(-1)
     assert torch.equal(fused, want)
     d = tans_codec.encode(x, hist, tile=0, table_log=11)
-    out = _C.gpu_tans_decode(*[t.to(dev) for t in d[:5]], d[6].to(dev), d[5].to(dev), N)
+    out = _C.gpu_tans_decode(*parts(d), d[6].to(dev), d[5].to(dev), N)
     assert torch.equal(out.cpu(), x.T.contiguous())
     assert _C.data_status(dev) == 0
 
