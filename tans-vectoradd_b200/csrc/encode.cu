@@ -59,7 +59,7 @@ constexpr int kScanThreads = 1024;
 // Workspace layout (bytes).  The header is the public tans_b200_enc_header.
 constexpr int kInfoCopies = 4;
 constexpr size_t kWsInfo = 16;                                 // uint32[256][4] packed delta/base
-constexpr size_t kWsNext = kWsInfo + 256 * 4 * kInfoCopies;    // uint16[4096]
+constexpr size_t kWsNext = kWsInfo + 256 * 4 * kInfoCopies;    // uint16[L]
 constexpr size_t kWsSlabs = 12544;                             // uint32[K]: slabs per stream
 static_assert(kWsNext + kL * 2 <= kWsSlabs, "workspace tables overlap");
 

@@ -185,18 +185,20 @@ __global__ void __launch_bounds__(kStreamThreads) vecadd_raw_kernel(const uint4 
 
 // ------------------------------------------------------ decode-table build
 
-// One CTA of 1024 threads.  Warp w owns slots [128w, 128w+128).  A symbol's
-// rank at a slot is the number of earlier slots holding it: per-warp
-// histograms, an exclusive scan across warps, then in-warp ranks from
-// __match_any_sync, processed in slot order.
-__global__ void __launch_bounds__(1024) build_table_kernel(const int32_t *__restrict__ spread,
+// One CTA of kBuildWarps warps (L / 4 threads: 1024 for L = 4096).  Warp w
+// owns slots [128w, 128w+128).  A symbol's rank at a slot is the number of
+// earlier slots holding it: per-warp histograms, an exclusive scan across
+// warps, then in-warp ranks from __match_any_sync, processed in slot order.
+constexpr int kBuildWarps = kL / 128;
+static_assert(kBuildWarps * 128 == kL && kBuildWarps <= 32, "table builder geometry");
+__global__ void __launch_bounds__(kBuildWarps * 32) build_table_kernel(const int32_t *__restrict__ spread,
                                                            const int32_t *__restrict__ freqs,
                                                            int n_syms, int32_t *__restrict__ table,
                                                            int32_t *__restrict__ status) {
-    __shared__ uint32_t cnt[32][256];
+    __shared__ uint32_t cnt[kBuildWarps][256];
     __shared__ int32_t fr[256];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    for (int i = tid; i < 32 * 256; i += blockDim.x) (&cnt[0][0])[i] = 0;
+    for (int i = tid; i < kBuildWarps * 256; i += blockDim.x) (&cnt[0][0])[i] = 0;
     if (tid < 256) fr[tid] = tid < n_syms ? freqs[tid] : 0;
     __syncthreads();
     int sym[4];
@@ -213,7 +215,7 @@ __global__ void __launch_bounds__(1024) build_table_kernel(const int32_t *__rest
     __syncthreads();
     if (tid < 256) {  // exclusive scan over warps for symbol tid
         uint32_t run = 0;
-        for (int w = 0; w < 32; w++) {
+        for (int w = 0; w < kBuildWarps; w++) {
             uint32_t v = cnt[w][tid];
             cnt[w][tid] = run;
             run += v;
@@ -2468,8 +2470,8 @@ extern "C" int tans_b200_build_decode_table(const int32_t *spread, const int32_t
     int sms;
     int rc = device_setup(&sms);
     if (rc) return rc;
-    build_table_kernel<<<1, 1024, 0, (cudaStream_t)stream>>>(spread, freqs, (int)n_syms, table,
-                                                             status);
+    build_table_kernel<<<1, kBuildWarps * 32, 0, (cudaStream_t)stream>>>(spread, freqs, (int)n_syms,
+                                                                         table, status);
     return launch_status("build_table_kernel");
 }
 
@@ -3118,7 +3120,7 @@ extern "C" int tans_b200_decode_noalloc(const uint8_t *compressed, int64_t compr
     rc = noalloc_table(&table);
     if (rc) return rc;
     cudaStream_t st = (cudaStream_t)stream;
-    build_table_kernel<<<1, 1024, 0, st>>>(spread, freqs, (int)n_syms, table, status);
+    build_table_kernel<<<1, kBuildWarps * 32, 0, st>>>(spread, freqs, (int)n_syms, table, status);
     rc = launch_status("build_table_kernel");
     if (rc) return rc;
     DecodeArgs args{reinterpret_cast<const uint32_t *>(compressed), compressed_bytes, offsets,
