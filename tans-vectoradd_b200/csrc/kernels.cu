@@ -528,9 +528,9 @@ Geometry balance(int64_t n_groups, int sms, int max_warps_per_cta) {
 
 constexpr int kTableBytes = kL * kCopies * 4;
 constexpr int kMaxWarps = 16;  // 512 threads per CTA, one CTA per SM
-// The decode kernel: up to 6 teams of 4 warps (its registers fit 768
-// threads without spills; cfg2: 2.82 ms vs 2.92 ms with 4 teams)
-constexpr int kDecodeMaxWarps = 24;
+// The decode kernel: up to 7 teams of 4 warps (its registers fit 896
+// threads, 72 each, without spills)
+constexpr int kDecodeMaxWarps = 28;
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
     return (uint32_t)__cvta_generic_to_shared(p);
