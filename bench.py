@@ -64,6 +64,8 @@ def parse():
                     "container (save/load of encoded tensors)")
     ap.add_argument("--container-log2", type=int, default=30,
                     help="log2 e4m3 bytes saved and loaded by --workload container")
+    ap.add_argument("--gemm-batches", default="16,64,256,512,2048",
+                    help="--workload gemm: comma-separated token counts")
     ap.add_argument("--decode-log2", type=int, default=32,
                     help="log2 fp8 elements (decode, encode)")
     ap.add_argument("--layers", type=int, default=40, help="layers of the GEMV stack")
@@ -729,7 +731,7 @@ def run_gemm(args, dev, barrier):
             "dense_decode_us": round(ms_dec * 1e3, 2),
             "dense_decode_gbs_e4m3": round(R * C / (ms_dec / 1e3) / 1e9, 1),
             "dense_exact": exact, "batches": []}
-    for B in (16, 64, 256, 512, 2048):
+    for B in [int(b) for b in args.gemm_batches.split(",")]:
         g = torch.Generator(device=dev).manual_seed(B)
         x = torch.randn(B, C, device=dev, generator=g).to(torch.bfloat16)
         y = tans_gemv.gemm(enc, x)

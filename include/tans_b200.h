@@ -319,8 +319,9 @@ int tans_b200_gemv_gather(const uint8_t *compressed, int64_t compressed_bytes,
  * scale * W @ x^T for x bf16 [m][cols] (16-byte aligned), W in the GEMV
  * stream format (tans_b200_gemv).  Tensor cores (tcgen05.mma, bf16 in, fp32
  * accumulate in tensor memory); W never goes through HBM decoded.
- * rows % 128 == 0; tokens are processed 256 per CTA (the weight is decoded
- * once per 256 tokens).  A bounded wait that runs out ORs
+ * rows % 128 == 0; up to 256 tokens one CTA per 128-row block decodes the
+ * weight once; above that, when rows / 128 is even, CTA pairs on 2-SM MMAs
+ * decode it once per 512 tokens (else once per 256).  A bounded wait that runs out ORs
  * TANS_B200_DATA_TIMEOUT into the optional status word (no result for that
  * CTA's rows).  No reference
  * counterpart. */
