@@ -874,6 +874,54 @@ def stack_cfg4(args, ws, rank, dev, barrier):
     return None
 
 
+def stack_per_rank_compute(args, dev, barrier, shards=(2, 4, 8)):
+    """The GEMV work one rank of an S-way row-sharded cfg4 stack does, run
+    alone on this GPU (no gather): per layer its up shard [F/S x H] on x
+    [B, H] and its down shard [H/S x F] on a full-width h [B, F], the
+    forward captured in one CUDA graph.  Set beside stack_cfg4 at N = S it
+    separates the per-rank compute from the gather and the rank skew."""
+    from rans_vectoradd import tans_gemv
+    H, F, B = 5120, 17408, args.batch
+    stream = torch.cuda.current_stream(dev)
+    out = {}
+    for S in shards:
+        fr, hr = F // S, H // S
+        ups = [make_gemv_weight(fr, H, 1000 * l, dev, None)[0] for l in range(args.layers)]
+        downs = [make_gemv_weight(hr, F, 1000 * l + 500, dev, None)[0] for l in range(args.layers)]
+        g = torch.Generator(device=dev).manual_seed(7)
+        x = torch.randn(B, H, device=dev, generator=g).to(torch.bfloat16)
+        h = torch.randn(B, F, device=dev, generator=g).to(torch.bfloat16)
+        yf = torch.empty((B, fr), dtype=torch.bfloat16, device=dev)
+        yh = torch.empty((B, hr), dtype=torch.bfloat16, device=dev)
+        pu = torch.empty((ups[0].col_splits, B, fr), dtype=torch.float32, device=dev)
+        pd = torch.empty((downs[0].col_splits, B, hr), dtype=torch.float32, device=dev)
+
+        def forward():
+            for up, down in zip(ups, downs):
+                tans_gemv.gemv(up, x, yf, pu if up.col_splits > 1 else None)
+                tans_gemv.gemv(down, h, yh, pd if down.col_splits > 1 else None)
+
+        for _ in range(2):
+            forward()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                forward()
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        steps = max(3, args.steps // 2)
+        ms = timed(graph.replay, steps, 2, stream, barrier) / steps
+        out[str(S)] = {"ms_per_forward": round(ms, 4),
+                       "us_per_gemv": round(ms / (2 * args.layers) * 1e3, 2),
+                       "col_splits_up_down": [ups[0].col_splits, downs[0].col_splits]}
+        del graph, ups, downs
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_stack(args, ws, rank, dev, barrier):
     r = stack_cfg4(args, ws, rank, dev, barrier)
     if r is not None:
@@ -1164,6 +1212,8 @@ def main():
         extras["stack_cfg4"] = stack_cfg4(args, ws, rank, dev, barrier)
         torch.cuda.empty_cache()
         if rank == 0 and ws == 1:
+            extras["stack_cfg4_per_rank_compute"] = stack_per_rank_compute(args, dev, barrier)
+            torch.cuda.empty_cache()
             extras["table_log_11"] = table_log11_extra(args, x, y, N, raw_step, stream, barrier,
                                                        dev)
             torch.cuda.empty_cache()
