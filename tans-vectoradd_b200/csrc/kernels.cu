@@ -669,10 +669,82 @@ __device__ __forceinline__ void chain_step2_global(Chain &ch, const uint8_t *tb,
           "r"(kUnit == 64 ? q.back64 : q.back), "l"(ch.src), "n"(512 / kUnit));
 }
 
-// NP pair steps (NP % 4 == 0), pair symbols packed four to a word.
+// Refill from a register window (a tile that cannot use the ring): win[0]
+// is the next row of this stream, win[1] the one below it, ...; a refill
+// takes win[0] and shifts the window down by one row.  kUnit as for
+// chain_step2_ring (v counts rows in units of kUnit); NW = 6 covers 16
+// steps, NW = 3 covers 8.
+template <int kUnit, int NW>
+__device__ __forceinline__ void chain_step2_window(Chain &ch, const uint8_t *tb, const Opq &q,
+                                                   uint32_t (&win)[NW], uint32_t &e1, uint32_t &e2) {
+    static_assert(NW == 3 || NW == 6, "window of 3 or 6 rows");
+    e1 = *reinterpret_cast<const uint32_t *>(tb + ch.addr);
+    uint32_t w, a1;
+    TANS_STEP2_FIRST;
+    e2 = *reinterpret_cast<const uint32_t *>(tb + a1);
+    uint32_t pa;
+    asm volatile(
+        "{\n\t.reg .u32 w2, b, f, c, t;\n\t.reg .pred pa;\n\t"
+        "shf.l.wrap.b32 w2, 0, %7, %6;\n\t"  /* w << nb1 */
+        "shf.l.wrap.b32 b, w2, 0, %8;\n\t"   /* bits2 */
+        "mul.hi.u32 f, %8, %10;\n\t"
+        "mad.lo.u32 %0, b, %11, f;\n\t"      /* next entry */
+        "mad.lo.u32 c, %6, %9, %1;\n\t"      /* cnt + e1 + e2: bit 5 flips per slab */
+        "mad.lo.u32 c, %8, %9, c;\n\t"
+        "xor.b32 t, c, %1;\n\t"
+        "and.b32 t, t, 32;\n\t"
+        "setp.ne.u32 pa, t, 0;\n\t"
+        "mov.u32 %1, c;\n\t"
+        "@pa mad.lo.u32 %2, %3, %9, 0;\n\t"  /* hi <- lo */
+        "@pa mad.lo.s32 %4, %9, %12, %4;\n\t" /* one row down */
+        "selp.b32 %5, 1, 0, pa;\n\t"
+        "}"
+        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.v), "=r"(pa)
+        : "r"(e1), "r"(w), "r"(e2), "r"(q.one), "r"(q.p16), "r"(q.step),
+          "r"(kUnit == 64 ? q.back64 : q.back));
+    if (pa) {  // lo <- win[0], the window moves down one row
+        ch.lo = win[0];
+#pragma unroll
+        for (int k = 0; k + 1 < NW; k++) win[k] = win[k + 1];
+    }
+}
+
+// This lane's rows row .. row - NW + 1 of its stream (row = the next row it
+// refills from; rows below the block's first read as 0 and are never
+// consumed), loaded together.
+template <int kUnit, int NW>
+__device__ __forceinline__ void chain_window_load(const Chain &ch, const Opq &q, uint32_t (&win)[NW]) {
+    int32_t r;
+    asm("mul.hi.s32 %0, %1, %2;" : "=r"(r) : "r"(ch.v), "r"(kUnit == 64 ? q.p26 : q.p25));
+    const uint8_t *col = reinterpret_cast<const uint8_t *>(ch.src);  // row 0 of its column
+#pragma unroll
+    for (int k = 0; k < NW; k++)
+        win[k] = r - k >= 0 ? __ldg(reinterpret_cast<const uint32_t *>(col + (int64_t)(r - k) * 512)) : 0u;
+}
+
+// Row of a 64-unit v, on the FMA pipe (arithmetic: rows below 0 stay negative).
+__device__ __forceinline__ int32_t row_of(int32_t v, const Opq &q) {
+    int32_t r;
+    asm("mul.hi.s32 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(q.p26));
+    return r;
+}
+// Row of a 128-unit v.
+__device__ __forceinline__ int32_t row_of128(int32_t v, const Opq &q) {
+    int32_t r;
+    asm("mul.hi.s32 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(q.p25));
+    return r;
+}
+
+// NP pair steps (NP % 4 == 0), pair symbols packed four to a word.  Without
+// the ring, the tile first loads every row its refills can reach (NP steps
+// refill at most 3 NP / 8 times; rows below the block's first read as 0 and
+// are never consumed) with independent loads, so it pays one memory round
+// trip instead of one per refill.
 template <bool kRing, int NP>
 __device__ __forceinline__ void chain_tile(Chain &ch, const uint8_t *tb, uint32_t ring_lane,
                                            const Opq &q, uint32_t (&S)[NP / 4]) {
+    uint32_t win[6];
+    if (!kRing) chain_window_load<64, 6>(ch, q, win);
 #pragma unroll
     for (int j = 0; j < NP / 4; j++) {
         uint32_t e0, e1, e2, e3;
@@ -680,8 +752,8 @@ __device__ __forceinline__ void chain_tile(Chain &ch, const uint8_t *tb, uint32_
             chain_step2_ring<64>(ch, tb, ring_lane, q.rmask, q, e0, e1);
             chain_step2_ring<64>(ch, tb, ring_lane, q.rmask, q, e2, e3);
         } else {
-            chain_step2_global<64>(ch, tb, q, e0, e1);
-            chain_step2_global<64>(ch, tb, q, e2, e3);
+            chain_step2_window<64, 6>(ch, tb, q, win, e0, e1);
+            chain_step2_window<64, 6>(ch, tb, q, win, e2, e3);
         }
         S[j] = gather_syms(e0, e1, e2, e3);
     }
@@ -702,19 +774,6 @@ __device__ __forceinline__ int32_t chain_init64(Chain &ch, const uint32_t *__res
     row0 = (G > 0 && base % 512 == 0) ? (int32_t)(base / 512) : -1;
     ch.v = (G - 3) * 64;
     return G;
-}
-
-// Row of a 64-unit v, on the FMA pipe (arithmetic: rows below 0 stay negative).
-__device__ __forceinline__ int32_t row_of(int32_t v, const Opq &q) {
-    int32_t r;
-    asm("mul.hi.s32 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(q.p26));
-    return r;
-}
-// Row of a 128-unit v.
-__device__ __forceinline__ int32_t row_of128(int32_t v, const Opq &q) {
-    int32_t r;
-    asm("mul.hi.s32 %0, %1, %2;" : "=r"(r) : "r"(v), "r"(q.p25));
-    return r;
 }
 
 // Per-tile upkeep of one warp's ring of 128-byte rows (one chain per lane):
@@ -881,10 +940,12 @@ __global__ void __launch_bounds__(kDecodeMaxWarps * 32, 1) decode_kernel(const D
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j += 2)
                     chain_step2_ring<128>(ch, tb, ring_lane, mask, p.q, e[j], e[j + 1]);
-            } else {
+            } else {  // rows from a register window loaded at once (8 steps: 3 rows at most)
+                uint32_t win[3];
+                chain_window_load<128, 3>(ch, p.q, win);
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j += 2)
-                    chain_step2_global<128>(ch, tb, p.q, e[j], e[j + 1]);
+                    chain_step2_window<128, 3>(ch, tb, p.q, win, e[j], e[j + 1]);
             }
             const uint32_t M0 = quad_transpose(w0, sel1, sel2);
             const uint32_t M1 = quad_transpose(w1, sel1, sel2);
@@ -926,9 +987,11 @@ __global__ void __launch_bounds__(kDecodeMaxWarps * 32, 1) decode_kernel(const D
                 for (int j = 0; j < kTablePairs; j += 2)
                     chain_step2_ring<128>(ch, tb, ring_lane, mask, p.q, s8[j], s8[j + 1]);
             } else {
+                uint32_t win[3];
+                chain_window_load<128, 3>(ch, p.q, win);
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j += 2)
-                    chain_step2_global<128>(ch, tb, p.q, s8[j], s8[j + 1]);
+                    chain_step2_window<128, 3>(ch, tb, p.q, win, s8[j], s8[j + 1]);
             }
             if (active) {
 #pragma unroll
@@ -1516,11 +1579,14 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
                     chain_step2_ring<128>(ca, tb, lane_a, mask, p.q, ea[j], ea[j + 1]);
                     chain_step2_ring<128>(cb, tb, lane_b, mask, p.q, eb[j], eb[j + 1]);
                 }
-            } else {
+            } else {  // rows from register windows loaded at once (8 steps: 3 rows at most)
+                uint32_t wa[3], wb[3];
+                chain_window_load<128, 3>(ca, p.q, wa);
+                chain_window_load<128, 3>(cb, p.q, wb);
 #pragma unroll
                 for (int j = 0; j < kTablePairs; j += 2) {
-                    chain_step2_global<128>(ca, tb, p.q, ea[j], ea[j + 1]);
-                    chain_step2_global<128>(cb, tb, p.q, eb[j], eb[j + 1]);
+                    chain_step2_window<128, 3>(ca, tb, p.q, wa, ea[j], ea[j + 1]);
+                    chain_step2_window<128, 3>(cb, tb, p.q, wb, eb[j], eb[j + 1]);
                 }
             }
             uint32_t wa[4], wb[4];
@@ -2179,8 +2245,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) gemm_tc_kernel(const __grid_con
                 for (int j = 0; j < kTablePairs; j += 2)
                     chain_step2_ring<128>(ch, tb, ring_lane, mask, p.q, e[j], e[j + 1]);
             } else {
+                uint32_t win[3];
+                chain_window_load<128, 3>(ch, p.q, win);
 #pragma unroll
-                for (int j = 0; j < kTablePairs; j += 2) chain_step2_global<128>(ch, tb, p.q, e[j], e[j + 1]);
+                for (int j = 0; j < kTablePairs; j += 2) chain_step2_window<128, 3>(ch, tb, p.q, win, e[j], e[j + 1]);
             }
             uint32_t wd[4];
             compose_pairs(gather_syms(e[0], e[1], e[2], e[3]), m.x, p.q, wd[0], wd[1]);

@@ -186,6 +186,30 @@ def test_gemm_tc_matches_reference(cuda, R, C, B, KS):
     assert tans_gemv.rel_err(y, ref) <= TOL
 
 
+def skewed_weight(R, C, seed):
+    """e4m3 rows that alternate between one repeated byte (few bits per pair)
+    and exponents uniform over all 16 values (up to 12 bits per pair), NaN
+    bytes excluded: the lanes of a warp drift apart in their slab rows and
+    the kernels take their register-window refill fallback."""
+    from rans_vectoradd.data import random_fp8_bytes
+    g = torch.Generator().manual_seed(seed)
+    w8 = random_fp8_bytes(R * C, device="cpu", generator=g, exp_probs=tuple([1.0] * 16)).reshape(R, C)
+    w8[(w8 & 0x7F) == 0x7F] = 0x7E
+    w8[0::2] = 0x38  # 1.0
+    return w8, torch.full((R,), 1.0 / 448.0)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("R,C,KS,B", [(256, 8192, 1, 8), (1024, 16384, 2, 3)])
+def test_gemv_skewed_rows_fallback(cuda, R, C, KS, B):
+    w8, s = skewed_weight(R, C, R + C)
+    enc = tans_gemv.encode_weight(w8.to(cuda), s.to(cuda), col_splits=KS)
+    x = torch.randn(B, C, generator=torch.Generator().manual_seed(B)).to(torch.bfloat16).to(cuda)
+    ref = tans_gemv.reference_gemv(w8.to(cuda), s.to(cuda), x)
+    assert tans_gemv.rel_err(tans_gemv.gemv(enc, x), ref) <= TOL
+    assert tans_gemv.rel_err(tans_gemv.gemm_tc(enc, x), ref) <= TOL
+
+
 class _LocalGather:
     """A gather descriptor over local buffers only (one GPU): `world` ranks
     whose gathered buffers and flag arrays all live on this device."""
