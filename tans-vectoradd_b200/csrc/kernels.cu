@@ -646,29 +646,6 @@ __device__ __forceinline__ void chain_step2_ring(Chain &ch, const uint8_t *tb, u
           "r"(kUnit == 64 ? q.back64 : q.back), "r"(mask), "r"(ring_lane));
 }
 
-// Refill from global memory (any row, any time); past the block's first row
-// nothing is loaded and lo keeps a stale word whose bits are never consumed.
-template <int kUnit>
-__device__ __forceinline__ void chain_step2_global(Chain &ch, const uint8_t *tb, const Opq &q,
-                                                   uint32_t &e1, uint32_t &e2) {
-    e1 = *reinterpret_cast<const uint32_t *>(tb + ch.addr);
-    uint32_t w, a1;
-    TANS_STEP2_FIRST;
-    e2 = *reinterpret_cast<const uint32_t *>(tb + a1);
-    asm volatile(
-        "{\n\t.reg .u32 w2, b, f, c, t;\n\t.reg .pred pa, pl;\n\t.reg .u64 ga;\n\t" TANS_STEP2_HEAD
-        "setp.ge.and.s32 pl, %4, 0, pa;\n\t"
-        "mul.wide.s32 ga, %4, %13;\n\t"   /* 512 / kUnit bytes per unit of v */
-        "add.u64 ga, ga, %12;\n\t"
-        "@pa mad.lo.u32 %2, %3, %8, 0;\n\t"    /* hi <- lo */
-        "@pl ld.global.nc.u32 %3, [ga];\n\t"   /* lo <- next row of this stream */
-        "@pa mad.lo.s32 %4, %8, %11, %4;\n\t"  /* one row down */
-        "}"
-        : "+r"(ch.addr), "+r"(ch.cnt), "+r"(ch.hi), "+r"(ch.lo), "+r"(ch.v)
-        : "r"(e1), "r"(w), "r"(e2), "r"(q.one), "r"(q.p16), "r"(q.step),
-          "r"(kUnit == 64 ? q.back64 : q.back), "l"(ch.src), "n"(512 / kUnit));
-}
-
 // Refill from a register window (a tile that cannot use the ring): win[0]
 // is the next row of this stream, win[1] the one below it, ...; a refill
 // takes win[0] and shifts the window down by one row.  kUnit as for
