@@ -270,7 +270,7 @@ def gemm_tc(weight: EncodedWeight, x: torch.Tensor, out: torch.Tensor | None = N
 def raw_col_splits(rows: int, cols: int, sms: int = 148) -> int:
     """Column slices of the uncompressed GEMV: the fewest that divide the
     64-column chunks and give about 4.5 CTAs (128 rows each) per SM (best of
-    a sweep over slices and grid shapes on the cfg3 matrices)."""
+    a sweep over slices and grid shapes on [17408 x 5120] and [5120 x 17408])."""
     chunks = cols // 64
     for d in range(1, chunks + 1):
         if chunks % d == 0 and (rows + 127) // 128 * d * 2 >= 9 * sms:
