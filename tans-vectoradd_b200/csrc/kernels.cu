@@ -1417,33 +1417,78 @@ __device__ __forceinline__ void compose_pairs(uint32_t S, uint32_t M, const Opq 
 
 constexpr int kGemvMaxWarps = 20;
 
+// One warp's row group of the GEMV: its two chains (a: rows g, b: rows
+// g + 8), their slab rings and the first sign/mantissa words.  Set up from
+// the weight alone (nothing an earlier kernel writes).
+struct GemvGroup {
+    Chain ca, cb;
+    PairRing ra, rb;
+    const uint8_t *src_a, *src_b;
+    const uint8_t *spa, *spb;  // this tile's sign/mantissa words
+    uint2 sa_n, sb_n;          // ... loaded one tile ahead
+    bool live, on;
+};
+
+template <int R>
+__device__ __forceinline__ void gemv_group_start(const GemvArgs &p, int64_t w, int k, int lane,
+                                                 uint32_t lane_off, uint32_t dst_a, uint32_t dst_b,
+                                                 int32_t n_tiles, GemvGroup &gs) {
+    const uint32_t full = 0xffffffffu;
+    const uint32_t mask = (uint32_t)(R - 1) << 7;
+    const int64_t sa_id = ((w * p.KS + k) * 2 + 0) * 32 + lane;
+    const int64_t sb_id = sa_id + 32;
+    const int32_t ga = chain_init(gs.ca, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
+                                  sa_id, lane_off, p.status);
+    const int32_t gb = chain_init(gs.cb, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
+                                  sb_id, lane_off, p.status);
+    gs.live = ga > 0 && gb > 0;
+    // row 0 of each chain's 32 stream columns, copied 16 bytes at a time
+    // when every lane is live and it is 16-byte aligned
+    const uintptr_t r0a = reinterpret_cast<uintptr_t>(gs.ca.src) - 4u * lane;
+    const uintptr_t r0b = reinterpret_cast<uintptr_t>(gs.cb.src) - 4u * lane;
+    const int32_t Ga = __reduce_max_sync(full, gs.live ? ga : 0);
+    const int32_t Gb = __reduce_max_sync(full, gs.live ? gb : 0);
+    gs.on = __all_sync(full, gs.live && ((r0a | r0b) & 15u) == 0);
+    if (!gs.live) {
+        chain_idle(gs.ca, p.comp);
+        chain_idle(gs.cb, p.comp);
+    }
+    gs.src_a = reinterpret_cast<const uint8_t *>(r0a) + 16 * (lane & 7);
+    gs.src_b = reinterpret_cast<const uint8_t *>(r0b) + 16 * (lane & 7);
+    gs.ra.fill = Ga - 3;
+    gs.rb.fill = Gb - 3;
+    gs.ra.done0 = gs.ra.done1 = Ga >= 3 ? Ga - 2 : INT_MIN;
+    gs.rb.done0 = gs.rb.done1 = Gb >= 3 ? Gb - 2 : INT_MIN;
+    if (gs.on) {
+        // the first rows: three fills of four per chain in one copy group;
+        // the first tile's cp.async.wait_group 1 (after it commits its own
+        // fills) covers this group before any lane reads the ring
+#pragma unroll
+        for (int i = 0; i < 3; i++) {
+            gs.ra.fill = ring_fill16<128>(gs.ra.fill, -1, true, lane, gs.src_a, dst_a, mask);
+            gs.rb.fill = ring_fill16<128>(gs.rb.fill, -1, true, lane, gs.src_b, dst_b, mask);
+        }
+        cp_async_commit();
+        gs.ra.done0 = gs.ra.done1 = gs.ra.fill < 0 ? INT_MIN : gs.ra.fill + 1;
+        gs.rb.done0 = gs.rb.done1 = gs.rb.fill < 0 ? INT_MIN : gs.rb.fill + 1;
+    }
+    __syncwarp();
+    gs.spa = p.sm + sa_id * 8;
+    gs.spb = p.sm + sb_id * 8;
+    gs.sa_n = gs.sb_n = make_uint2(0, 0);
+    if (gs.live && n_tiles > 0) {
+        gs.sa_n = ld_stream_v2(gs.spa);
+        gs.sb_n = ld_stream_v2(gs.spb);
+    }
+}
+
 template <int R>
 __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvArgs p) {
     extern __shared__ __align__(16) uint8_t smem[];
     pdl_trigger();
-    // the table is this weight's own (not written by the kernel before this
-    // one): load it while that kernel may still run, then wait for it
-    load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
-    pdl_wait();
-    if (p.wait_n > 0) {  // x is gathered by the peers' epilogues: wait for all of them
-        if (threadIdx.x == 0 && !peer_wait(p.wait_flags, *p.wait_seq, p.wait_n) && p.status)
-            atomicOr(p.status, TANS_B200_DATA_TIMEOUT);
-        __syncthreads();
-    }
     const int64_t CS = p.C / p.KS;
     const int k = blockIdx.y;
     const int64_t pitch = CS + 8;  // halves
-    uint16_t *xs = reinterpret_cast<uint16_t *>(smem + kTableBytes);
-    // x slice -> f16 in shared memory (rows >= B are zero)
-    for (int b = 0; b < kGemvMaxBatch; b++) {
-        const uint16_t *xr = p.x + b * p.C + k * CS;
-        for (int32_t c = threadIdx.x; c < (int32_t)CS; c += blockDim.x) {
-            const float v = b < p.B ? __uint_as_float((uint32_t)xr[c] << 16) : 0.f;
-            xs[b * pitch + c] = __half_as_ushort(__float2half_rn(v));
-        }
-    }
-    __syncthreads();
-    const uint8_t *tb = smem;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const uint32_t lane_off = 4u * (lane % kCopies);
@@ -1465,59 +1510,45 @@ __global__ void __launch_bounds__(kGemvMaxWarps * 32, 1) gemv_kernel(const GemvA
     const int64_t N = CS / 4;          // fp8 per stream
     const int32_t n_tiles = (int32_t)(N / 16);  // CS / 64
     const int64_t groups = p.R / 16;
+    const int64_t w0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+    const int64_t wstep = (int64_t)gridDim.x * (blockDim.x >> 5);
+    // The prologue reads only this weight (not written by the kernel before
+    // this one): the table, and the first row group's chains, slab-ring
+    // fills and sign/mantissa words, all while that kernel may still run.
+    load_table(reinterpret_cast<uint32_t *>(smem), p.table, p.status);
+    GemvGroup gs;
+    if (w0 < groups) gemv_group_start<R>(p, w0, k, lane, lane_off, dst_a, dst_b, n_tiles, gs);
+    pdl_wait();
+    if (p.wait_n > 0) {  // x is gathered by the peers' epilogues: wait for all of them
+        if (threadIdx.x == 0 && !peer_wait(p.wait_flags, *p.wait_seq, p.wait_n) && p.status)
+            atomicOr(p.status, TANS_B200_DATA_TIMEOUT);
+        __syncthreads();
+    }
+    uint16_t *xs = reinterpret_cast<uint16_t *>(smem + kTableBytes);
+    // x slice -> f16 in shared memory (rows >= B are zero)
+    for (int b = 0; b < kGemvMaxBatch; b++) {
+        const uint16_t *xr = p.x + b * p.C + k * CS;
+        for (int32_t c = threadIdx.x; c < (int32_t)CS; c += blockDim.x) {
+            const float v = b < p.B ? __uint_as_float((uint32_t)xr[c] << 16) : 0.f;
+            xs[b * pitch + c] = __half_as_ushort(__float2half_rn(v));
+        }
+    }
+    __syncthreads();
+    const uint8_t *tb = smem;
     const uint32_t *xw = reinterpret_cast<const uint32_t *>(xs) + g * (pitch / 2) + t;
     const int64_t tstep = K * 8;  // sign/mantissa bytes per tile row
     const uint32_t full = 0xffffffffu;
-    for (int64_t w = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp; w < groups;
-         w += (int64_t)gridDim.x * (blockDim.x >> 5)) {
-        const int64_t sa_id = ((w * p.KS + k) * 2 + 0) * 32 + lane;
-        const int64_t sb_id = sa_id + 32;
-        Chain ca, cb;
-        const int32_t ga = chain_init(ca, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
-                                      sa_id, lane_off, p.status);
-        const int32_t gb = chain_init(cb, p.comp, p.comp_bytes, p.offsets, p.states, p.partial,
-                                      sb_id, lane_off, p.status);
-        const bool live = ga > 0 && gb > 0;
-        // row 0 of each chain's 32 stream columns, copied 16 bytes at a time
-        // when every lane is live and it is 16-byte aligned
-        const uintptr_t r0a = reinterpret_cast<uintptr_t>(ca.src) - 4u * lane;
-        const uintptr_t r0b = reinterpret_cast<uintptr_t>(cb.src) - 4u * lane;
-        const int32_t Ga = __reduce_max_sync(full, live ? ga : 0);
-        const int32_t Gb = __reduce_max_sync(full, live ? gb : 0);
-        const bool on = __all_sync(full, live && ((r0a | r0b) & 15u) == 0);
-        if (!live) {
-            chain_idle(ca, p.comp);
-            chain_idle(cb, p.comp);
-        }
-        const uint8_t *src_a = reinterpret_cast<const uint8_t *>(r0a) + 16 * (lane & 7);
-        const uint8_t *src_b = reinterpret_cast<const uint8_t *>(r0b) + 16 * (lane & 7);
-        PairRing ra, rb;
-        ra.fill = Ga - 3;
-        rb.fill = Gb - 3;
-        ra.done0 = ra.done1 = Ga >= 3 ? Ga - 2 : INT_MIN;
-        rb.done0 = rb.done1 = Gb >= 3 ? Gb - 2 : INT_MIN;
-        if (on) {
-            // the first rows: three fills of four per chain, then wait for all
-#pragma unroll
-            for (int i = 0; i < 3; i++) {
-                ra.fill = ring_fill16<128>(ra.fill, -1, true, lane, src_a, dst_a, mask);
-                rb.fill = ring_fill16<128>(rb.fill, -1, true, lane, src_b, dst_b, mask);
-            }
-            cp_async_commit();
-            cp_async_wait<0>();
-            ra.done0 = ra.done1 = ra.fill < 0 ? INT_MIN : ra.fill + 1;
-            rb.done0 = rb.done1 = rb.fill < 0 ? INT_MIN : rb.fill + 1;
-        }
-        __syncwarp();
+    for (int64_t w = w0; w < groups; w += wstep) {
+        if (w != w0) gemv_group_start<R>(p, w, k, lane, lane_off, dst_a, dst_b, n_tiles, gs);
+        Chain &ca = gs.ca, &cb = gs.cb;
+        PairRing &ra = gs.ra, &rb = gs.rb;
+        const bool live = gs.live, on = gs.on;
+        const uint8_t *src_a = gs.src_a, *src_b = gs.src_b;
         float d[4] = {0.f, 0.f, 0.f, 0.f};
-        uint2 sa_n = make_uint2(0, 0), sb_n = make_uint2(0, 0);
+        uint2 sa_n = gs.sa_n, sb_n = gs.sb_n;
         // running pointers: this tile's sign/mantissa words and x fragments
-        const uint8_t *spa = p.sm + sa_id * 8, *spb = p.sm + sb_id * 8;
+        const uint8_t *spa = gs.spa, *spb = gs.spb;
         const uint32_t *xp = xw;
-        if (live && n_tiles > 0) {
-            sa_n = ld_stream_v2(spa);
-            sb_n = ld_stream_v2(spb);
-        }
         for (int32_t tt = 0; tt < n_tiles; tt++) {
             const uint2 sa = sa_n, sb = sb_n;
             spa += tstep;

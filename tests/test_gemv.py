@@ -84,6 +84,39 @@ def test_gemv_down_projection_split(cuda):
 
 
 @pytest.mark.gpu
+def test_gemv_chain_reads_each_input_after_its_producer(cuda):
+    """Six GEMVs back to back on one stream, each reading the previous one's
+    output (an up/down pair of 8-way row-shard shapes, then the full down
+    projection, with and without column slices), no host sync in between.
+    Each GEMV starts its weight-side set-up while its predecessor still runs;
+    its x must still be read only once that predecessor is done.  Output
+    buffers start as NaN, so an early read of x would show up in the result.
+    Each step is checked against the fp32 reference on the GPU's own input."""
+    shapes = [(2176, 5120, None), (5120, 2176, None), (640, 5120, 1), (5120, 640, 2),
+              (17408, 5120, None), (5120, 17408, None)]
+    B = 8
+    encs = []
+    for i, (R, C, KS) in enumerate(shapes):
+        w8, s = make(R, C, 100 + i)
+        encs.append((tans_gemv.encode_weight(w8, s, col_splits=KS).to(cuda), w8.to(cuda), s.to(cuda)))
+    x = torch.randn(B, shapes[0][1], generator=torch.Generator().manual_seed(9))
+    x = x.to(torch.bfloat16).to(cuda)
+    outs = [torch.full((B, R), float("nan"), dtype=torch.bfloat16, device=cuda)
+            for R, _, _ in shapes]
+    torch.cuda.synchronize()
+    h = x
+    for (enc, _, _), out in zip(encs, outs):
+        h = tans_gemv.gemv(enc, h, out=out)
+    torch.cuda.synchronize()
+    h = x
+    for (enc, w8, s), y in zip(encs, outs):
+        ref = tans_gemv.reference_gemv(w8, s, h)
+        assert not torch.isnan(y).any()
+        assert tans_gemv.rel_err(y, ref) <= TOL
+        h = y
+
+
+@pytest.mark.gpu
 @pytest.mark.parametrize("R,C,B,KS", [(16, 64, 1, 1), (48, 128, 3, 2), (256, 1024, 8, 4),
                                       (17408, 5120, 1, None), (5120, 17408, 8, None)])
 def test_gemv_raw_matches_fp32_reference(cuda, R, C, B, KS):
