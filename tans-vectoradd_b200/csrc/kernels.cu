@@ -92,10 +92,12 @@ __device__ __forceinline__ void prefetch_l2(const void *p) {
 
 // Programmatic dependent launch (the GEMV chain: GEMV -> reduce or publish ->
 // next GEMV).  A kernel lets the next one in its stream start as soon as all
-// of its own CTAs are running, so the next kernel's prologue (table load)
+// of its own CTAs are running, so the next kernel's prologue (the GEMV's
+// table load and first row group's set-up, which read only its weight)
 // overlaps its tail; the next kernel waits for this one to complete, with
 // its memory visible, before it reads anything this one writes.  Every
-// global write of these kernels comes after their wait.
+// global write of these kernels, other than an error bit ORed into the
+// status word, comes after their wait.
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
