@@ -249,7 +249,7 @@ int tans_b200_fp8_vecadd_fused_host(
  * reduced through `partials` (caller-owned f32 [col_splits][batch][rows]),
  * deterministically.  Launched with programmatic dependent launch: the
  * weight-side set-up may overlap the previous kernel on the stream, x and
- * the outputs are touched only after it completes (see INTEGRATION.md). */
+ * the outputs are touched only after it completes. */
 int tans_b200_gemv(const uint8_t *compressed, int64_t compressed_bytes,
                    const int32_t *offsets, const uint16_t *states,
                    const uint8_t *partial, const uint8_t *sign_mantissa,
