@@ -33,6 +33,19 @@ def test_stream_matrix_layout():
             assert sm[sid, pos].item() == r * C + c
 
 
+@pytest.mark.parametrize("R,C,KS", [(17408, 5120, 5), (5120, 17408, 17), (8704, 5120, 5),
+                                    (2560, 17408, 17), (4352, 5120, 10), (1280, 17408, 34),
+                                    (2176, 5120, 20), (640, 17408, 68)])
+def test_default_col_splits_for_stack_shards(R, C, KS):
+    """Column slices chosen for the cfg3 matrices and their 2-, 4- and 8-way
+    row shards: slices of >= 1024 columns while that gives enough warps,
+    else 512 and then 256 (the short-slice build covers <= 512); every
+    choice divides the columns into whole 64-column chunks."""
+    ks = tans_gemv.default_col_splits(R, C)
+    assert ks == KS
+    assert C % (64 * ks) == 0
+
+
 def test_quantize_rows_maps_row_max_to_448():
     w8, s = make(16, 64, 0)
     v = w8.view(torch.float8_e4m3fn).float()
